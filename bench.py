@@ -1,0 +1,464 @@
+"""Benchmark of the stateful hybrid attention hot path on B200.
+
+Workload (N=1): benchmark configuration 3, the batched ragged hybrid decode
+step -- 256 sequences with KV lengths uniform in [512, 32768] (seeded), 64-token
+paged bf16 KV, fp32 DeltaNet states and bf16 conv states ~ N(0, 0.1), KV ~ N(0, 1),
+random-init weights of the 40-layer 3:1 stack (30 Gated DeltaNet + 10 GQA).
+One step = every layer's attention (input norm, projections, fused kernel,
+output projection, residual) for all 256 sequences: one decoded token per
+sequence.  Metric: decode tokens/s (whole job) with the fraction of the HBM
+roofline of the dominant kernel.
+
+Multi-GPU (torchrun): each rank decodes its own 256 sequences (weak scaling, no
+collective on the path); the elapsed time is the max over ranks.
+
+``--impl reference`` times router-ia's algorithm on the host cores (the CPU
+oracle port of qwen36_attention_cache's layer steps, one sequence at a time as
+the reference runs) on a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from datetime import timedelta
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+for _p in (str(REPO / "router-ia_b200"), str(REPO)):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+
+METRIC = "attn decode tokens/s/GPU + %HBM peak; DeltaNet chunked prefill tokens/s"
+UNIT = "tokens/s"
+B_DN = 4_292_736  # algorithmic bytes of K1 per (sequence, layer)
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--batch", type=int, default=256)
+    ap.add_argument("--len-lo", type=int, default=512)
+    ap.add_argument("--len-hi", type=int, default=32768)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true")
+    ap.add_argument("--cpu-sample", type=int, default=4, help="sequences in the CPU baseline sample")
+    return ap.parse_args()
+
+
+def peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.is_file():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]), "source": "measured"}
+    return dict(PEAKS_FALLBACK, source="fallback")
+
+
+# --------------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: torch.device):
+        self.proc = None
+        self.path = None
+        try:
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            self.gpu = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+        except Exception:
+            self.gpu = str(device.index or 0)
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", self.gpu, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-f", self.path], stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return float("nan")
+        sm = [num(r[1]) for r in rows]
+        power = [num(r[3]) for r in rows]
+        pmax = max(p for p in power if not math.isnan(p)) if any(not math.isnan(p) for p in power) else 0
+        loaded = [s for s, p in zip(sm, power) if p >= 0.5 * pmax] or sm
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[j] for r in rows for j in range(4) if r[5 + j].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(num(r[2]) for r in rows),
+                "reasons": reasons, "samples": len(rows), "power_w_max": pmax}
+
+
+# --------------------------------------------------------------------------- launch instrumentation
+class EventHook:
+    """CUDA events around each kernel-launching library call (on the current
+    stream, which is the launch stream) plus a launch counter."""
+
+    def __init__(self, timed=("gqa_decode", "gdn_decode")):
+        self.timed = set(timed)
+        self.events: dict[str, list] = {n: [] for n in timed}
+        self.launches = 0
+        self._open = None
+
+    def before(self, name):
+        if name in self.timed:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            self._open = e
+
+    def after(self, name, kernels):
+        self.launches += kernels
+        if name in self.timed:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            self.events[name].append((self._open, e))
+
+    def mean_ms(self, name):
+        pairs = self.events[name]
+        return sum(a.elapsed_time(b) for a, b in pairs) / max(1, len(pairs)), len(pairs)
+
+
+# --------------------------------------------------------------------------- workload
+def build_engine(args, device, rank, headroom):
+    from ria_b200 import constants as C, synthetic
+    from ria_b200.engine import BatchedAttentionState
+    from ria_b200.weights import DeltaNetWeights, GqaWeights
+
+    lengths = synthetic.ragged_lengths(args.batch, args.len_lo, args.len_hi, seed=rank)
+    layers = {}
+    for layer in range(C.NUM_LAYERS):
+        t = synthetic.layer_weights_on_device(layer, device, seed=0)
+        cls = GqaWeights if C.is_full_attention_layer(layer) else DeltaNetWeights
+        layers[layer] = cls.from_tensors(t, device)
+        del t
+    blocks = [math.ceil((n + headroom) / C.KV_BLOCK) for n in lengths]
+    eng = BatchedAttentionState(layers, batch=args.batch, pool_blocks=sum(blocks) + 8,
+                                max_blocks_per_seq=max(blocks) + 1, device=device)
+    g = torch.Generator(device=device)
+    g.manual_seed(1234 + rank)
+    for layer in eng.rec:
+        eng.rec[layer].normal_(0.0, 0.1, generator=g)
+        eng.conv[layer].normal_(0.0, 0.1, generator=g)
+    for layer in eng.k_pool:
+        eng.k_pool[layer].normal_(0.0, 1.0, generator=g)
+        eng.v_pool[layer].normal_(0.0, 1.0, generator=g)
+    for i, n in enumerate(lengths):
+        eng.set_length(i, n)
+    eng.sync_tables()
+    torch.cuda.synchronize(device)
+    return eng, lengths
+
+
+def gqa_bytes(lengths):
+    """Algorithmic bytes of one K3 launch: KV read 2048 B/token, the appended
+    token 2048 B, q+gate in and output (3 x 16 x 256 x 2 B) per sequence."""
+    return sum(2048 * n + 2048 + 24576 for n in lengths)
+
+
+def run_ours(args, rank, world, device):
+    from ria_b200 import _ext
+
+    headroom = args.warmup + 2 * args.steps + 4
+    t_setup = time.perf_counter()
+    eng, lengths = build_engine(args, device, rank, headroom)
+    setup_s = time.perf_counter() - t_setup
+    x = torch.randn(args.batch, 2048, device=device).to(torch.bfloat16).float()
+
+    for _ in range(args.warmup):
+        eng.step(x)
+    torch.cuda.synchronize(device)
+    _ext.device_error()
+    barrier(world, device)
+
+    hook = EventHook()
+    _ext.launch_hook = hook
+    lens_timed = []
+    clocks = ClockSampler(device)
+    clocks.start()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(device)
+    start.record()
+    for _ in range(args.steps):
+        lens_timed.append(list(eng.lengths))
+        eng.step(x)
+    end.record()
+    torch.cuda.synchronize(device)
+    _ext.launch_hook = None
+    clock_info = clocks.stop()
+    elapsed_ms = start.elapsed_time(end)
+    elapsed_ms = reduce_max(elapsed_ms, world, device)
+    barrier(world, device)
+
+    # e2e: host inputs in pinned memory, copies inside the timed region
+    x_h = torch.empty(args.batch, 2048, dtype=torch.float32, pin_memory=True)
+    x_h.copy_(x.cpu())
+    y_h = torch.empty_like(x_h, pin_memory=True)
+    x_d = torch.empty_like(x)
+    torch.cuda.synchronize(device)
+    barrier(world, device)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        x_d.copy_(x_h, non_blocking=True)
+        y = eng.step(x_d)
+        y_h.copy_(y, non_blocking=True)
+        torch.cuda.current_stream(device).synchronize()
+    t1.record()
+    torch.cuda.synchronize(device)
+    e2e_ms = reduce_max(t0.elapsed_time(t1), world, device)
+    dev_err = _ext.device_error()
+
+    p = peaks()
+    gqa_ms, gqa_n = hook.mean_ms("gqa_decode")
+    gdn_ms, gdn_n = hook.mean_ms("gdn_decode")
+    gqa_b = statistics.mean(gqa_bytes(ls) for ls in lens_timed)
+    gdn_b = args.batch * B_DN
+    kernels = {
+        "gqa_decode": {"ms_per_launch": gqa_ms, "launches": gqa_n, "bytes_per_launch": gqa_b,
+                       "achieved_gbs": gqa_b / (gqa_ms * 1e6), "frac": gqa_b / (gqa_ms * 1e6) / p["hbm_gbs"]},
+        "gdn_decode": {"ms_per_launch": gdn_ms, "launches": gdn_n, "bytes_per_launch": gdn_b,
+                       "achieved_gbs": gdn_b / (gdn_ms * 1e6), "frac": gdn_b / (gdn_ms * 1e6) / p["hbm_gbs"]},
+    }
+    dom = max(kernels, key=lambda k: kernels[k]["ms_per_launch"] * kernels[k]["launches"])
+    step_bytes = 10 * gqa_b + 30 * gdn_b
+    tokens = world * args.batch * args.steps
+    line = {
+        "metric": METRIC,
+        "value": tokens / (elapsed_ms / 1e3),
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": elapsed_ms / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16 I/O, fp32 state/accumulate",
+        "data": "synthetic (seeded random-init weights, N(0,0.1) states, N(0,1) KV)",
+        "config": {
+            "workload": "config3: batched ragged hybrid decode step, 30 DeltaNet + 10 GQA layers",
+            "sequences_per_gpu": args.batch,
+            "kv_len_range": [args.len_lo, args.len_hi],
+            "kv_tokens_per_gpu": sum(lengths),
+            "kv_block_tokens": 64,
+            "parallelism": f"sequence-sharded x{world} (no collective)",
+            "l2": "inputs larger than L2 (state+KV ~%.0f GB per step)" % (step_bytes / 1e9),
+        },
+        "roofline": {
+            "kernel": dom, "bound": "hbm", "achieved": kernels[dom]["achieved_gbs"], "peak": p["hbm_gbs"],
+            "unit": "GB/s", "frac": kernels[dom]["frac"], "peak_source": p["source"],
+            "traffic": None,
+        },
+        "kernels": kernels,
+        "step_hbm_fraction": step_bytes / ((elapsed_ms / args.steps) * 1e6) / p["hbm_gbs"],
+        "e2e": {"value": tokens / (e2e_ms / 1e3), "unit": UNIT,
+                "h2d_bytes_per_step": args.batch * 2048 * 4, "d2h_bytes_per_step": args.batch * 2048 * 4},
+        "gpu_launches": hook.launches,
+        "clocks": clock_info,
+        "setup_s": round(setup_s, 1),
+        "device_error": dev_err,
+    }
+    del eng
+    torch.cuda.empty_cache()
+    return line
+
+
+def barrier(world, device):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier(device_ids=[device.index])
+
+
+def reduce_max(v, world, device):
+    if world == 1:
+        return v
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# --------------------------------------------------------------------------- extras (rank 0)
+def config1_latency(device, iters=50):
+    """Benchmark configuration 1: one GQA layer decode step, batch 1, 4096
+    cached tokens (bf16 KV N(0,1)); returns step and kernel times."""
+    from ria_b200 import _ext, synthetic
+    from ria_b200.engine import gqa_decode, plan_gqa_split
+    from ria_b200.weights import GqaWeights, rope_inv_freq
+
+    w = GqaWeights.from_tensors(synthetic.layer_weights_on_device(3, device), device)
+    L = 4096
+    k = torch.randn(2, 8192, 256, device=device).to(torch.bfloat16)
+    v = torch.randn(2, 8192, 256, device=device).to(torch.bfloat16)
+    table = torch.arange(128, dtype=torch.int32, device=device).reshape(1, -1)
+    inv = rope_inv_freq(device)
+    launch = plan_gqa_split([L + 1], device)
+    x = torch.randn(1, 2048, device=device)
+    for _ in range(10):
+        gqa_decode(x, w, k, v, table, inv, launch, seq_len0=L, position0=L)
+    hook = EventHook(timed=("gqa_decode",))
+    _ext.launch_hook = hook
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(device)
+    s.record()
+    for _ in range(iters):
+        gqa_decode(x, w, k, v, table, inv, launch, seq_len0=L, position0=L)
+    e.record()
+    torch.cuda.synchronize(device)
+    _ext.launch_hook = None
+    kms, _ = hook.mean_ms("gqa_decode")
+    step_ms = s.elapsed_time(e) / iters
+    kbytes = gqa_bytes([L])
+    return {"layer_step_us": step_ms * 1e3, "gqa_kernel_us": kms * 1e3, "kernel_bytes": kbytes,
+            "kernel_gbs": kbytes / (kms * 1e6), "split_pages": launch.split_pages, "splits": launch.max_splits}
+
+
+# --------------------------------------------------------------------------- CPU reference (oracle port)
+def cpu_reference(args, steps, warmup, sample):
+    """router-ia's layer algorithm on the host cores, one sequence at a time
+    (as the reference runs): per-token time = 30 x DeltaNet layer + 10 x GQA
+    layer at the sequence's KV length, timed on ``sample`` sequences at
+    stratified lengths of the workload and extrapolated to the stack."""
+    from oracle import attention_oracle as O
+    from ria_b200 import synthetic
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    lengths = sorted(synthetic.ragged_lengths(args.batch, args.len_lo, args.len_hi, seed=0))
+    picks = [lengths[int((i + 0.5) * len(lengths) / sample)] for i in range(sample)]
+    dn_w = {k: v for k, v in synthetic.layer_weights(0, 0).items()}
+    gqa_w = {k: v for k, v in synthetic.layer_weights(3, 0).items()}
+    # the reference keeps fp32 projections on the CPU path; convert once
+    for w in (dn_w, gqa_w):
+        for k in list(w):
+            if w[k].dim() == 2:
+                w[k] = w[k].float()
+    g = torch.Generator().manual_seed(0)
+    caches = []
+    for n in picks:
+        kc = torch.randn(1, 2, n, 256, generator=g).to(torch.bfloat16).float()
+        vc = torch.randn(1, 2, n, 256, generator=g).to(torch.bfloat16).float()
+        conv = (torch.randn(1, 8192, 4, generator=g) * 0.1).to(torch.bfloat16)
+        rec = torch.randn(1, 32, 128, 128, generator=g) * 0.1
+        caches.append((kc, vc, conv, rec))
+    x = torch.randn(1, 2048, generator=g).to(torch.bfloat16).float()
+    per_token = []
+    for it in range(warmup + steps):
+        t_tok = 0.0
+        for (kc, vc, conv, rec), n in zip(caches, picks):
+            t0 = time.perf_counter()
+            O.deltanet_step(dn_w, x, conv, rec)
+            t1 = time.perf_counter()
+            O.gqa_step(gqa_w, x, kc, vc, n)
+            t2 = time.perf_counter()
+            t_tok += 30 * (t1 - t0) + 10 * (t2 - t1)
+        if it >= warmup:
+            per_token.append(t_tok / len(picks))
+    sec_per_token = statistics.mean(per_token)
+    return {
+        "value": 1.0 / sec_per_token,
+        "unit": UNIT,
+        "cores": torch.get_num_threads(),
+        "kind": "port",
+        "sample": (f"{sample} sequences at KV lengths {picks} (strata of the workload), one DeltaNet and one GQA "
+                   f"layer step each per timed step, extrapolated to 30+10 layers; {steps} timed steps"),
+        "cpu": _cpu_model(),
+    }
+
+
+def _cpu_model():
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def main():
+    args = parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        ref = cpu_reference(args, steps=args.steps, warmup=args.warmup, sample=args.cpu_sample)
+        line = {
+            "metric": METRIC, "impl": "reference", "value": ref["value"], "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 / ref["value"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (reference CPU path)",
+            "data": "synthetic", "config": {"workload": "config3: batched ragged hybrid decode step (CPU sample)",
+                                            "sequences_per_gpu": args.batch,
+                                            "kv_len_range": [args.len_lo, args.len_hi]},
+            "cpu_baseline": ref, "e2e": {"value": ref["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
+                                         "d2h_bytes_per_step": 0},
+        }
+        print(json.dumps(line), flush=True)
+        return
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+    try:
+        line = run_ours(args, rank, world, device)
+        if rank == 0 and not args.no_extras:
+            line["config1_gqa_b1_l4096"] = config1_latency(device)
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_reference(args, steps=2, warmup=1, sample=args.cpu_sample)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier(device_ids=[device.index])
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

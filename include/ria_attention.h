@@ -1,0 +1,163 @@
+/*
+ * router-ia B200 attention library: C ABI.
+ *
+ * Drop-in device kernels for router-ia's stateful hybrid attention path
+ * (v2/src/router_ia/qwen36_attention_cache.py).  Every entry point:
+ *   - takes raw device pointers, element strides and sizes (no framework types);
+ *   - only enqueues work on `stream` (no host synchronisation, no allocation);
+ *   - returns RIA_OK (0) or a nonzero status, with a message available from
+ *     ria_last_error_string() (per host thread).
+ * The Python host side maps a nonzero status to RuntimeError/ValueError, the
+ * exception types the reference raises for the same conditions.
+ *
+ * Shapes are fixed by the Qwen3.6-35B-A3B attention layers:
+ *   Gated DeltaNet: 16 key heads, 32 value heads, head dim 128,
+ *                   conv channels 8192 (q 2048 | k 2048 | v 4096), conv kernel 4.
+ *   GQA:            16 query heads, 2 KV heads, head dim 256, RoPE on dims [0,64).
+ */
+#ifndef RIA_ATTENTION_H_
+#define RIA_ATTENTION_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define RIA_API __attribute__((visibility("default")))
+#else
+#define RIA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RIA_ABI_VERSION 1
+
+#define RIA_OK 0
+#define RIA_ERR_INVALID 1     /* bad argument: shape, stride, alignment, range */
+#define RIA_ERR_CUDA 2        /* a CUDA runtime call or launch failed */
+#define RIA_ERR_UNSUPPORTED 3 /* device or configuration not supported */
+
+/* Opaque CUDA stream (cudaStream_t); NULL is the legacy default stream. */
+typedef void* ria_stream_t;
+
+/* Message describing the last failure on the calling host thread. */
+RIA_API const char* ria_last_error_string(void);
+RIA_API int ria_abi_version(void);
+
+/* Reads (and optionally clears) the device error word that kernels set when a
+ * bounded wait gives up or a block-table entry is out of range.  Synchronous.
+ * *code_out = 0 means no device-side error was recorded. */
+RIA_API int ria_device_error(int clear, unsigned int* code_out);
+
+/* ------------------------------------------------------------------------
+ * K1: Gated DeltaNet decode step, batched over sequences.
+ *
+ * Replaces, per layer and per sequence, the body of
+ *   _causal_conv1d_step      qwen36_attention_cache.py:176-221
+ *   _linear_stateful         qwen36_attention_cache.py:232-271 (after the input
+ *                            projections, before out_proj)
+ *   gated_rmsnorm            qwen36_gated_norm_probe.py:19-36
+ * in one pass over each head's fp32 128x128 state.
+ *
+ * Inputs are the projection outputs of the layer for B sequences, bf16:
+ *   mixed [B, 8192] (row stride mixed_stride): in_proj_qkv output
+ *   z     [B, 4096] (z_stride):  in_proj_z output
+ *   b     [B, 32]   (b_stride):  in_proj_b output  (beta = sigmoid(b))
+ *   a     [B, 32]   (a_stride):  in_proj_a output
+ * Parameters: conv_weight [8192, 4] bf16 (the checkpoint's [8192,1,4]),
+ *   a_log [32] f32, dt_bias [32] f32, norm_weight [128] f32.
+ * State (updated in place): conv_state [slots, 8192, 4] bf16 (the last four
+ *   conv inputs, current token last), rec_state [slots, 32, 128, 128] f32
+ *   indexed [head][k][v] (16-byte aligned).  Sequence i uses slot
+ *   slots[i] (slots == NULL: slot i).
+ * Output: out [B, 4096] bf16 (row stride out_stride): the gated RMSNorm output
+ *   that feeds out_proj.
+ */
+RIA_API int ria_gdn_decode_step(const void* mixed, int64_t mixed_stride, const void* z, int64_t z_stride, const void* b,
+                        int64_t b_stride, const void* a, int64_t a_stride, const void* conv_weight,
+                        const float* a_log, const float* dt_bias, const float* norm_weight, void* conv_state,
+                        float* rec_state, const int32_t* slots, int32_t num_slots, void* out, int64_t out_stride,
+                        int32_t batch, ria_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * K3: paged, ragged, split-KV GQA decode step with KV append.
+ *
+ * Replaces, per layer and per sequence, _full_stateful after the q/k/v
+ * projections and before o_proj (qwen36_attention_cache.py:298-318):
+ * per-head q/k RMSNorm (the (1+w) form, qwen36_op_probe.py:55-67), partial RoPE
+ * on dims [0,64) (_apply_rope, :137-162), the KV append (_append_full_kv,
+ * :334-373), softmax(q K^T / 16) V over the 8 query heads of each KV head and
+ * the sigmoid output gate.
+ *
+ * q     [B, 16*512] bf16 (q_stride): q_proj output; head h holds q in
+ *        [512h, 512h+256) and the gate in [512h+256, 512h+512).
+ * k, v  [B, 2*256] bf16 (k_stride, v_stride): k_proj / v_proj outputs.
+ * q_norm_weight, k_norm_weight [256] f32; inv_freq [32] f32 RoPE inverse
+ *        frequencies (theta 1e7 over 64 rotary dims).
+ * k_pool, v_pool [2, pool_tokens, 256] bf16: paged cache, 64-token blocks;
+ *        logical block j of sequence i is physical block
+ *        block_table[i*block_table_stride + j].  16-byte aligned.
+ * seq_lens [B]: cached tokens before this step; the new token is written at
+ *        index seq_lens[i].  positions [B]: absolute RoPE positions.  For a
+ *        single sequence (batch 1) either may be NULL, and the host values
+ *        seq_len0 / position0 are used instead (the reference's per-layer
+ *        length and tokens_seen).
+ * out   [B, 4096] bf16 (out_stride): gated attention output feeding o_proj.
+ * workspace: scratch of at least ria_gqa_decode_workspace_bytes(B, max_splits)
+ *        bytes (split partials), 16-byte aligned.
+ * split_pages: KV blocks per split (>= 1); max_splits >= ceil(blocks / split_pages)
+ *        for the longest sequence after the append.
+ */
+RIA_API int64_t ria_gqa_decode_workspace_bytes(int32_t batch, int32_t max_splits);
+RIA_API int ria_gqa_decode_paged(const void* q, int64_t q_stride, const void* k, int64_t k_stride, const void* v,
+                         int64_t v_stride, const float* q_norm_weight, const float* k_norm_weight,
+                         const float* inv_freq, void* k_pool, void* v_pool, int64_t pool_tokens,
+                         const int32_t* block_table, int32_t block_table_stride, const int32_t* seq_lens,
+                         const int32_t* positions, int32_t seq_len0, int32_t position0, void* out,
+                         int64_t out_stride, void* workspace,
+                         int64_t workspace_bytes, int32_t batch, int32_t split_pages, int32_t max_splits,
+                         ria_stream_t stream);
+
+/* Split size heuristic used by the Python host: KV blocks per split so that the
+ * grid holds a few waves of CTAs for `total_blocks` blocks of work. */
+RIA_API int32_t ria_gqa_decode_split_pages(int64_t total_blocks, int32_t num_kv_heads);
+
+/* ------------------------------------------------------------------------
+ * Small fused row kernels used around the projections.
+ */
+
+/* out[B, n] (bf16) = rmsnorm(x[B, n] f32) * (1 + weight[n]); eps 1e-6.
+ * Replaces rmsnorm (qwen36_op_probe.py:55-67) on the layer input. */
+RIA_API int ria_rmsnorm_rows(const float* x, int64_t x_stride, const float* weight, void* out, int64_t out_stride, int32_t rows,
+                     int32_t n, ria_stream_t stream);
+
+/* out[B, n] f32 = x0[B, n] f32 + proj[B, n] bf16: the residual add that ends
+ * _linear_stateful / _full_stateful (qwen36_attention_cache.py:276-277, 320-321). */
+RIA_API int ria_residual_add(const float* x0, int64_t x0_stride, const void* proj, int64_t proj_stride, float* out,
+                     int64_t out_stride, int32_t rows, int32_t n, ria_stream_t stream);
+
+/* One-token causal depthwise conv (kernel 4) + SiLU for B rows of `channels`
+ * channels, in bf16 like the reference's conv weight dtype:
+ * _causal_conv1d_step (qwen36_attention_cache.py:176-221).
+ * x [B, channels] bf16, conv_state [B, channels, 4] bf16 updated in place,
+ * weight [channels, 4] bf16, out [B, channels] bf16. */
+RIA_API int ria_conv1d_step(const void* x, int64_t x_stride, void* conv_state, const void* weight, void* out,
+                    int64_t out_stride, int32_t rows, int32_t channels, ria_stream_t stream);
+
+/* lens[i] += 1 and positions[i] += 1 for i < batch: advances a batch of
+ * sequences by one decoded token after all layers ran (the caller-side
+ * `tokens_seen += 1`, qwen36_chat_batch.py:204-206), on the device so that a
+ * captured decode step needs no host data. */
+RIA_API int ria_advance_positions(int32_t* seq_lens, int32_t* positions, int32_t batch, ria_stream_t stream);
+
+/* Partial NeoX RoPE in place on rows of f32 vectors: x[rows, head_dim] with the
+ * first rope_dim dims rotated (rotate-half inside that slice) at `position`.
+ * _apply_rope (qwen36_attention_cache.py:154-162). */
+RIA_API int ria_rope_apply(float* x, int32_t rows, int32_t head_dim, int32_t rope_dim, const float* inv_freq,
+                   int64_t position, ria_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RIA_ATTENTION_H_ */

@@ -1,0 +1,208 @@
+"""ctypes binding of ``libria_attention.so`` (the C ABI in include/ria_attention.h).
+
+This is the only door to the device kernels.  There is no CPU fallback: when
+the library is missing or a CUDA device is absent, calls raise.  Each wrapper
+takes torch tensors only as carriers of device pointers, strides and the
+current stream, and maps a nonzero status to ``RuntimeError`` (``ValueError``
+for argument errors), the exception types router-ia raises for the same
+conditions.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from ctypes import c_char_p, c_int, c_int32, c_int64, c_uint, c_void_p, POINTER
+from pathlib import Path
+
+import torch
+
+from .build import INCLUDE, LIB_PATH
+
+RIA_OK = 0
+RIA_ERR_INVALID = 1
+
+_lib: ctypes.CDLL | None = None
+
+# Optional instrumentation: an object with ``before(name)`` / ``after(name,
+# kernels)`` called around each kernel-launching entry point (the benchmark
+# records CUDA events and counts launches through it).
+launch_hook = None
+
+
+class _Hooked:
+    def __init__(self, name: str, kernels: int = 1):
+        self.name, self.kernels = name, kernels
+
+    def __enter__(self):
+        if launch_hook is not None:
+            launch_hook.before(self.name)
+
+    def __exit__(self, *exc):
+        if launch_hook is not None and exc[0] is None:
+            launch_hook.after(self.name, self.kernels)
+        return False
+
+_SIGNATURES: dict[str, tuple[object, list]] = {
+    "ria_last_error_string": (c_char_p, []),
+    "ria_abi_version": (c_int, []),
+    "ria_device_error": (c_int, [c_int, POINTER(c_uint)]),
+    "ria_gdn_decode_step": (
+        c_int,
+        [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_void_p,
+         c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_void_p, c_int64, c_int32, c_void_p],
+    ),
+    "ria_gqa_decode_workspace_bytes": (c_int64, [c_int32, c_int32]),
+    "ria_gqa_decode_split_pages": (c_int32, [c_int64, c_int32]),
+    "ria_gqa_decode_paged": (
+        c_int,
+        [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+         c_int64, c_void_p, c_int32, c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_int64, c_void_p, c_int64,
+         c_int32, c_int32, c_int32, c_void_p],
+    ),
+    "ria_advance_positions": (c_int, [c_void_p, c_void_p, c_int32, c_void_p]),
+    "ria_rmsnorm_rows": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int32, c_int32, c_void_p]),
+    "ria_residual_add": (
+        c_int, [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_int32, c_int32, c_void_p]),
+    "ria_conv1d_step": (
+        c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int64, c_int32, c_int32, c_void_p]),
+    "ria_rope_apply": (c_int, [c_void_p, c_int32, c_int32, c_int32, c_void_p, c_int64, c_void_p]),
+}
+
+
+def header_symbols() -> list[str]:
+    """Entry points declared in include/ria_attention.h."""
+    text = (INCLUDE / "ria_attention.h").read_text()
+    return re.findall(r"^RIA_API\s+[\w\s\*]+?\b(ria_\w+)\s*\(", text, flags=re.M)
+
+
+def lib() -> ctypes.CDLL:
+    """Load the library once; raise if it has not been built."""
+    global _lib
+    if _lib is None:
+        path = Path(LIB_PATH)
+        if not path.exists():
+            raise RuntimeError(
+                f"router-ia B200 CUDA library not found at {path}; build it with "
+                "`python router-ia_b200/ria_b200/build.py` (there is no CPU fallback)"
+            )
+        handle = ctypes.CDLL(str(path))
+        for name, (restype, argtypes) in _SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.restype = restype
+            fn.argtypes = argtypes
+        _lib = handle
+    return _lib
+
+
+def last_error() -> str:
+    msg = lib().ria_last_error_string()
+    return msg.decode("utf-8", "replace") if msg else ""
+
+
+def _check(rc: int, what: str) -> None:
+    if rc == RIA_OK:
+        return
+    msg = f"{what}: {last_error()}"
+    if rc == RIA_ERR_INVALID:
+        raise ValueError(msg)
+    raise RuntimeError(msg)
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _require_cuda(*tensors: torch.Tensor) -> None:
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("router-ia B200 kernels need CUDA tensors (no CPU fallback)")
+
+
+def device_error(clear: bool = True) -> int:
+    """Device error word set by kernels (0 = none); synchronises the device."""
+    code = c_uint(0)
+    _check(lib().ria_device_error(1 if clear else 0, ctypes.byref(code)), "ria_device_error")
+    return int(code.value)
+
+
+def gdn_decode_step(mixed, z, b, a, conv_weight, a_log, dt_bias, norm_weight, conv_state, rec_state, slots, out):
+    """K1 over ``mixed.shape[0]`` sequences (see ria_gdn_decode_step)."""
+    _require_cuda(mixed, z, b, a, conv_weight, conv_state, rec_state, out)
+    batch = mixed.shape[0]
+    num_slots = rec_state.shape[0]
+    if conv_state.shape[0] != num_slots:
+        raise ValueError("conv_state and rec_state must have the same number of slots")
+    with _Hooked("gdn_decode"):
+        rc = lib().ria_gdn_decode_step(
+            mixed.data_ptr(), mixed.stride(0), z.data_ptr(), z.stride(0), b.data_ptr(), b.stride(0), a.data_ptr(),
+            a.stride(0), conv_weight.data_ptr(), a_log.data_ptr(), dt_bias.data_ptr(), norm_weight.data_ptr(),
+            conv_state.data_ptr(), rec_state.data_ptr(), _ptr(slots), num_slots, out.data_ptr(), out.stride(0), batch,
+            _stream(mixed))
+    _check(rc, "ria_gdn_decode_step")
+
+
+def gqa_workspace_bytes(batch: int, max_splits: int) -> int:
+    return int(lib().ria_gqa_decode_workspace_bytes(batch, max_splits))
+
+
+def gqa_split_pages(total_blocks: int, num_kv_heads: int = 2) -> int:
+    return int(lib().ria_gqa_decode_split_pages(total_blocks, num_kv_heads))
+
+
+def gqa_decode_paged(q, k, v, q_norm_w, k_norm_w, inv_freq, k_pool, v_pool, block_table, seq_lens, positions,
+                     out, workspace, split_pages, max_splits, seq_len0=0, position0=0):
+    """K3 over ``q.shape[0]`` sequences (see ria_gqa_decode_paged)."""
+    _require_cuda(q, k, v, k_pool, v_pool, block_table, out)
+    batch = q.shape[0]
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    with _Hooked("gqa_decode", 2 if int(max_splits) > 1 else 1):
+        rc = lib().ria_gqa_decode_paged(
+            q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0), q_norm_w.data_ptr(),
+            k_norm_w.data_ptr(), inv_freq.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(), k_pool.shape[1],
+            block_table.data_ptr(), block_table.stride(0), _ptr(seq_lens), _ptr(positions), int(seq_len0),
+            int(position0), out.data_ptr(), out.stride(0), _ptr(workspace), ws_bytes, batch, int(split_pages),
+            int(max_splits), _stream(q))
+    _check(rc, "ria_gqa_decode_paged")
+
+
+def advance_positions(seq_lens, positions):
+    with _Hooked("advance"):
+        rc = lib().ria_advance_positions(seq_lens.data_ptr(), positions.data_ptr(), seq_lens.shape[0], _stream(seq_lens))
+    _check(rc, "ria_advance_positions")
+
+
+def rmsnorm_rows(x, weight, out):
+    _require_cuda(x, weight, out)
+    with _Hooked("rmsnorm"):
+        rc = lib().ria_rmsnorm_rows(x.data_ptr(), x.stride(0), weight.data_ptr(), out.data_ptr(), out.stride(0),
+                                    x.shape[0], x.shape[1], _stream(x))
+    _check(rc, "ria_rmsnorm_rows")
+
+
+def residual_add(x0, proj, out):
+    _require_cuda(x0, proj, out)
+    with _Hooked("residual_add"):
+        rc = lib().ria_residual_add(x0.data_ptr(), x0.stride(0), proj.data_ptr(), proj.stride(0), out.data_ptr(),
+                                    out.stride(0), x0.shape[0], x0.shape[1], _stream(x0))
+        _check(rc, "ria_residual_add")
+    
+    
+    def conv1d_step(x, conv_state, weight, out):
+        _require_cuda(x, conv_state, weight, out)
+        with _Hooked("conv1d_step"):
+            rc = lib().ria_conv1d_step(x.data_ptr(), x.stride(0), conv_state.data_ptr(), weight.data_ptr(), out.data_ptr(),
+                                   out.stride(0), x.shape[0], x.shape[1], _stream(x))
+    _check(rc, "ria_conv1d_step")
+
+
+def rope_apply(x, inv_freq, rope_dim: int, position: int):
+    _require_cuda(x, inv_freq)
+    rows, head_dim = x.shape
+    with _Hooked("rope_apply"):
+        rc = lib().ria_rope_apply(x.data_ptr(), rows, head_dim, rope_dim, inv_freq.data_ptr(), int(position), _stream(x))
+    _check(rc, "ria_rope_apply")

@@ -1,0 +1,226 @@
+"""Batched decode of the hybrid attention stack on one GPU.
+
+One decode step of one layer for B sequences is:
+
+    DeltaNet: h = rmsnorm(x) -> proj = h W_in^T (cuBLAS) -> K1 (conv, gates,
+              norms, delta rule, gated norm) -> o = g W_out^T (cuBLAS) -> x + o
+    GQA:      h = rmsnorm(x) -> proj = h W_in^T -> K3 (q/k norm, RoPE, KV append,
+              split-KV attention, gate) -> o = a W_out^T -> x + o
+
+which is router-ia's ``_linear_stateful`` / ``_full_stateful``
+(qwen36_attention_cache.py:224-324) with the per-sequence Python loop replaced
+by a batch dimension.  All state stays in HBM:
+
+* DeltaNet: ``rec[layer]`` [slots, 32, 128, 128] fp32 and ``conv[layer]``
+  [slots, 8192, 4] bf16, one slot per sequence;
+* GQA: one paged bf16 pool per layer, K and V each [2, pool_tokens, 256], with
+  64-token blocks; all GQA layers share one block table because every layer
+  appends the same token positions.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import torch
+import torch.nn.functional as F
+
+from . import _ext
+from . import constants as C
+from .weights import DeltaNetWeights, GqaWeights, rope_inv_freq
+
+
+def _cdiv(a: int, b: int) -> int:
+    return (a + b - 1) // b
+
+
+def deltanet_decode(x: torch.Tensor, w: DeltaNetWeights, rec: torch.Tensor, conv: torch.Tensor,
+                    slots: torch.Tensor | None = None) -> torch.Tensor:
+    """One DeltaNet layer step for ``x`` [B, 2048] fp32; returns the residual."""
+    batch = x.shape[0]
+    h = torch.empty(batch, C.HIDDEN, dtype=torch.bfloat16, device=x.device)
+    _ext.rmsnorm_rows(x, w.in_norm, h)
+    proj = F.linear(h, w.w_in)
+    gated = torch.empty(batch, C.LINEAR_VALUE_DIM, dtype=torch.bfloat16, device=x.device)
+    _ext.gdn_decode_step(
+        proj[:, C.DN_PROJ_QKV[0]:C.DN_PROJ_QKV[1]], proj[:, C.DN_PROJ_Z[0]:C.DN_PROJ_Z[1]],
+        proj[:, C.DN_PROJ_B[0]:C.DN_PROJ_B[1]], proj[:, C.DN_PROJ_A[0]:C.DN_PROJ_A[1]],
+        w.conv_w, w.a_log, w.dt_bias, w.norm_w, conv, rec, slots, gated)
+    o = F.linear(gated, w.w_out)
+    out = torch.empty(batch, C.HIDDEN, dtype=torch.float32, device=x.device)
+    _ext.residual_add(x, o, out)
+    return out
+
+
+@dataclass
+class GqaLaunch:
+    """Split-KV launch shape for one decode step of a batch."""
+
+    split_pages: int
+    max_splits: int
+    workspace: torch.Tensor | None
+
+
+def plan_gqa_split(lengths_after: list[int], device, workspace: torch.Tensor | None = None) -> GqaLaunch:
+    """Choose blocks-per-split for a batch whose KV lengths (after this step's
+    append) are ``lengths_after`` and size the split workspace."""
+    blocks = [_cdiv(n, C.KV_BLOCK) for n in lengths_after]
+    split_pages = _ext.gqa_split_pages(sum(blocks), C.FULL_NUM_KV_HEADS)
+    max_splits = max(_cdiv(b, split_pages) for b in blocks)
+    need = _ext.gqa_workspace_bytes(len(blocks), max_splits) if max_splits > 1 else 0
+    if need:
+        if workspace is None or workspace.numel() * workspace.element_size() < need:
+            workspace = torch.empty(_cdiv(need, 16) * 4, dtype=torch.float32, device=device)
+    return GqaLaunch(split_pages, max_splits, workspace)
+
+
+def gqa_decode(x: torch.Tensor, w: GqaWeights, k_pool: torch.Tensor, v_pool: torch.Tensor,
+               block_table: torch.Tensor, inv_freq: torch.Tensor, launch: GqaLaunch,
+               seq_lens: torch.Tensor | None = None, positions: torch.Tensor | None = None,
+               seq_len0: int = 0, position0: int = 0) -> torch.Tensor:
+    """One GQA layer step for ``x`` [B, 2048] fp32; returns the residual.  The
+    new token of sequence i is appended to the pool at index seq_lens[i]."""
+    batch = x.shape[0]
+    h = torch.empty(batch, C.HIDDEN, dtype=torch.bfloat16, device=x.device)
+    _ext.rmsnorm_rows(x, w.in_norm, h)
+    proj = F.linear(h, w.w_in)
+    attn = torch.empty(batch, C.FULL_Q_DIM, dtype=torch.bfloat16, device=x.device)
+    _ext.gqa_decode_paged(
+        proj[:, C.GQA_PROJ_Q[0]:C.GQA_PROJ_Q[1]], proj[:, C.GQA_PROJ_K[0]:C.GQA_PROJ_K[1]],
+        proj[:, C.GQA_PROJ_V[0]:C.GQA_PROJ_V[1]], w.q_norm, w.k_norm, inv_freq, k_pool, v_pool, block_table,
+        seq_lens, positions, attn, launch.workspace, launch.split_pages, launch.max_splits,
+        seq_len0=seq_len0, position0=position0)
+    o = F.linear(attn, w.w_out)
+    out = torch.empty(batch, C.HIDDEN, dtype=torch.float32, device=x.device)
+    _ext.residual_add(x, o, out)
+    return out
+
+
+class BlockAllocator:
+    """Free list of physical KV blocks shared by every GQA layer's pool."""
+
+    def __init__(self, num_blocks: int):
+        self.num_blocks = int(num_blocks)
+        self._free = list(range(self.num_blocks - 1, -1, -1))
+
+    def alloc(self, n: int) -> list[int]:
+        if n > len(self._free):
+            raise RuntimeError(f"KV pool exhausted: need {n} blocks, {len(self._free)} free of {self.num_blocks}")
+        return [self._free.pop() for _ in range(n)]
+
+    def free(self, blocks: list[int]) -> None:
+        self._free.extend(reversed(blocks))
+
+    @property
+    def free_blocks(self) -> int:
+        return len(self._free)
+
+
+@dataclass
+class BatchedAttentionState:
+    """Decode state of B sequences over the whole hybrid stack on one device.
+
+    ``layers`` maps a layer index to DeltaNetWeights or GqaWeights.  Sequences
+    occupy slots 0..B-1; their KV lengths and absolute positions live on the
+    device (``seq_lens``, ``positions``) with a host mirror used for planning.
+    """
+
+    layers: dict[int, DeltaNetWeights | GqaWeights]
+    batch: int
+    pool_blocks: int
+    max_blocks_per_seq: int
+    device: torch.device
+    rec: dict[int, torch.Tensor] = field(default_factory=dict)
+    conv: dict[int, torch.Tensor] = field(default_factory=dict)
+    k_pool: dict[int, torch.Tensor] = field(default_factory=dict)
+    v_pool: dict[int, torch.Tensor] = field(default_factory=dict)
+
+    def __post_init__(self):
+        dev = self.device
+        for layer, w in self.layers.items():
+            if isinstance(w, DeltaNetWeights):
+                self.rec[layer] = torch.zeros(self.batch, C.LINEAR_NUM_V_HEADS, C.LINEAR_HEAD_DIM,
+                                              C.LINEAR_HEAD_DIM, dtype=torch.float32, device=dev)
+                self.conv[layer] = torch.zeros(self.batch, C.LINEAR_CONV_DIM, C.LINEAR_CONV_STATE,
+                                               dtype=torch.bfloat16, device=dev)
+            else:
+                shape = (C.FULL_NUM_KV_HEADS, self.pool_blocks * C.KV_BLOCK, C.FULL_HEAD_DIM)
+                self.k_pool[layer] = torch.zeros(shape, dtype=torch.bfloat16, device=dev)
+                self.v_pool[layer] = torch.zeros(shape, dtype=torch.bfloat16, device=dev)
+        self.allocator = BlockAllocator(self.pool_blocks)
+        self.block_table = torch.zeros(self.batch, self.max_blocks_per_seq, dtype=torch.int32, device=dev)
+        self._table_host = torch.zeros(self.batch, self.max_blocks_per_seq, dtype=torch.int32)
+        self._blocks: list[list[int]] = [[] for _ in range(self.batch)]
+        self.lengths: list[int] = [0] * self.batch
+        self.positions_host: list[int] = [0] * self.batch
+        self.seq_lens = torch.zeros(self.batch, dtype=torch.int32, device=dev)
+        self.positions = torch.zeros(self.batch, dtype=torch.int32, device=dev)
+        self.inv_freq = rope_inv_freq(dev)
+        self._workspace: torch.Tensor | None = None
+
+    # ---- bookkeeping
+    def reserve(self, seq: int, total_tokens: int) -> None:
+        """Make sure sequence ``seq`` owns blocks for ``total_tokens`` tokens."""
+        need = _cdiv(total_tokens, C.KV_BLOCK)
+        if need > self.max_blocks_per_seq:
+            raise RuntimeError(f"sequence {seq} needs {need} blocks > max_blocks_per_seq={self.max_blocks_per_seq}")
+        have = len(self._blocks[seq])
+        if need > have:
+            new = self.allocator.alloc(need - have)
+            self._blocks[seq].extend(new)
+            self._table_host[seq, have:need] = torch.tensor(new, dtype=torch.int32)
+
+    def sync_tables(self) -> None:
+        """Upload the block table and lengths (call after reserve/set_length)."""
+        self.block_table.copy_(self._table_host)
+        self.seq_lens.copy_(torch.tensor(self.lengths, dtype=torch.int32))
+        self.positions.copy_(torch.tensor(self.positions_host, dtype=torch.int32))
+
+    def set_length(self, seq: int, length: int, position: int | None = None) -> None:
+        self.reserve(seq, length)
+        self.lengths[seq] = int(length)
+        self.positions_host[seq] = int(length if position is None else position)
+
+    def physical_rows(self, seq: int, length: int) -> torch.Tensor:
+        """Pool row indices (per KV head) of the first ``length`` tokens."""
+        blocks = torch.tensor(self._blocks[seq][: _cdiv(length, C.KV_BLOCK)], dtype=torch.int64)
+        rows = (blocks[:, None] * C.KV_BLOCK + torch.arange(C.KV_BLOCK)[None, :]).reshape(-1)
+        return rows[:length]
+
+    # ---- one decode step over all layers
+    def plan(self) -> GqaLaunch:
+        launch = plan_gqa_split([n + 1 for n in self.lengths], self.device, self._workspace)
+        self._workspace = launch.workspace
+        return launch
+
+    def prepare_step(self) -> GqaLaunch:
+        """Reserve the block of each sequence's next token and plan the launch."""
+        grew = False
+        for i, n in enumerate(self.lengths):
+            if n % C.KV_BLOCK == 0 and len(self._blocks[i]) * C.KV_BLOCK <= n:
+                self.reserve(i, n + 1)
+                grew = True
+        if grew:
+            self.block_table.copy_(self._table_host)
+        return self.plan()
+
+    def step(self, x: torch.Tensor, launch: GqaLaunch | None = None, advance: bool = True) -> torch.Tensor:
+        """Run every layer once for the batch: x [B, 2048] fp32 -> [B, 2048] fp32.
+
+        This is ``run_forward_token``'s attention chain (qwen36_chat_batch.py:
+        184-187) without the MoE; ``advance`` then moves every sequence one
+        position forward on the device (the caller's ``tokens_seen += 1``)."""
+        if launch is None:
+            launch = self.prepare_step()
+        for layer in sorted(self.layers):
+            w = self.layers[layer]
+            if isinstance(w, DeltaNetWeights):
+                x = deltanet_decode(x, w, self.rec[layer], self.conv[layer])
+            else:
+                x = gqa_decode(x, w, self.k_pool[layer], self.v_pool[layer], self.block_table, self.inv_freq,
+                               launch, self.seq_lens, self.positions)
+        if advance:
+            _ext.advance_positions(self.seq_lens, self.positions)
+            self.lengths = [n + 1 for n in self.lengths]
+            self.positions_host = [p + 1 for p in self.positions_host]
+        return x

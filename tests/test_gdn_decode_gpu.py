@@ -1,0 +1,137 @@
+"""K1 (fused Gated DeltaNet decode step) against the CPU oracle.
+
+Tolerances (bf16 I/O, fp32 state): outputs within 2e-2 max-abs and 1e-2
+relative RMS of the oracle; the fp32 state within 1e-3 relative RMS after 1024
+steps (checked against an fp64 recurrence on the same kernel inputs)."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from oracle import attention_oracle as O
+from ria_b200 import _ext, synthetic
+from ria_b200 import constants as C
+from ria_b200.weights import DeltaNetWeights
+
+pytestmark = pytest.mark.gpu
+
+OUT_MAX_ABS = 2e-2
+OUT_REL_RMS = 1e-2
+STATE_REL_RMS = 1e-3
+
+
+def _proj_inputs(batch: int, gen: torch.Generator, scale: float = 1.0):
+    """Random projection outputs (bf16) in the fused [qkv | z | b | a] layout."""
+    p = torch.randn(batch, C.DN_PROJ_WIDTH, generator=gen) * scale
+    return p.to(torch.bfloat16)
+
+
+def _split(p):
+    return (p[:, C.DN_PROJ_QKV[0]:C.DN_PROJ_QKV[1]], p[:, C.DN_PROJ_Z[0]:C.DN_PROJ_Z[1]],
+            p[:, C.DN_PROJ_B[0]:C.DN_PROJ_B[1]], p[:, C.DN_PROJ_A[0]:C.DN_PROJ_A[1]])
+
+
+def test_kernel_boundary_1024_steps_state_drift(cuda_device):
+    torch.manual_seed(0)
+    wt = synthetic.deltanet_weights(7)
+    w = DeltaNetWeights.from_tensors(wt, cuda_device)
+    batch = 2
+    gen = torch.Generator().manual_seed(1)
+    rec = torch.zeros(batch, 32, 128, 128, device=cuda_device)
+    conv = torch.zeros(batch, 8192, 4, dtype=torch.bfloat16, device=cuda_device)
+    rec64 = torch.zeros(batch, 32, 128, 128, dtype=torch.float64)
+    conv_ref = torch.zeros(batch, 8192, 4, dtype=torch.bfloat16)
+    out = torch.empty(batch, 4096, dtype=torch.bfloat16, device=cuda_device)
+    worst_abs = worst_rel = 0.0
+    for step in range(1024):
+        p = _proj_inputs(batch, gen)
+        pd = p.to(cuda_device)
+        _ext.gdn_decode_step(*_split(pd), w.conv_w, w.a_log, w.dt_bias, w.norm_w, conv, rec, None, out)
+        mixed, z, b, a = (t.float() for t in _split(p))
+        ref_out, conv_ref, rec64 = O.deltanet_kernel_ref(mixed, z, b, a, wt, conv_ref, rec64, dtype=torch.float64)
+        if step % 64 == 0 or step == 1023:
+            got = out.float().cpu()
+            worst_abs = max(worst_abs, O.max_abs(got, ref_out))
+            worst_rel = max(worst_rel, O.rel_rms(got, ref_out))
+    assert _ext.device_error() == 0
+    assert worst_abs < OUT_MAX_ABS and worst_rel < OUT_REL_RMS, (worst_abs, worst_rel)
+    state_err = O.rel_rms(rec.double().cpu(), rec64)
+    assert state_err < STATE_REL_RMS, state_err
+    conv_mismatch = (conv.cpu().float() != conv_ref.float()).float().mean().item()
+    assert conv_mismatch == 0.0
+
+
+def test_slots_ragged_batch_matches_single_sequence_calls(cuda_device):
+    wt = synthetic.deltanet_weights(3)
+    w = DeltaNetWeights.from_tensors(wt, cuda_device)
+    gen = torch.Generator().manual_seed(2)
+    num_slots, batch = 7, 5
+    rec0 = (torch.randn(num_slots, 32, 128, 128, generator=gen) * 0.1).to(cuda_device)
+    conv0 = (torch.randn(num_slots, 8192, 4, generator=gen) * 0.1).to(torch.bfloat16).to(cuda_device)
+    slots = torch.tensor([6, 0, 3, 2, 5], dtype=torch.int32, device=cuda_device)
+    p = _proj_inputs(batch, gen).to(cuda_device)
+    rec, conv = rec0.clone(), conv0.clone()
+    out = torch.empty(batch, 4096, dtype=torch.bfloat16, device=cuda_device)
+    _ext.gdn_decode_step(*_split(p), w.conv_w, w.a_log, w.dt_bias, w.norm_w, conv, rec, slots, out)
+    for i, s in enumerate(slots.tolist()):
+        r1, c1 = rec0[s:s + 1].clone(), conv0[s:s + 1].clone()
+        o1 = torch.empty(1, 4096, dtype=torch.bfloat16, device=cuda_device)
+        _ext.gdn_decode_step(*_split(p[i:i + 1]), w.conv_w, w.a_log, w.dt_bias, w.norm_w, c1, r1, None, o1)
+        assert torch.equal(o1, out[i:i + 1])
+        assert torch.equal(r1, rec[s:s + 1])
+        assert torch.equal(c1, conv[s:s + 1])
+    untouched = [1, 4]
+    assert torch.equal(rec[untouched], rec0[untouched]) and torch.equal(conv[untouched], conv0[untouched])
+    # and the batch result equals the oracle from the same starting state
+    mixed, z, b, a = (t.float().cpu() for t in _split(p))
+    sl = slots.long().cpu()
+    ref_out, _, ref_rec = O.deltanet_kernel_ref(mixed, z, b, a, wt, conv0.cpu()[sl], rec0.cpu()[sl])
+    assert O.max_abs(out.float().cpu(), ref_out) < OUT_MAX_ABS
+    assert O.rel_rms(rec.cpu()[sl], ref_rec) < 1e-5
+
+
+def test_large_batch_many_units_per_cta(cuda_device):
+    """More units than SMs: every CTA walks several (sequence, key head)
+    units through the TMA ring."""
+    wt = synthetic.deltanet_weights(4)
+    w = DeltaNetWeights.from_tensors(wt, cuda_device)
+    gen = torch.Generator().manual_seed(3)
+    batch = 37
+    rec0 = (torch.randn(batch, 32, 128, 128, generator=gen) * 0.1)
+    conv0 = (torch.randn(batch, 8192, 4, generator=gen) * 0.5).to(torch.bfloat16)
+    p = _proj_inputs(batch, gen)
+    rec, conv = rec0.to(cuda_device), conv0.to(cuda_device)
+    out = torch.empty(batch, 4096, dtype=torch.bfloat16, device=cuda_device)
+    _ext.gdn_decode_step(*_split(p.to(cuda_device)), w.conv_w, w.a_log, w.dt_bias, w.norm_w, conv, rec, None, out)
+    mixed, z, b, a = (t.float() for t in _split(p))
+    ref_out, ref_conv, ref_rec = O.deltanet_kernel_ref(mixed, z, b, a, wt, conv0, rec0)
+    assert O.max_abs(out.float().cpu(), ref_out) < OUT_MAX_ABS
+    assert O.rel_rms(out.float().cpu(), ref_out) < OUT_REL_RMS
+    assert O.rel_rms(rec.cpu(), ref_rec) < 1e-5
+    assert torch.equal(conv.cpu(), ref_conv)
+    assert _ext.device_error() == 0
+
+
+def test_extreme_gates_stay_finite(cuda_device):
+    """Decay near 0 (g down to about -40), softplus above its threshold and
+    saturated sigmoids follow torch's semantics."""
+    wt = synthetic.deltanet_weights(5)
+    wt["linear_attn.A_log"] = torch.full((32,), 3.0)
+    w = DeltaNetWeights.from_tensors(wt, cuda_device)
+    gen = torch.Generator().manual_seed(4)
+    p = _proj_inputs(2, gen).float()
+    p[:, C.DN_PROJ_A[0]:C.DN_PROJ_A[1]] = 25.0  # softplus(x) = x branch, g ~ -500
+    p[0, C.DN_PROJ_B[0]:C.DN_PROJ_B[1]] = -30.0  # beta ~ 0
+    p[1, C.DN_PROJ_B[0]:C.DN_PROJ_B[1]] = 30.0  # beta ~ 1
+    p = p.to(torch.bfloat16)
+    rec0 = torch.randn(2, 32, 128, 128, generator=gen)
+    conv0 = torch.zeros(2, 8192, 4, dtype=torch.bfloat16)
+    rec, conv = rec0.to(cuda_device), conv0.to(cuda_device)
+    out = torch.empty(2, 4096, dtype=torch.bfloat16, device=cuda_device)
+    _ext.gdn_decode_step(*_split(p.to(cuda_device)), w.conv_w, w.a_log, w.dt_bias, w.norm_w, conv, rec, None, out)
+    mixed, z, b, a = (t.float() for t in _split(p))
+    ref_out, _, ref_rec = O.deltanet_kernel_ref(mixed, z, b, a, wt, conv0, rec0)
+    assert O.finite(out.float()) and O.finite(rec)
+    assert O.max_abs(out.float().cpu(), ref_out) < OUT_MAX_ABS
+    assert O.max_abs(rec.cpu(), ref_rec) < 1e-5
