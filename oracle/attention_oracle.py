@@ -296,6 +296,14 @@ def max_abs(a: torch.Tensor, b: torch.Tensor) -> float:
     return (a.double() - b.double()).abs().max().item()
 
 
+def max_err_bf16(a: torch.Tensor, b: torch.Tensor) -> float:
+    """max |a - b| / max(1, |b|): absolute error for |b| <= 1 and relative
+    error above, the scale-aware form of a max-abs bound for values that are
+    stored in bf16 (whose rounding step grows with magnitude)."""
+    a64, b64 = a.double(), b.double()
+    return ((a64 - b64).abs() / b64.abs().clamp(min=1.0)).max().item()
+
+
 def finite(x: torch.Tensor) -> bool:
     return bool(torch.isfinite(x).all())
 

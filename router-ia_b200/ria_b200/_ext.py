@@ -189,14 +189,14 @@ def residual_add(x0, proj, out):
     with _Hooked("residual_add"):
         rc = lib().ria_residual_add(x0.data_ptr(), x0.stride(0), proj.data_ptr(), proj.stride(0), out.data_ptr(),
                                     out.stride(0), x0.shape[0], x0.shape[1], _stream(x0))
-        _check(rc, "ria_residual_add")
-    
-    
-    def conv1d_step(x, conv_state, weight, out):
-        _require_cuda(x, conv_state, weight, out)
-        with _Hooked("conv1d_step"):
-            rc = lib().ria_conv1d_step(x.data_ptr(), x.stride(0), conv_state.data_ptr(), weight.data_ptr(), out.data_ptr(),
-                                   out.stride(0), x.shape[0], x.shape[1], _stream(x))
+    _check(rc, "ria_residual_add")
+
+
+def conv1d_step(x, conv_state, weight, out):
+    _require_cuda(x, conv_state, weight, out)
+    with _Hooked("conv1d_step"):
+        rc = lib().ria_conv1d_step(x.data_ptr(), x.stride(0), conv_state.data_ptr(), weight.data_ptr(),
+                                   out.data_ptr(), out.stride(0), x.shape[0], x.shape[1], _stream(x))
     _check(rc, "ria_conv1d_step")
 
 

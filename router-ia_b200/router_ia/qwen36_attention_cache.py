@@ -315,7 +315,7 @@ def _apply_rope(q: torch.Tensor, k: torch.Tensor, position: int) -> tuple[torch.
     inv = _inv_freq(dev)
     outs = []
     for t in (q, k):
-        rows = t.detach().to(device=dev, dtype=torch.float32).reshape(-1, t.shape[-1]).contiguous()
+        rows = t.detach().to(device=dev, dtype=torch.float32).reshape(-1, t.shape[-1]).clone()
         _ext.rope_apply(rows, inv, ROPE_DIM, int(position))
         outs.append(rows.reshape(t.shape).to(dtype=t.dtype))
     return outs[0], outs[1]

@@ -1,8 +1,10 @@
 """K1 (fused Gated DeltaNet decode step) against the CPU oracle.
 
-Tolerances (bf16 I/O, fp32 state): outputs within 2e-2 max-abs and 1e-2
-relative RMS of the oracle; the fp32 state within 1e-3 relative RMS after 1024
-steps (checked against an fp64 recurrence on the same kernel inputs)."""
+Tolerances (bf16 I/O, fp32 state): outputs within 2e-2 of the oracle in the
+scale-aware max form (``max |d| / max(1, |ref|)``: the kernel stores bf16,
+whose rounding step exceeds 2e-2 above |x| = 4) and 1e-2 relative RMS; the
+fp32 state within 1e-3 relative RMS after 1024 steps (against an fp64
+recurrence on the same kernel inputs)."""
 
 from __future__ import annotations
 
@@ -52,7 +54,7 @@ def test_kernel_boundary_1024_steps_state_drift(cuda_device):
         ref_out, conv_ref, rec64 = O.deltanet_kernel_ref(mixed, z, b, a, wt, conv_ref, rec64, dtype=torch.float64)
         if step % 64 == 0 or step == 1023:
             got = out.float().cpu()
-            worst_abs = max(worst_abs, O.max_abs(got, ref_out))
+            worst_abs = max(worst_abs, O.max_err_bf16(got, ref_out))
             worst_rel = max(worst_rel, O.rel_rms(got, ref_out))
     assert _ext.device_error() == 0
     assert worst_abs < OUT_MAX_ABS and worst_rel < OUT_REL_RMS, (worst_abs, worst_rel)
@@ -87,7 +89,7 @@ def test_slots_ragged_batch_matches_single_sequence_calls(cuda_device):
     mixed, z, b, a = (t.float().cpu() for t in _split(p))
     sl = slots.long().cpu()
     ref_out, _, ref_rec = O.deltanet_kernel_ref(mixed, z, b, a, wt, conv0.cpu()[sl], rec0.cpu()[sl])
-    assert O.max_abs(out.float().cpu(), ref_out) < OUT_MAX_ABS
+    assert O.max_err_bf16(out.float().cpu(), ref_out) < OUT_MAX_ABS
     assert O.rel_rms(rec.cpu()[sl], ref_rec) < 1e-5
 
 
@@ -106,7 +108,7 @@ def test_large_batch_many_units_per_cta(cuda_device):
     _ext.gdn_decode_step(*_split(p.to(cuda_device)), w.conv_w, w.a_log, w.dt_bias, w.norm_w, conv, rec, None, out)
     mixed, z, b, a = (t.float() for t in _split(p))
     ref_out, ref_conv, ref_rec = O.deltanet_kernel_ref(mixed, z, b, a, wt, conv0, rec0)
-    assert O.max_abs(out.float().cpu(), ref_out) < OUT_MAX_ABS
+    assert O.max_err_bf16(out.float().cpu(), ref_out) < OUT_MAX_ABS
     assert O.rel_rms(out.float().cpu(), ref_out) < OUT_REL_RMS
     assert O.rel_rms(rec.cpu(), ref_rec) < 1e-5
     assert torch.equal(conv.cpu(), ref_conv)
@@ -133,5 +135,5 @@ def test_extreme_gates_stay_finite(cuda_device):
     mixed, z, b, a = (t.float() for t in _split(p))
     ref_out, _, ref_rec = O.deltanet_kernel_ref(mixed, z, b, a, wt, conv0, rec0)
     assert O.finite(out.float()) and O.finite(rec)
-    assert O.max_abs(out.float().cpu(), ref_out) < OUT_MAX_ABS
+    assert O.max_err_bf16(out.float().cpu(), ref_out) < OUT_MAX_ABS
     assert O.max_abs(rec.cpu(), ref_rec) < 1e-5
