@@ -118,6 +118,30 @@ RIA_API int ria_gqa_decode_paged(const void* q, int64_t q_stride, const void* k,
                          int64_t workspace_bytes, int32_t batch, int32_t split_pages, int32_t max_splits,
                          ria_stream_t stream);
 
+/* Allocation-free variant of ria_gqa_decode_paged.  No counterpart in the
+ * reference (router-ia has no device kernels); it exists for callers that
+ * cannot allocate device memory where they decode -- code being captured into
+ * a CUDA graph, runtimes that own all GPU memory or hold a hard VRAM budget,
+ * plugin interfaces that provide no workspace.  Same arguments as
+ * ria_gqa_decode_paged without the workspace: the split partials go to a
+ * fixed RIA_GQA_STATIC_SCRATCH_BYTES array inside the library, present on
+ * every GPU that loads the library until the process exits.  Calls needing
+ * more (ria_gqa_decode_workspace_bytes(batch, max_splits) larger than that)
+ * fail with RIA_ERR_INVALID.  The first call on a device looks up the array's
+ * device address (cudaGetSymbolAddress, with that device current); make that
+ * first call before any stream capture.  All calls on a device share the
+ * array: calls whose kernels can overlap on the GPU race; calls ordered on one
+ * stream do not.  Allocates nothing (no cudaMalloc/cudaFree). */
+#define RIA_GQA_STATIC_SCRATCH_BYTES (4u << 20)
+RIA_API int ria_gqa_decode_paged_static(const void* q, int64_t q_stride, const void* k, int64_t k_stride,
+                                        const void* v, int64_t v_stride, const float* q_norm_weight,
+                                        const float* k_norm_weight, const float* inv_freq, void* k_pool,
+                                        void* v_pool, int64_t pool_tokens, const int32_t* block_table,
+                                        int32_t block_table_stride, const int32_t* seq_lens,
+                                        const int32_t* positions, int32_t seq_len0, int32_t position0, void* out,
+                                        int64_t out_stride, int32_t batch, int32_t split_pages, int32_t max_splits,
+                                        ria_stream_t stream);
+
 /* Split size heuristic used by the Python host: KV blocks per split so that the
  * grid holds a few waves of CTAs for `total_blocks` blocks of work. */
 RIA_API int32_t ria_gqa_decode_split_pages(int64_t total_blocks, int32_t num_kv_heads);

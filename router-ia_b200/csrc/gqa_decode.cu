@@ -27,6 +27,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <mutex>
 
 #include "ria_capi_internal.h"
 #include "ria_common.cuh"
@@ -567,4 +568,86 @@ extern "C" int ria_gqa_decode_paged(const void* q, int64_t q_stride, const void*
     rc = ria::check_launch("ria_gqa_decode_paged (combine)");
   }
   return rc;
+}
+
+// ---------------------------------------------------------------- allocation-free variant
+//
+// Some callers cannot allocate device memory at the point where they decode:
+// code that is being captured into a CUDA graph (cudaMalloc is not allowed
+// during capture and synchronises the device), host runtimes that own all GPU
+// memory through their own pool or hold a hard VRAM budget, and plugin
+// interfaces that hand a kernel its inputs and outputs but no workspace.  For
+// them ria_gqa_decode_paged_static keeps the split partials in a fixed array
+// that is part of the library image instead of a caller workspace.
+//
+// The array lives for as long as the library is loaded, on every GPU that
+// loads it (RIA_GQA_STATIC_SCRATCH_BYTES each).  All calls on a device share
+// it, so two calls whose kernels overlap on the GPU (different streams without
+// ordering between them) race on it; calls ordered on one stream are safe.
+// Nothing in it has to start at zero: every partial the combine pass reads was
+// written by the attention pass of the same call.  The array keeps the last
+// call's partials.
+namespace {
+
+static __device__ __align__(256) unsigned char g_gqa_static_scratch[RIA_GQA_STATIC_SCRATCH_BYTES];
+
+// Device address of g_gqa_static_scratch on the current device.  Host code
+// cannot use the symbol itself (it names a host-side shadow, not device
+// memory), so the address is looked up once per device, with that device
+// current, and cached.
+void* gqa_static_scratch(int* rc_out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    *rc_out = ria::fail(RIA_ERR_CUDA, "ria_gqa_decode_paged_static: cudaGetDevice: %s", cudaGetErrorString(e));
+    return nullptr;
+  }
+  if (dev < 0 || dev >= 64) {
+    *rc_out = ria::fail(RIA_ERR_UNSUPPORTED, "ria_gqa_decode_paged_static: device %d out of range", dev);
+    return nullptr;
+  }
+  static std::mutex mu;
+  static void* cache[64] = {nullptr};
+  std::lock_guard<std::mutex> lock(mu);
+  if (!cache[dev]) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_gqa_static_scratch);
+    if (e != cudaSuccess || ptr == nullptr) {
+      *rc_out = ria::fail(RIA_ERR_CUDA, "ria_gqa_decode_paged_static: cudaGetSymbolAddress: %s",
+                          cudaGetErrorString(e));
+      return nullptr;
+    }
+    cache[dev] = ptr;
+  }
+  *rc_out = RIA_OK;
+  return cache[dev];
+}
+
+}  // namespace
+
+extern "C" int ria_gqa_decode_paged_static(const void* q, int64_t q_stride, const void* k, int64_t k_stride,
+                                           const void* v, int64_t v_stride, const float* q_norm_weight,
+                                           const float* k_norm_weight, const float* inv_freq, void* k_pool,
+                                           void* v_pool, int64_t pool_tokens, const int32_t* block_table,
+                                           int32_t block_table_stride, const int32_t* seq_lens,
+                                           const int32_t* positions, int32_t seq_len0, int32_t position0, void* out,
+                                           int64_t out_stride, int32_t batch, int32_t split_pages, int32_t max_splits,
+                                           ria_stream_t stream) {
+  if (batch < 0 || max_splits < 1)
+    return ria::fail(RIA_ERR_INVALID, "ria_gqa_decode_paged_static: batch=%d max_splits=%d", batch, max_splits);
+  if (batch == 0) return RIA_OK;
+  const int64_t need = ria_gqa_decode_workspace_bytes(batch, max_splits);
+  if (max_splits > 1 && need > static_cast<int64_t>(RIA_GQA_STATIC_SCRATCH_BYTES))
+    return ria::fail(RIA_ERR_INVALID,
+                     "ria_gqa_decode_paged_static: batch=%d x max_splits=%d needs %lld bytes of split scratch, more "
+                     "than the fixed %lld-byte array; use a larger split_pages or ria_gqa_decode_paged with a workspace",
+                     batch, max_splits, static_cast<long long>(need),
+                     static_cast<long long>(RIA_GQA_STATIC_SCRATCH_BYTES));
+  int rc = RIA_OK;
+  void* scratch = gqa_static_scratch(&rc);
+  if (!scratch) return rc;
+  return ria_gqa_decode_paged(q, q_stride, k, k_stride, v, v_stride, q_norm_weight, k_norm_weight, inv_freq, k_pool,
+                              v_pool, pool_tokens, block_table, block_table_stride, seq_lens, positions, seq_len0,
+                              position0, out, out_stride, scratch, RIA_GQA_STATIC_SCRATCH_BYTES, batch, split_pages,
+                              max_splits, stream);
 }

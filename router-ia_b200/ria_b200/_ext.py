@@ -60,6 +60,12 @@ _SIGNATURES: dict[str, tuple[object, list]] = {
          c_int64, c_void_p, c_int32, c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_int64, c_void_p, c_int64,
          c_int32, c_int32, c_int32, c_void_p],
     ),
+    "ria_gqa_decode_paged_static": (
+        c_int,
+        [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+         c_int64, c_void_p, c_int32, c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_int64, c_int32, c_int32,
+         c_int32, c_void_p],
+    ),
     "ria_advance_positions": (c_int, [c_void_p, c_void_p, c_int32, c_void_p]),
     "ria_rmsnorm_rows": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int32, c_int32, c_void_p]),
     "ria_residual_add": (
@@ -168,6 +174,24 @@ def gqa_decode_paged(q, k, v, q_norm_w, k_norm_w, inv_freq, k_pool, v_pool, bloc
             int(position0), out.data_ptr(), out.stride(0), _ptr(workspace), ws_bytes, batch, int(split_pages),
             int(max_splits), _stream(q))
     _check(rc, "ria_gqa_decode_paged")
+
+
+GQA_STATIC_SCRATCH_BYTES = 4 << 20  # RIA_GQA_STATIC_SCRATCH_BYTES
+
+
+def gqa_decode_paged_static(q, k, v, q_norm_w, k_norm_w, inv_freq, k_pool, v_pool, block_table, seq_lens,
+                            positions, out, split_pages, max_splits, seq_len0=0, position0=0):
+    """K3 with the split partials in the library's fixed device array instead
+    of a caller workspace (see ria_gqa_decode_paged_static): for callers that
+    cannot allocate device memory where they decode."""
+    _require_cuda(q, k, v, k_pool, v_pool, block_table, out)
+    with _Hooked("gqa_decode", 2 if int(max_splits) > 1 else 1):
+        rc = lib().ria_gqa_decode_paged_static(
+            q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0), q_norm_w.data_ptr(),
+            k_norm_w.data_ptr(), inv_freq.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(), k_pool.shape[1],
+            block_table.data_ptr(), block_table.stride(0), _ptr(seq_lens), _ptr(positions), int(seq_len0),
+            int(position0), out.data_ptr(), out.stride(0), q.shape[0], int(split_pages), int(max_splits), _stream(q))
+    _check(rc, "ria_gqa_decode_paged_static")
 
 
 def advance_positions(seq_lens, positions):
