@@ -42,6 +42,12 @@ METRIC = "attn decode tokens/s/GPU + %HBM peak; DeltaNet chunked prefill tokens/
 UNIT = "tokens/s"
 B_DN = 4_292_736  # algorithmic bytes of K1 per (sequence, layer)
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) over algorithmic
+# bytes, from one ncu capture of each kernel on a small case
+# (profiles/gqa_decode_kernel_b32_l4096.md: 280.3 / 269.3 MB;
+#  profiles/gdn_decode_kernel_b64.md: 222.0 / 274.7 MB, written state partly
+#  still in L2 at kernel end).  Traffic of a full launch = ratio x its bytes.
+TRAFFIC_RATIO = {"gqa_decode": 280.3 / 269.3, "gdn_decode": 222.0 / 274.7}
 
 
 def parse_args():
@@ -154,12 +160,16 @@ class EventHook:
 
 
 # --------------------------------------------------------------------------- workload
-def build_engine(args, device, rank, headroom):
+def build_engine(args, device, rank, world, headroom):
     from ria_b200 import constants as C, synthetic
     from ria_b200.engine import BatchedAttentionState
+    from ria_b200.sharding import shard_range
     from ria_b200.weights import DeltaNetWeights, GqaWeights
 
-    lengths = synthetic.ragged_lengths(args.batch, args.len_lo, args.len_hi, seed=rank)
+    # One seeded request list for the whole job; each rank decodes its shard.
+    requests = synthetic.ragged_lengths(world * args.batch, args.len_lo, args.len_hi, seed=0)
+    shard = shard_range(len(requests), world, rank)
+    lengths = requests[shard.start:shard.stop]
     layers = {}
     for layer in range(C.NUM_LAYERS):
         t = synthetic.layer_weights_on_device(layer, device, seed=0)
@@ -195,7 +205,7 @@ def run_ours(args, rank, world, device):
 
     headroom = args.warmup + 2 * args.steps + 4
     t_setup = time.perf_counter()
-    eng, lengths = build_engine(args, device, rank, headroom)
+    eng, lengths = build_engine(args, device, rank, world, headroom)
     setup_s = time.perf_counter() - t_setup
     x = torch.randn(args.batch, 2048, device=device).to(torch.bfloat16).float()
 
@@ -243,7 +253,11 @@ def run_ours(args, rank, world, device):
     t1.record()
     torch.cuda.synchronize(device)
     e2e_ms = reduce_max(t0.elapsed_time(t1), world, device)
-    dev_err = _ext.device_error()
+    from ria_b200.sharding import gather_to_rank0
+
+    per_rank = gather_to_rank0({"rank": rank, "device_error": _ext.device_error(), "seqs": len(lengths),
+                                "ms": elapsed_ms}, world)
+    dev_err = max(r["device_error"] for r in per_rank)
 
     p = peaks()
     gqa_ms, gqa_n = hook.mean_ms("gqa_decode")
@@ -284,7 +298,8 @@ def run_ours(args, rank, world, device):
         "roofline": {
             "kernel": dom, "bound": "hbm", "achieved": kernels[dom]["achieved_gbs"], "peak": p["hbm_gbs"],
             "unit": "GB/s", "frac": kernels[dom]["frac"], "peak_source": p["source"],
-            "traffic": None,
+            "traffic": TRAFFIC_RATIO[dom] * kernels[dom]["bytes_per_launch"],
+            "traffic_source": "ncu small-case ratio x full-launch algorithmic bytes",
         },
         "kernels": kernels,
         "step_hbm_fraction": step_bytes / ((elapsed_ms / args.steps) * 1e6) / p["hbm_gbs"],

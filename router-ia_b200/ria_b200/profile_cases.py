@@ -1,0 +1,106 @@
+"""Small, self-contained kernel cases for profiler captures and quick timing.
+
+    python router-ia_b200/ria_b200/profile_cases.py --kernel gdn --batch 64 --iters 20
+    python router-ia_b200/ria_b200/profile_cases.py --kernel gqa --batch 32 --len 4096 --iters 20
+
+Each case allocates only one layer's state (about 1 GB), so a multi-pass
+``ncu`` capture of one launch stays small, while one launch still moves more
+than the 126 MB L2 (DRAM counters stay meaningful).  Prints the mean CUDA-event
+time per launch and the achieved algorithmic bandwidth.
+"""
+
+from __future__ import annotations
+
+import argparse
+import sys
+from pathlib import Path
+
+if __package__ in (None, ""):
+    sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
+
+import torch  # noqa: E402
+
+from ria_b200 import _ext, synthetic  # noqa: E402
+from ria_b200 import constants as C  # noqa: E402
+from ria_b200.engine import plan_gqa_split  # noqa: E402
+from ria_b200.weights import DeltaNetWeights, GqaWeights, rope_inv_freq  # noqa: E402
+
+B_DN = 4_292_736
+
+
+def gdn_case(batch: int, iters: int, device) -> dict:
+    w = DeltaNetWeights.from_tensors(synthetic.layer_weights_on_device(0, device), device)
+    g = torch.Generator(device=device)
+    g.manual_seed(0)
+    rec = torch.randn(batch, 32, 128, 128, device=device, generator=g) * 0.1
+    conv = (torch.randn(batch, 8192, 4, device=device, generator=g) * 0.1).to(torch.bfloat16)
+    proj = torch.randn(batch, C.DN_PROJ_WIDTH, device=device, generator=g).to(torch.bfloat16)
+    out = torch.empty(batch, 4096, dtype=torch.bfloat16, device=device)
+    parts = (proj[:, :8192], proj[:, 8192:12288], proj[:, 12288:12320], proj[:, 12320:12352])
+
+    def run():
+        _ext.gdn_decode_step(*parts, w.conv_w, w.a_log, w.dt_bias, w.norm_w, conv, rec, None, out)
+
+    ms = _time(run, iters, device)
+    return {"kernel": "gdn_decode", "batch": batch, "ms": ms, "gbs": batch * B_DN / (ms * 1e6)}
+
+
+def gqa_case(batch: int, length: int, iters: int, device) -> dict:
+    w = GqaWeights.from_tensors(synthetic.layer_weights_on_device(3, device), device)
+    nb = (length + 1 + 63) // 64
+    pool_tokens = batch * nb * 64
+    g = torch.Generator(device=device)
+    g.manual_seed(1)
+    k_pool = torch.randn(2, pool_tokens, 256, device=device, generator=g).to(torch.bfloat16)
+    v_pool = torch.randn(2, pool_tokens, 256, device=device, generator=g).to(torch.bfloat16)
+    table = torch.arange(batch * nb, dtype=torch.int32, device=device).reshape(batch, nb)
+    proj = torch.randn(batch, C.GQA_PROJ_WIDTH, device=device, generator=g).to(torch.bfloat16)
+    lens = torch.full((batch,), length, dtype=torch.int32, device=device)
+    pos = lens.clone()
+    out = torch.empty(batch, 4096, dtype=torch.bfloat16, device=device)
+    inv = rope_inv_freq(device)
+    launch = plan_gqa_split([length + 1] * batch, device)
+
+    def run():
+        _ext.gqa_decode_paged(proj[:, :8192], proj[:, 8192:8704], proj[:, 8704:], w.q_norm, w.k_norm, inv, k_pool,
+                              v_pool, table, lens, pos, out, launch.workspace, launch.split_pages, launch.max_splits)
+
+    ms = _time(run, iters, device)
+    nbytes = batch * (2048 * length + 2048 + 24576)
+    return {"kernel": "gqa_decode", "batch": batch, "len": length, "ms": ms, "gbs": nbytes / (ms * 1e6),
+            "split_pages": launch.split_pages, "max_splits": launch.max_splits}
+
+
+def _time(fn, iters, device):
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize(device)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    torch.cuda.synchronize(device)
+    return s.elapsed_time(e) / iters
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--kernel", choices=("gdn", "gqa", "all"), default="all")
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--len", type=int, default=4096)
+    ap.add_argument("--iters", type=int, default=20)
+    args = ap.parse_args()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    if args.kernel in ("gdn", "all"):
+        print(gdn_case(args.batch, args.iters, dev), flush=True)
+    if args.kernel in ("gqa", "all"):
+        print(gqa_case(args.batch if args.kernel == "gqa" else max(1, args.batch // 2), args.len, args.iters, dev),
+              flush=True)
+    if _ext.device_error():
+        raise SystemExit("device error word set")
+
+
+if __name__ == "__main__":
+    main()
