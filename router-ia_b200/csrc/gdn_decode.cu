@@ -14,15 +14,22 @@
 //   * Work unit = (sequence, key head j): value heads 2j and 2j+1 share q/k, so
 //     the conv of the q/k channels, the L2 norms and the conv-state write happen
 //     exactly once per unit with no cross-CTA traffic.
-//   * Persistent grid (one 256-thread CTA per SM).  Each head's 64 KiB fp32
-//     state tile is streamed HBM -> SMEM by the TMA engine (cp.async.bulk,
-//     mbarrier completion) through a 3-stage ring, so the next tiles are in
-//     flight while the current one is reduced and written back.
-//   * One read and one write of the state: r = S^T k and S^T q are reduced in a
-//     single sweep of SMEM; o is rebuilt as decay*S^T q + d (k.q) so the update
-//     and the output need no second reduction; the updated tile is stored with
-//     16-byte coalesced st.global.v4 (512 contiguous bytes per warp row).
+//   * Persistent grid, two 256-thread CTAs per SM.  Each head's 64 KiB fp32
+//     state tile arrives as two 32 KiB halves by cp.async.bulk (the TMA engine,
+//     mbarrier completion) through a 3-slot ring per CTA; warps 0-3 own rows
+//     0-63 (first half), warps 4-7 rows 64-127.  Each thread moves its 16x4
+//     slice of the tile into registers, so a slot is handed back to the TMA
+//     right after the first barrier and the next halves stream in while the
+//     tile is reduced and written back.
+//   * One read and one write of the state: S^T k and S^T q are reduced in one
+//     sweep (with the raw, un-normalised q and k; the L2-norm scales are applied
+//     to the reduced sums), o is rebuilt as decay*S^T q + d (k.q), and the new
+//     tile is stored from registers with 16-byte coalesced stores.
+//   * The next unit's conv state, conv weights, projections and gates are
+//     loaded into registers one unit ahead, so the per-unit prologue never waits
+//     on global memory.  Two barriers per tile, two per unit.
 #include <algorithm>
+#include <mutex>
 
 #include "ria_capi_internal.h"
 #include "ria_common.cuh"
@@ -36,10 +43,11 @@ constexpr int kConvDim = 8192;
 constexpr int kKeyDim = 2048;
 constexpr int kValDim = 4096;
 constexpr int kThreads = 256;
-constexpr int kStages = 3;
-constexpr int kTileFloats = kD * kD;
-constexpr uint32_t kTileBytes = kTileFloats * 4;
-constexpr int kCopyChunks = 8;  // bulk copies per tile (8 KiB each)
+constexpr int kSlots = 3;                      // ring of half tiles
+constexpr int kTileFloats = kD * kD;           // 16384
+constexpr int kHalfFloats = kTileFloats / 2;   // 8192 (64 rows)
+constexpr uint32_t kHalfBytes = kHalfFloats * 4;
+constexpr int kCopyChunks = 4;                 // bulk copies per half tile (8 KiB each)
 
 struct GdnParams {
   const __nv_bfloat16* mixed;
@@ -66,59 +74,57 @@ struct GdnParams {
 
 // Shared-memory map (bytes).
 constexpr int kOffStage = 0;
-constexpr int kOffRed = kOffStage + kStages * kTileBytes;  // [8 warps][2][128] f32
-constexpr int kOffQ = kOffRed + 8 * 2 * kD * 4;            // [128] f32
-constexpr int kOffK = kOffQ + kD * 4;                      // [128] f32
-constexpr int kOffV = kOffK + kD * 4;                      // [2][128] f32
-constexpr int kOffDelta = kOffV + 2 * kD * 4;              // [128] f32
-constexpr int kOffScal = kOffDelta + kD * 4;               // [32] f32
-constexpr int kOffWred = kOffScal + 32 * 4;                // [8][4] f32
-constexpr int kOffBar = kOffWred + 32 * 4;                 // kStages x u64
-constexpr int kSmemBytes = kOffBar + kStages * 8;
+constexpr int kOffRed = kOffStage + kSlots * kHalfBytes;  // [8 warps][2][128] f32
+constexpr int kOffQ = kOffRed + 8 * 2 * kD * 4;           // [128] f32 raw q
+constexpr int kOffK = kOffQ + kD * 4;                     // [128] f32 raw k
+constexpr int kOffV = kOffK + kD * 4;                     // [2][128] f32
+constexpr int kOffDelta = kOffV + 2 * kD * 4;             // [128] f32
+constexpr int kOffScal = kOffDelta + kD * 4;              // [8] f32: beta[2], decay[2]
+constexpr int kOffWred = kOffScal + 8 * 4;                // [32] f32
+constexpr int kOffBar = kOffWred + 32 * 4;                // kSlots x u64
+constexpr int kSmemBytes = kOffBar + kSlots * 8;
 
-// scal[] slots
-constexpr int kSBeta = 0;    // [2]
-constexpr int kSDecay = 2;   // [2]
-
-__device__ __forceinline__ float silu_bf16(float acc) {
-  // conv1d output and SiLU both materialise in bf16 in the reference.
-  float y = bf16_round(acc);
-  return bf16_round(y / (1.0f + expf(-y)));
-}
-
-__device__ __forceinline__ float conv_channel(const GdnParams& p, int b, int slot, bool write, int ch) {
-  const __nv_bfloat16* st = p.conv_state + (static_cast<int64_t>(slot) * kConvDim + ch) * 4;
-  uint2 sraw = *reinterpret_cast<const uint2*>(st);
-  uint2 wraw = *reinterpret_cast<const uint2*>(p.conv_w + static_cast<int64_t>(ch) * 4);
-  __nv_bfloat16 x = p.mixed[static_cast<int64_t>(b) * p.mixed_stride + ch];
-  const __nv_bfloat162* s2 = reinterpret_cast<const __nv_bfloat162*>(&sraw);
-  const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&wraw);
-  float2 s01 = __bfloat1622float2(s2[0]);
-  float2 s23 = __bfloat1622float2(s2[1]);
-  float2 w01 = __bfloat1622float2(w2[0]);
-  float2 w23 = __bfloat1622float2(w2[1]);
-  float xf = __bfloat162float(x);
-  // history = [s0 s1 s2 s3 x]; last output reads history[1..4].
-  float acc = w01.x * s01.y;
-  acc = fmaf(w01.y, s23.x, acc);
-  acc = fmaf(w23.x, s23.y, acc);
-  acc = fmaf(w23.y, xf, acc);
-  // new state = [s1 s2 s3 x]
-  __nv_bfloat162 n0 = __halves2bfloat162(s2[0].y, s2[1].x);
-  __nv_bfloat162 n1 = __halves2bfloat162(s2[1].y, x);
-  uint2 nraw;
-  nraw.x = *reinterpret_cast<uint32_t*>(&n0);
-  nraw.y = *reinterpret_cast<uint32_t*>(&n1);
-  if (write) *reinterpret_cast<uint2*>(const_cast<__nv_bfloat16*>(st)) = nraw;
-  return silu_bf16(acc);
-}
+// Global inputs of one unit, loaded one unit ahead.
+struct Prefetch {
+  uint2 st_qk, w_qk, st_v, w_v;  // conv state / weights of this thread's two channels
+  __nv_bfloat16 x_qk, x_v;       // projection outputs of those channels
+  __nv_bfloat16 z0, z1;          // z of value heads 2j, 2j+1 (threads < 128)
+  __nv_bfloat16 bb, aa;          // b, a of value head 2j + tid (threads < 2)
+  float a_log, dt_bias;
+};
 
 __device__ __forceinline__ float softplus_torch(float x) {
   // torch.nn.functional.softplus, beta=1, threshold=20.
   return x > 20.0f ? x : log1pf(expf(x));
 }
 
-__global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const GdnParams p) {
+// Causal conv over history [s0 s1 s2 s3 x] (last output reads s1..x), then the
+// bf16 conv output and bf16 SiLU of the reference.  Returns y; writes the new
+// state [s1 s2 s3 x] to *st when `write`.
+__device__ __forceinline__ float conv_silu(uint2 sraw, uint2 wraw, __nv_bfloat16 x, __nv_bfloat16* st, bool write) {
+  const __nv_bfloat162* s2 = reinterpret_cast<const __nv_bfloat162*>(&sraw);
+  const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&wraw);
+  const float2 s01 = __bfloat1622float2(s2[0]);
+  const float2 s23 = __bfloat1622float2(s2[1]);
+  const float2 w01 = __bfloat1622float2(w2[0]);
+  const float2 w23 = __bfloat1622float2(w2[1]);
+  float acc = w01.x * s01.y;
+  acc = fmaf(w01.y, s23.x, acc);
+  acc = fmaf(w23.x, s23.y, acc);
+  acc = fmaf(w23.y, __bfloat162float(x), acc);
+  if (write) {
+    __nv_bfloat162 n0 = __halves2bfloat162(s2[0].y, s2[1].x);
+    __nv_bfloat162 n1 = __halves2bfloat162(s2[1].y, x);
+    uint2 nraw;
+    nraw.x = *reinterpret_cast<uint32_t*>(&n0);
+    nraw.y = *reinterpret_cast<uint32_t*>(&n1);
+    *reinterpret_cast<uint2*>(st) = nraw;
+  }
+  const float y = bf16_round(acc);
+  return bf16_round(y / (1.0f + expf(-y)));
+}
+
+__global__ void __launch_bounds__(kThreads, 2) gdn_decode_kernel(const GdnParams p) {
   extern __shared__ __align__(1024) unsigned char smem[];
   float* stage = reinterpret_cast<float*>(smem + kOffStage);
   float* red = reinterpret_cast<float*>(smem + kOffRed);
@@ -136,182 +142,206 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const GdnParams
   const int units = p.batch * kHk;
   if (static_cast<int>(blockIdx.x) >= units) return;
   const int my_units = (units - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1;
-  const int my_tiles = 2 * my_units;
+  const int my_halves = 4 * my_units;  // 2 tiles x 2 halves per unit
 
-  auto tile_unit = [&](int n) { return static_cast<int>(blockIdx.x) + (n >> 1) * static_cast<int>(gridDim.x); };
+  auto unit_of = [&](int ui) { return static_cast<int>(blockIdx.x) + ui * static_cast<int>(gridDim.x); };
   // Out-of-range slots read slot 0 (always mapped) and skip every write; the
   // error word records the bad entry.
+  auto raw_slot = [&](int b) { return p.slots ? p.slots[b] : b; };
   auto slot_of = [&](int b) {
-    const int s = p.slots ? p.slots[b] : b;
+    const int s = raw_slot(b);
     return (s >= 0 && s < p.num_slots) ? s : 0;
   };
-  auto slot_ok = [&](int b) {
-    const int s = p.slots ? p.slots[b] : b;
-    return s >= 0 && s < p.num_slots;
-  };
 
-  // Producer: lanes 0..7 of warp 0 each issue one 8 KiB slice of the tile.
-  auto issue = [&](int n) {
-    const int u = tile_unit(n);
+  // Producer (warp 0): half tile jh -> ring slot jh % kSlots.
+  auto issue = [&](int jh) {
+    const int u = unit_of(jh >> 2);
     const int b = u / kHk;
-    const int h = 2 * (u % kHk) + (n & 1);
-    const int s = n % kStages;
-    const float* src = p.rec_state + (static_cast<int64_t>(slot_of(b)) * kHv + h) * kTileFloats;
-    if (lane == 0) mbar_arrive_expect_tx(&full[s], kTileBytes);
+    const int h = 2 * (u % kHk) + ((jh >> 1) & 1);
+    const int s = jh % kSlots;
+    const float* src = p.rec_state + (static_cast<int64_t>(slot_of(b)) * kHv + h) * kTileFloats + (jh & 1) * kHalfFloats;
+    if (lane == 0) mbar_arrive_expect_tx(&full[s], kHalfBytes);
     __syncwarp();
     if (lane < kCopyChunks) {
-      constexpr int chunk_floats = kTileFloats / kCopyChunks;
-      bulk_g2s(stage + s * kTileFloats + lane * chunk_floats, src + lane * chunk_floats, kTileBytes / kCopyChunks,
-               &full[s]);
+      constexpr int chunk = kHalfFloats / kCopyChunks;
+      bulk_g2s(stage + s * kHalfFloats + lane * chunk, src + lane * chunk, kHalfBytes / kCopyChunks, &full[s]);
+    }
+  };
+
+  // Channels owned by this thread inside a unit: one of q/k, one of v.
+  auto load_prefetch = [&](int ui, Prefetch& pf) {
+    const int u = unit_of(ui);
+    const int b = u / kHk;
+    const int j = u % kHk;
+    const int slot = slot_of(b);
+    const int ch_qk = (tid < 128) ? (j * kD + tid) : (kKeyDim + j * kD + (tid - 128));
+    const int ch_v = 2 * kKeyDim + j * 2 * kD + tid;
+    const __nv_bfloat16* cs = p.conv_state + static_cast<int64_t>(slot) * kConvDim * 4;
+    pf.st_qk = *reinterpret_cast<const uint2*>(cs + ch_qk * 4);
+    pf.st_v = *reinterpret_cast<const uint2*>(cs + ch_v * 4);
+    pf.w_qk = *reinterpret_cast<const uint2*>(p.conv_w + ch_qk * 4);
+    pf.w_v = *reinterpret_cast<const uint2*>(p.conv_w + ch_v * 4);
+    const __nv_bfloat16* mrow = p.mixed + static_cast<int64_t>(b) * p.mixed_stride;
+    pf.x_qk = mrow[ch_qk];
+    pf.x_v = mrow[ch_v];
+    if (tid < 128) {
+      const __nv_bfloat16* zrow = p.z + static_cast<int64_t>(b) * p.z_stride + 2 * j * kD + tid;
+      pf.z0 = zrow[0];
+      pf.z1 = zrow[kD];
+    }
+    if (tid < 2) {
+      const int hh = 2 * j + tid;
+      pf.bb = p.bgate[static_cast<int64_t>(b) * p.b_stride + hh];
+      pf.aa = p.agate[static_cast<int64_t>(b) * p.a_stride + hh];
+      pf.a_log = p.a_log[hh];
+      pf.dt_bias = p.dt_bias[hh];
     }
   };
 
   if (tid == 0) {
-    for (int s = 0; s < kStages; ++s) mbar_init(&full[s], 1);
+    for (int s = 0; s < kSlots; ++s) mbar_init(&full[s], 1);
     mbar_fence_init();
   }
   __syncthreads();
   if (warp == 0) {
-    for (int n = 0; n < kStages && n < my_tiles; ++n) issue(n);
+    for (int jh = 0; jh < kSlots && jh < my_halves; ++jh) issue(jh);
   }
 
-  const int row0 = warp * 16;  // rows of S owned by this warp (k index)
-  float kq = 0.f;
+  Prefetch pf;
+  load_prefetch(0, pf);
 
-  for (int n = 0; n < my_tiles; ++n) {
-    const int u = tile_unit(n);
+  const int half = warp >> 2;       // which half tile this warp reads
+  const int lrow0 = (warp & 3) * 16;  // first row inside the half
+  const int row0 = half * 64 + lrow0;  // first row of the tile (k index)
+
+  for (int ui = 0; ui < my_units; ++ui) {
+    const int u = unit_of(ui);
     const int b = u / kHk;
     const int j = u % kHk;
-    const int hp = n & 1;  // 0: head 2j, 1: head 2j+1
-    const int h = 2 * j + hp;
     const int slot = slot_of(b);
-    const bool wr = slot_ok(b);
-    if (!wr && hp == 0 && tid == 0) ria_set_error(p.err, RIA_DEVERR_BAD_SLOT);
+    const int rs = raw_slot(b);
+    const bool wr = rs >= 0 && rs < p.num_slots;
 
-    if (hp == 0) {
-      // ---- per-unit prologue: conv + SiLU for 128 q, 128 k and 256 v channels,
-      // L2 norms, gates for both value heads.
+    // ---- unit prologue from the prefetched registers
+    __syncthreads();  // previous unit's readers of qs/ks/vs/scal are done
+    {
+      __nv_bfloat16* cs = p.conv_state + static_cast<int64_t>(slot) * kConvDim * 4;
       const int ch_qk = (tid < 128) ? (j * kD + tid) : (kKeyDim + j * kD + (tid - 128));
-      const float yqk = conv_channel(p, b, slot, wr, ch_qk);
-      const float yv = conv_channel(p, b, slot, wr, 2 * kKeyDim + j * 2 * kD + tid);
+      const int ch_v = 2 * kKeyDim + j * 2 * kD + tid;
+      const float yqk = conv_silu(pf.st_qk, pf.w_qk, pf.x_qk, cs + ch_qk * 4, wr);
+      const float yv = conv_silu(pf.st_v, pf.w_v, pf.x_v, cs + ch_v * 4, wr);
       vs[tid] = yv;
       if (tid < 128) qs[tid] = yqk; else ks[tid - 128] = yqk;
       if (tid < 2) {
-        const int hh = 2 * j + tid;
-        const float bb = __bfloat162float(p.bgate[static_cast<int64_t>(b) * p.b_stride + hh]);
-        const float aa = __bfloat162float(p.agate[static_cast<int64_t>(b) * p.a_stride + hh]);
-        const float beta = 1.0f / (1.0f + expf(-bb));
-        const float g = -expf(p.a_log[hh]) * softplus_torch(aa + p.dt_bias[hh]);
-        scal[kSBeta + tid] = beta;
-        scal[kSDecay + tid] = expf(g);
+        const float bb = __bfloat162float(pf.bb);
+        const float aa = __bfloat162float(pf.aa);
+        scal[tid] = 1.0f / (1.0f + expf(-bb));
+        scal[2 + tid] = expf(-expf(pf.a_log) * softplus_torch(aa + pf.dt_bias));
       }
-      __syncthreads();
-      if (tid < 128) {
-        const float qv = qs[tid], kv = ks[tid];
-        float sq = warp_sum(qv * qv), sk = warp_sum(kv * kv), sqk = warp_sum(qv * kv);
-        if (lane == 0) {
-          wred[warp * 4 + 0] = sq;
-          wred[warp * 4 + 1] = sk;
-          wred[warp * 4 + 2] = sqk;
-        }
-      }
-      __syncthreads();
-      {
-        float sq = 0.f, sk = 0.f, sqk = 0.f;
-#pragma unroll
-        for (int w = 0; w < 4; ++w) {
-          sq += wred[w * 4 + 0];
-          sk += wred[w * 4 + 1];
-          sqk += wred[w * 4 + 2];
-        }
-        const float rq = rsqrtf(sq + 1e-6f);
-        const float rk = rsqrtf(sk + 1e-6f);
-        const float qscale = 0.08838834764831845f;  // 128 ** -0.5
-        kq = sqk * rq * rk * qscale;
-        __syncthreads();  // everyone has read qs/ks raw values
-        if (tid < 128) {
-          qs[tid] = qs[tid] * rq * qscale;
-          ks[tid] = ks[tid] * rk;
-        }
-      }
-      __syncthreads();
+      if (!wr && tid == 0) ria_set_error(p.err, RIA_DEVERR_BAD_SLOT);
     }
-
-    // ---- wait for this tile
-    const int s = n % kStages;
-    mbar_wait_bounded(&full[s], (n / kStages) & 1, p.err, RIA_DEVERR_MBAR_TIMEOUT_GDN);
-    const float* tile = stage + s * kTileFloats;
-    const float decay = scal[kSDecay + hp];
-    const float beta = scal[kSBeta + hp];
-
-    // ---- phase 1: partial S^T k and S^T q over this warp's 16 rows
-    float4 racc = make_float4(0.f, 0.f, 0.f, 0.f);
-    float4 oacc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-    for (int r = 0; r < 16; ++r) {
-      const int row = row0 + r;
-      const float4 sv = reinterpret_cast<const float4*>(tile + row * kD)[lane];
-      const float kk = ks[row];
-      const float qq = qs[row];
-      racc.x = fmaf(sv.x, kk, racc.x);
-      racc.y = fmaf(sv.y, kk, racc.y);
-      racc.z = fmaf(sv.z, kk, racc.z);
-      racc.w = fmaf(sv.w, kk, racc.w);
-      oacc.x = fmaf(sv.x, qq, oacc.x);
-      oacc.y = fmaf(sv.y, qq, oacc.y);
-      oacc.z = fmaf(sv.z, qq, oacc.z);
-      oacc.w = fmaf(sv.w, qq, oacc.w);
-    }
-    reinterpret_cast<float4*>(red + (warp * 2 + 0) * kD)[lane] = racc;
-    reinterpret_cast<float4*>(red + (warp * 2 + 1) * kD)[lane] = oacc;
+    const float z0 = (tid < 128) ? __bfloat162float(pf.z0) : 0.f;
+    const float z1 = (tid < 128) ? __bfloat162float(pf.z1) : 0.f;
+    if (ui + 1 < my_units) load_prefetch(ui + 1, pf);  // in flight during this unit
     __syncthreads();
-
-    // ---- reduce over the 8 warps: delta and the head output
-    float o = 0.f;
-    if (tid < kD) {
-      float rr = 0.f, oo = 0.f;
-#pragma unroll
-      for (int w = 0; w < 8; ++w) {
-        rr += red[(w * 2 + 0) * kD + tid];
-        oo += red[(w * 2 + 1) * kD + tid];
+    if (tid < 128) {
+      const float qv = qs[tid], kv = ks[tid];
+      const float sq = warp_sum(qv * qv), sk = warp_sum(kv * kv), sqk = warp_sum(qv * kv);
+      if (lane == 0) {
+        wred[warp * 4 + 0] = sq;
+        wred[warp * 4 + 1] = sk;
+        wred[warp * 4 + 2] = sqk;
       }
-      const float delta = beta * (vs[hp * kD + tid] - decay * rr);
-      o = fmaf(decay, oo, delta * kq);
-      ds[tid] = delta;
-      const float so = warp_sum(o * o);
-      if (lane == 0) wred[16 + warp] = so;
-    }
-    __syncthreads();
-
-    // ---- epilogue: gated RMSNorm -> bf16 output row
-    if (tid < kD) {
-      const float ss = wred[16] + wred[17] + wred[18] + wred[19];
-      const float on = o * rsqrtf(ss * (1.0f / kD) + 1e-6f);
-      const float zz = __bfloat162float(p.z[static_cast<int64_t>(b) * p.z_stride + h * kD + tid]);
-      const float gate = zz / (1.0f + expf(-zz));
-      if (wr)
-        p.out[static_cast<int64_t>(b) * p.out_stride + h * kD + tid] = __float2bfloat16_rn(p.norm_w[tid] * on * gate);
     }
 
-    // ---- phase 2: S' = decay*S + k d^T, streamed back to HBM
-    {
-      float* dst = p.rec_state + (static_cast<int64_t>(slot) * kHv + h) * kTileFloats;
-      const float4 d4 = reinterpret_cast<const float4*>(ds)[lane];
+    for (int t = 0; t < 2; ++t) {
+      const int n = 2 * ui + t;
+      const int h = 2 * j + t;
+      const int jh = 2 * n + half;
+      const int s = jh % kSlots;
+      mbar_wait_bounded(&full[s], (jh / kSlots) & 1, p.err, RIA_DEVERR_MBAR_TIMEOUT_GDN);
+      const float* hs = stage + s * kHalfFloats;
+
+      // ---- phase 1: this warp's 16 rows into registers; partial S^T k, S^T q
+      float4 sreg[16];
+      float4 racc = make_float4(0.f, 0.f, 0.f, 0.f);
+      float4 oacc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
       for (int r = 0; r < 16; ++r) {
-        const int row = row0 + r;
-        const float4 sv = reinterpret_cast<const float4*>(tile + row * kD)[lane];
-        const float kk = ks[row];
-        float4 nv;
-        nv.x = fmaf(decay, sv.x, kk * d4.x);
-        nv.y = fmaf(decay, sv.y, kk * d4.y);
-        nv.z = fmaf(decay, sv.z, kk * d4.z);
-        nv.w = fmaf(decay, sv.w, kk * d4.w);
-        if (wr) reinterpret_cast<float4*>(dst + row * kD)[lane] = nv;
+        sreg[r] = reinterpret_cast<const float4*>(hs + (lrow0 + r) * kD)[lane];
+        const float kk = ks[row0 + r];
+        const float qq = qs[row0 + r];
+        racc.x = fmaf(sreg[r].x, kk, racc.x);
+        racc.y = fmaf(sreg[r].y, kk, racc.y);
+        racc.z = fmaf(sreg[r].z, kk, racc.z);
+        racc.w = fmaf(sreg[r].w, kk, racc.w);
+        oacc.x = fmaf(sreg[r].x, qq, oacc.x);
+        oacc.y = fmaf(sreg[r].y, qq, oacc.y);
+        oacc.z = fmaf(sreg[r].z, qq, oacc.z);
+        oacc.w = fmaf(sreg[r].w, qq, oacc.w);
+      }
+      reinterpret_cast<float4*>(red + (warp * 2 + 0) * kD)[lane] = racc;
+      reinterpret_cast<float4*>(red + (warp * 2 + 1) * kD)[lane] = oacc;
+      __syncthreads();  // A: both halves of tile n are in registers
+      if (warp == 0) {
+        if (2 * n + kSlots < my_halves) issue(2 * n + kSlots);
+        if (2 * n + 1 + kSlots < my_halves) issue(2 * n + 1 + kSlots);
+      }
+
+      // L2-norm scales from the prologue sums (every thread needs rk)
+      float sq = 0.f, sk = 0.f, sqk = 0.f;
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        sq += wred[w * 4 + 0];
+        sk += wred[w * 4 + 1];
+        sqk += wred[w * 4 + 2];
+      }
+      const float qscale = 0.08838834764831845f;  // 128 ** -0.5
+      const float rq = rsqrtf(sq + 1e-6f) * qscale;
+      const float rk = rsqrtf(sk + 1e-6f);
+      const float decay = scal[2 + t];
+
+      // ---- reduce over the 8 warps: delta and the head output
+      float o = 0.f;
+      if (tid < kD) {
+        float rr = 0.f, oo = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+          rr += red[(w * 2 + 0) * kD + tid];
+          oo += red[(w * 2 + 1) * kD + tid];
+        }
+        const float delta = scal[t] * (vs[t * kD + tid] - decay * (rr * rk));
+        o = fmaf(decay, oo * rq, delta * (sqk * rq * rk));
+        ds[tid] = delta;
+        const float so = warp_sum(o * o);
+        if (lane == 0) wred[16 + warp] = so;
+      }
+      __syncthreads();  // B
+
+      // ---- phase 2: S' = decay*S + k d^T from registers to HBM
+      {
+        float* dst = p.rec_state + (static_cast<int64_t>(slot) * kHv + h) * kTileFloats;
+        const float4 d4 = reinterpret_cast<const float4*>(ds)[lane];
+#pragma unroll
+        for (int r = 0; r < 16; ++r) {
+          const float kk = ks[row0 + r] * rk;
+          float4 nv;
+          nv.x = fmaf(decay, sreg[r].x, kk * d4.x);
+          nv.y = fmaf(decay, sreg[r].y, kk * d4.y);
+          nv.z = fmaf(decay, sreg[r].z, kk * d4.z);
+          nv.w = fmaf(decay, sreg[r].w, kk * d4.w);
+          if (wr) reinterpret_cast<float4*>(dst + (row0 + r) * kD)[lane] = nv;
+        }
+      }
+      // ---- epilogue: gated RMSNorm -> bf16 output row
+      if (tid < kD && wr) {
+        const float ss = wred[16] + wred[17] + wred[18] + wred[19];
+        const float on = o * rsqrtf(ss * (1.0f / kD) + 1e-6f);
+        const float zz = t ? z1 : z0;
+        const float gate = zz / (1.0f + expf(-zz));
+        p.out[static_cast<int64_t>(b) * p.out_stride + h * kD + tid] = __float2bfloat16_rn(p.norm_w[tid] * on * gate);
       }
     }
-    __syncthreads();  // stage s, ds and wred are free again
-    if (warp == 0 && n + kStages < my_tiles) issue(n + kStages);
   }
 }
 
@@ -360,15 +390,22 @@ extern "C" int ria_gdn_decode_step(const void* mixed, int64_t mixed_stride, cons
   p.num_slots = num_slots;
   p.err = ria::device_error_word();
 
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(gdn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    if (e != cudaSuccess)
-      return ria::fail(RIA_ERR_CUDA, "ria_gdn_decode_step: smem attribute: %s", cudaGetErrorString(e));
-    attr_set = true;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static std::mutex mu;
+  static bool attr_set[64] = {false};
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+      cudaError_t e =
+          cudaFuncSetAttribute(gdn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+      if (e != cudaSuccess)
+        return ria::fail(RIA_ERR_CUDA, "ria_gdn_decode_step: smem attribute: %s", cudaGetErrorString(e));
+      attr_set[dev] = true;
+    }
   }
   const int units = batch * kHk;
-  const int grid = std::min(units, ria::num_sms());
+  const int grid = std::min(units, 2 * ria::num_sms());
   gdn_decode_kernel<<<grid, kThreads, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(p);
   return ria::check_launch("ria_gdn_decode_step");
 }
