@@ -146,6 +146,15 @@ RIA_API int ria_gqa_decode_paged_static(const void* q, int64_t q_stride, const v
  * grid holds a few waves of CTAs for `total_blocks` blocks of work. */
 RIA_API int32_t ria_gqa_decode_split_pages(int64_t total_blocks, int32_t num_kv_heads);
 
+/* Diagnostic (no counterpart in the reference): one CTA computes
+ * d[128 x n] = a[128 x k] * b[k x n] (row-major fp32 in/out, bf16 operands)
+ * with tcgen05 MMAs whose A / B operands are staged K-major (0) or MN-major (1)
+ * in 128-byte-swizzled shared memory -- the operand layouts the prefill
+ * kernels use.  n, k in {64, 128}.  Used by the tests to pin the descriptor
+ * encodings against a reference matmul. */
+RIA_API int ria_umma_selftest(int32_t a_mn_major, int32_t b_mn_major, int32_t n, int32_t k, const float* a,
+                              const float* b, float* d, ria_stream_t stream);
+
 /* ------------------------------------------------------------------------
  * Small fused row kernels used around the projections.
  */

@@ -66,6 +66,7 @@ _SIGNATURES: dict[str, tuple[object, list]] = {
          c_int64, c_void_p, c_int32, c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_int64, c_int32, c_int32,
          c_int32, c_void_p],
     ),
+    "ria_umma_selftest": (c_int, [c_int32, c_int32, c_int32, c_int32, c_void_p, c_void_p, c_void_p, c_void_p]),
     "ria_advance_positions": (c_int, [c_void_p, c_void_p, c_int32, c_void_p]),
     "ria_rmsnorm_rows": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int32, c_int32, c_void_p]),
     "ria_residual_add": (
@@ -192,6 +193,21 @@ def gqa_decode_paged_static(q, k, v, q_norm_w, k_norm_w, inv_freq, k_pool, v_poo
             block_table.data_ptr(), block_table.stride(0), _ptr(seq_lens), _ptr(positions), int(seq_len0),
             int(position0), out.data_ptr(), out.stride(0), q.shape[0], int(split_pages), int(max_splits), _stream(q))
     _check(rc, "ria_gqa_decode_paged_static")
+
+
+def umma_selftest(a, b, a_mn_major: bool, b_mn_major: bool):
+    """d = a @ b through one tcgen05 MMA chain (a: [128, k], b: [k, n] fp32
+    CUDA tensors; operands rounded to bf16)."""
+    _require_cuda(a, b)
+    a = a.float().contiguous()
+    b = b.float().contiguous()
+    n, k = b.shape[1], a.shape[1]
+    d = torch.empty(128, n, dtype=torch.float32, device=a.device)
+    with _Hooked("umma_selftest"):
+        rc = lib().ria_umma_selftest(int(a_mn_major), int(b_mn_major), n, k, a.data_ptr(), b.data_ptr(),
+                                     d.data_ptr(), _stream(a))
+    _check(rc, "ria_umma_selftest")
+    return d
 
 
 def advance_positions(seq_lens, positions):

@@ -1,0 +1,26 @@
+"""tcgen05 operand layouts: every (A major, B major, N, K) combination the
+prefill kernels use, against a float64 matmul of the same bf16-rounded
+operands (fp32 accumulation: relative error ~1e-6)."""
+
+from __future__ import annotations
+
+import itertools
+
+import pytest
+import torch
+
+from ria_b200 import _ext
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("a_mn,b_mn,n,k", list(itertools.product([False, True], [False, True], [64, 128], [64, 128])))
+def test_umma_layouts(cuda_device, a_mn, b_mn, n, k):
+    g = torch.Generator().manual_seed(n * 7 + k + 100 * a_mn + 10 * b_mn)
+    a = torch.randn(128, k, generator=g)
+    b = torch.randn(k, n, generator=g)
+    d = _ext.umma_selftest(a.to(cuda_device), b.to(cuda_device), a_mn, b_mn).cpu()
+    ref = a.to(torch.bfloat16).double() @ b.to(torch.bfloat16).double()
+    err = (d.double() - ref).abs().max().item() / ref.abs().max().item()
+    assert err < 1e-5, err
+    assert _ext.device_error() == 0
