@@ -146,6 +146,30 @@ RIA_API int ria_gqa_decode_paged_static(const void* q, int64_t q_stride, const v
  * grid holds a few waves of CTAs for `total_blocks` blocks of work. */
 RIA_API int32_t ria_gqa_decode_split_pages(int64_t total_blocks, int32_t num_kv_heads);
 
+/* ------------------------------------------------------------------------
+ * K2: chunked Gated DeltaNet prefill (chunk 64, WY/UT form) on tcgen05.
+ *
+ * Replaces gated_delta_chunk_initial (qwen36_linear_attention_hf.py:91-100,
+ * transformers torch_chunk_gated_delta_rule with use_qk_l2norm_in_kernel) and
+ * the token-by-token recurrence it equals (qwen36_attention_cache.py:256-266)
+ * for a whole prompt: q and k are L2-normalised in-kernel, q scaled by
+ * 128^-0.5, value head h reads key head h / (num_v_heads / num_k_heads).
+ *
+ * q, k [B, T, num_k_heads, 128] bf16 (element strides *_stride_b / *_stride_t,
+ *      head dims contiguous, 16-byte aligned); v [B, T, num_v_heads, 128] bf16;
+ * g    [B, T, num_v_heads] f32 log decay (-exp(A_log) softplus(a + dt_bias));
+ * beta [B, T, num_v_heads] f32 (sigmoid(b)); both with strides gb_stride_*;
+ * initial_state [B, num_v_heads, 128 k, 128 v] f32 or NULL (zeros);
+ * final_state   same layout (may alias initial_state): the state after T tokens,
+ *      in the decode kernel's layout;
+ * out  [B, T, num_v_heads, 128] bf16 (o_stride_b / o_stride_t). */
+RIA_API int ria_gdn_chunk_prefill(const void* q, int64_t q_stride_b, int64_t q_stride_t, const void* k,
+                                  int64_t k_stride_b, int64_t k_stride_t, const void* v, int64_t v_stride_b,
+                                  int64_t v_stride_t, const float* g, const float* beta, int64_t gb_stride_b,
+                                  int64_t gb_stride_t, const float* initial_state, float* final_state, void* out,
+                                  int64_t o_stride_b, int64_t o_stride_t, int32_t batch, int32_t seq_len,
+                                  int32_t num_k_heads, int32_t num_v_heads, ria_stream_t stream);
+
 /* Diagnostic (no counterpart in the reference): one CTA computes
  * d[128 x n] = a[128 x k] * b[k x n] (row-major fp32 in/out, bf16 operands)
  * with tcgen05 MMAs whose A / B operands are staged K-major (0) or MN-major (1)

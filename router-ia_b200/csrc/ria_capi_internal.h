@@ -1,6 +1,7 @@
 // Host-side helpers shared by the C-ABI translation units.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -19,5 +20,9 @@ bool aligned(const void* p, size_t a);
 // Device address of the error word on the current device (nullptr if the
 // symbol lookup failed; kernels then skip error reporting).
 unsigned int* device_error_word();
+// Tiled bf16 tensor map with 128-byte swizzle (no multicast users): `rank`
+// dims (innermost first), byte strides of dims 1..rank-1, box extents.
+int encode_bf16_sw128_map(CUtensorMap* m, const void* base, int rank, const uint64_t* dims,
+                          const uint64_t* strides_bytes, const uint32_t* box);
 
 }  // namespace ria

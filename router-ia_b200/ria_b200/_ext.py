@@ -66,6 +66,12 @@ _SIGNATURES: dict[str, tuple[object, list]] = {
          c_int64, c_void_p, c_int32, c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_int64, c_int32, c_int32,
          c_int32, c_void_p],
     ),
+    "ria_gdn_chunk_prefill": (
+        c_int,
+        [c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_void_p, c_void_p,
+         c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int32, c_int32, c_int32, c_int32,
+         c_void_p],
+    ),
     "ria_umma_selftest": (c_int, [c_int32, c_int32, c_int32, c_int32, c_void_p, c_void_p, c_void_p, c_void_p]),
     "ria_advance_positions": (c_int, [c_void_p, c_void_p, c_int32, c_void_p]),
     "ria_rmsnorm_rows": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int32, c_int32, c_void_p]),
@@ -193,6 +199,29 @@ def gqa_decode_paged_static(q, k, v, q_norm_w, k_norm_w, inv_freq, k_pool, v_poo
             block_table.data_ptr(), block_table.stride(0), _ptr(seq_lens), _ptr(positions), int(seq_len0),
             int(position0), out.data_ptr(), out.stride(0), q.shape[0], int(split_pages), int(max_splits), _stream(q))
     _check(rc, "ria_gqa_decode_paged_static")
+
+
+def gdn_chunk_prefill(q, k, v, g, beta, initial_state, final_state, out):
+    """K2 (see ria_gdn_chunk_prefill).  q, k [B, T, Hk, 128] bf16; v, out
+    [B, T, Hv, 128] bf16; g, beta [B, T, Hv] f32; states [B, Hv, 128, 128] f32."""
+    _require_cuda(q, k, v, g, beta, final_state, out)
+    B, T, Hk, dk = q.shape
+    Hv = v.shape[2]
+    for t, name in ((q, "q"), (k, "k"), (v, "v"), (out, "out")):
+        if t.dtype != torch.bfloat16 or t.shape[-1] != 128 or t.stride(-1) != 1 or t.stride(-2) != 128:
+            raise ValueError(f"{name}: expected [B, T, H, 128] bf16 with contiguous heads")
+    if g.dtype != torch.float32 or beta.dtype != torch.float32 or g.stride() != beta.stride() or g.stride(-1) != 1:
+        raise ValueError("g and beta: [B, T, Hv] float32 with the same strides")
+    if final_state.dtype != torch.float32 or not final_state.is_contiguous():
+        raise ValueError("final_state: contiguous [B, Hv, 128, 128] float32")
+    if initial_state is not None and (initial_state.dtype != torch.float32 or not initial_state.is_contiguous()):
+        raise ValueError("initial_state: contiguous [B, Hv, 128, 128] float32")
+    with _Hooked("gdn_prefill"):
+        rc = lib().ria_gdn_chunk_prefill(
+            q.data_ptr(), q.stride(0), q.stride(1), k.data_ptr(), k.stride(0), k.stride(1), v.data_ptr(),
+            v.stride(0), v.stride(1), g.data_ptr(), beta.data_ptr(), g.stride(0), g.stride(1), _ptr(initial_state),
+            final_state.data_ptr(), out.data_ptr(), out.stride(0), out.stride(1), B, T, Hk, Hv, _stream(q))
+    _check(rc, "ria_gdn_chunk_prefill")
 
 
 def umma_selftest(a, b, a_mn_major: bool, b_mn_major: bool):

@@ -71,6 +71,38 @@ def gqa_case(batch: int, length: int, iters: int, device) -> dict:
             "split_pages": launch.split_pages, "max_splits": launch.max_splits}
 
 
+PREFILL_FLOP_PER_CHUNK_HEAD = 11_534_336  # 2C^2(3d+2d) + 6 C d^2, C=64, d=128
+
+
+def prefill_case(batch: int, seq: int, iters: int, device, hk: int = 16, hv: int = 32) -> dict:
+    """Benchmark configuration 2 shape by default: 8 x 8192 tokens, 16 key / 32
+    value heads, chunk 64, bf16 inputs, fp32 final state."""
+    import torch.nn.functional as F
+
+    from ria_b200.prefill import chunk_gated_delta_rule
+
+    g0 = torch.Generator(device=device)
+    g0.manual_seed(2)
+    q = torch.randn(batch, seq, hk, 128, device=device, generator=g0).to(torch.bfloat16)
+    k = torch.randn(batch, seq, hk, 128, device=device, generator=g0).to(torch.bfloat16)
+    v = torch.randn(batch, seq, hv, 128, device=device, generator=g0).to(torch.bfloat16)
+    a_log = torch.rand(hv, device=device, generator=g0) * 2.7
+    dt_bias = torch.rand(hv, device=device, generator=g0) * 2 - 1
+    g = (-torch.exp(a_log) * F.softplus(torch.randn(batch, seq, hv, device=device, generator=g0) + dt_bias)).float()
+    beta = torch.sigmoid(torch.randn(batch, seq, hv, device=device, generator=g0)).float()
+    out = torch.empty(batch, seq, hv, 128, dtype=torch.bfloat16, device=device)
+    fs = torch.empty(batch, hv, 128, 128, dtype=torch.float32, device=device)
+
+    def run():
+        chunk_gated_delta_rule(q, k, v, g, beta, None, fs, out)
+
+    ms = _time(run, iters, device)
+    chunks = batch * hv * ((seq + 63) // 64)
+    flops = chunks * PREFILL_FLOP_PER_CHUNK_HEAD
+    return {"kernel": "gdn_prefill", "batch": batch, "seq": seq, "ms": ms, "tokens_per_s": batch * seq / (ms * 1e-3),
+            "tflops": flops / (ms * 1e9)}
+
+
 def _time(fn, iters, device):
     for _ in range(3):
         fn()
@@ -86,7 +118,8 @@ def _time(fn, iters, device):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--kernel", choices=("gdn", "gqa", "all"), default="all")
+    ap.add_argument("--kernel", choices=("gdn", "gqa", "prefill", "all"), default="all")
+    ap.add_argument("--seq", type=int, default=8192)
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--len", type=int, default=4096)
     ap.add_argument("--iters", type=int, default=20)
@@ -98,6 +131,8 @@ def main():
     if args.kernel in ("gqa", "all"):
         print(gqa_case(args.batch if args.kernel == "gqa" else max(1, args.batch // 2), args.len, args.iters, dev),
               flush=True)
+    if args.kernel == "prefill":
+        print(prefill_case(args.batch, args.seq, args.iters, dev), flush=True)
     if _ext.device_error():
         raise SystemExit("device error word set")
 
