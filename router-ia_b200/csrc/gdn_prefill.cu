@@ -22,8 +22,9 @@
 //   * Warpgroup 1 (recurrence) owns the fp32 state S^T in TMEM:
 //     X = S^T W^T and O = S^T Qr^T, V'^T = U^T - X, O += V'^T P^T and
 //     S^T = e^gamma_C S^T + V's^T K, then the bf16 output.
-//   The two hand chunks over through a two-slot SMEM ring guarded by
-//   full/empty mbarriers.  Every product is an M = 128 UMMA
+//   The two hand chunks over through a two-slot SMEM ring: prep arrives on a
+//   "full" mbarrier when a slot is ready, and the recurrence refills a slot
+//   with the TMA of chunk c + 2 as soon as its MMAs have read it.  Every product is an M = 128 UMMA
 //   (tcgen05.mma cta_group::1, bf16 operands in 128-byte-swizzled SMEM, fp32
 //   accumulation in TMEM); all waits are bounded.
 #include "ria_capi_internal.h"
@@ -48,17 +49,18 @@ constexpr uint32_t kSlX = 0, kSlY = 2 * kBox, kSlV = 4 * kBox, kSlWT = 6 * kBox,
 constexpr uint32_t kSlScal = 9 * kBox;  // eC, colscale[64]
 constexpr uint32_t kSlotBytes = 9 * kBox + 1024;
 constexpr uint32_t kOffSlot0 = 0;
-constexpr uint32_t kOffAT = 2 * kSlotBytes;        // fp32 A [64][64], then TW | TU bf16
-constexpr uint32_t kOffTf = kOffAT + 2 * kBox;     // fp32 T [64][64]
-constexpr uint32_t kOffST = kOffTf + 2 * kBox;     // bf16 S^T [128][128] (two boxes); later VN | VNS
+constexpr int kLd = 65;                            // padded fp32 row of A and T (bank-conflict free)
+constexpr uint32_t kOffAT = 2 * kSlotBytes;        // fp32 A [64][kLd], then TW | TU bf16
+constexpr uint32_t kOffTf = kOffAT + 64 * kLd * 4; // fp32 T [64][kLd]
+constexpr uint32_t kOffST = kOffAT + 33 * 1024;    // bf16 S^T [128][128] (two boxes); later VN | VNS, O staging
 constexpr uint32_t kOffMisc = kOffST + 4 * kBox;
 constexpr uint32_t kOffGraw = kOffMisc;
 constexpr uint32_t kOffGam = kOffMisc + 256;  // gamma * log2(e)
 constexpr uint32_t kOffBet = kOffMisc + 512;
 constexpr uint32_t kOffSq = kOffMisc + 768;
 constexpr uint32_t kOffSk = kOffMisc + 1024;
-constexpr uint32_t kOffZ = kOffMisc + 1280;  // inversion scratch, 768 f32
-constexpr uint32_t kOffBar = kOffZ + 3072;   // tma[2] full[2] empty[2] mma_p mma_r
+constexpr uint32_t kOffZ = kOffMisc + 1280;  // inversion scratch, 4 warps x 16 x 17 f32
+constexpr uint32_t kOffBar = kOffZ + 4 * 16 * 17 * 4;   // tma[2] full[2] (unused x2) mma_p mma_r
 constexpr uint32_t kOffTslot = kOffBar + 64;
 constexpr uint32_t kSmemBytes = kOffTslot + 16;
 
@@ -145,10 +147,50 @@ __device__ __forceinline__ void scale_row_bf16(unsigned char* box, int r, float 
   }
 }
 
-// T = (I + A)^-1 for strictly-lower A (fp32 [64][64]) by the 128 prep
-// threads: 16x16 diagonal blocks by substitution, off-diagonal blocks by
-// T_ij = -T_ii sum_m A_im T_mj in order of distance from the diagonal.
-__device__ void invert_unit_lower64(const float* A, float* T, float* Z, int tid) {
+// D (+)= A(16x8 tf32, row) * B(8x8 tf32, col), fp32 accumulate.
+__device__ __forceinline__ void mma_tf32_1688(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                              uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t to_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+
+// d[2][4] += X[16x16] * Y[16x16] for one warp; X, Y fp32 in SMEM with row
+// strides ldx, ldy.  C layout: d[nt][0..3] = rows g, g, g+8, g+8 and columns
+// 8nt + 2tig, +1, 2tig, +1.
+__device__ __forceinline__ void warp_mma16(float (&d)[2][4], const float* X, int ldx, const float* Y, int ldy,
+                                           int lane) {
+  const int g = lane >> 2, tg = lane & 3;
+#pragma unroll
+  for (int kk = 0; kk < 16; kk += 8) {
+    const uint32_t a0 = to_tf32(X[g * ldx + kk + tg]);
+    const uint32_t a1 = to_tf32(X[(g + 8) * ldx + kk + tg]);
+    const uint32_t a2 = to_tf32(X[g * ldx + kk + tg + 4]);
+    const uint32_t a3 = to_tf32(X[(g + 8) * ldx + kk + tg + 4]);
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      const uint32_t b0 = to_tf32(Y[(kk + tg) * ldy + 8 * nt + g]);
+      const uint32_t b1 = to_tf32(Y[(kk + tg + 4) * ldy + 8 * nt + g]);
+      mma_tf32_1688(d[nt], a0, a1, a2, a3, b0, b1);
+    }
+  }
+}
+
+// T = (I + A)^-1 for strictly-lower A (fp32 [64][kLd]) by the 128 prep
+// threads.  The four 16x16 diagonal blocks are inverted by substitution
+// (threads 0-63, one column each; threads 64-127 meanwhile scale Q rows and
+// clear the upper blocks).  Off-diagonal blocks follow in order of distance d
+// from the diagonal, one warp per block, on the tensor cores (tf32 in, fp32
+// accumulate): T_ij = -T_ii (sum_{m=j}^{i-1} A_im T_mj).
+template <class Side>
+__device__ void invert_unit_lower64(const float* A, float* T, float* Z, int tid, Side&& side_work) {
   if (tid < 64) {
     const int d = tid >> 4, jj = tid & 15, j = 16 * d + jj;
     float col[16];
@@ -157,45 +199,50 @@ __device__ void invert_unit_lower64(const float* A, float* T, float* Z, int tid)
       float acc = 0.f;
 #pragma unroll
       for (int m = 0; m < ii; ++m)
-        if (m >= jj) acc = fmaf(A[(16 * d + ii) * 64 + 16 * d + m], col[m], acc);
+        if (m >= jj) acc = fmaf(A[(16 * d + ii) * kLd + 16 * d + m], col[m], acc);
       col[ii] = (ii < jj) ? 0.f : (ii == jj ? 1.f : -acc);
     }
 #pragma unroll
-    for (int ii = 0; ii < 16; ++ii) T[(16 * d + ii) * 64 + j] = col[ii];
+    for (int ii = 0; ii < 16; ++ii) T[(16 * d + ii) * kLd + j] = col[ii];
   } else {
     for (int e = tid - 64; e < 6 * 256; e += 64) {
       const int blk = e >> 8;
       const int bi = blk < 3 ? 0 : (blk < 5 ? 1 : 2);
       const int bj = blk < 3 ? blk + 1 : (blk < 5 ? blk - 1 : 3);
-      T[(16 * bi + ((e >> 4) & 15)) * 64 + 16 * bj + (e & 15)] = 0.f;
+      T[(16 * bi + ((e >> 4) & 15)) * kLd + 16 * bj + (e & 15)] = 0.f;
     }
+    side_work(tid - 64);
   }
   named_bar_sync(kBarPrep, 128);
+  const int warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, tg = lane & 3;
+  float* zw = Z + warp * 16 * 17;  // warp-private 16x16 (row stride 17)
 #pragma unroll
   for (int dist = 1; dist < 4; ++dist) {
-    const int nb = 4 - dist;
-    for (int e = tid; e < nb * 256; e += 128) {
-      const int blk = e >> 8, r = (e >> 4) & 15, cc = e & 15;
-      const int bi = blk + dist, bj = blk;
-      float acc = 0.f;
+    if (warp < 4 - dist) {
+      const int bi = warp + dist, bj = warp;
+      float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      for (int mb = bj; mb < bi; ++mb)
+        warp_mma16(acc, A + (16 * bi) * kLd + 16 * mb, kLd, T + (16 * mb) * kLd + 16 * bj, kLd, lane);
 #pragma unroll
-      for (int mbo = 0; mbo < dist; ++mbo) {
-        const int mb = bj + mbo;
-#pragma unroll
-        for (int mm = 0; mm < 16; ++mm)
-          acc = fmaf(A[(16 * bi + r) * 64 + 16 * mb + mm], T[(16 * mb + mm) * 64 + 16 * bj + cc], acc);
+      for (int nt = 0; nt < 2; ++nt) {
+        zw[g * 17 + 8 * nt + 2 * tg] = acc[nt][0];
+        zw[g * 17 + 8 * nt + 2 * tg + 1] = acc[nt][1];
+        zw[(g + 8) * 17 + 8 * nt + 2 * tg] = acc[nt][2];
+        zw[(g + 8) * 17 + 8 * nt + 2 * tg + 1] = acc[nt][3];
       }
-      Z[e] = acc;
-    }
-    named_bar_sync(kBarPrep, 128);
-    for (int e = tid; e < nb * 256; e += 128) {
-      const int blk = e >> 8, r = (e >> 4) & 15, cc = e & 15;
-      const int bi = blk + dist, bj = blk;
-      float acc = 0.f;
+      __syncwarp();
+      float tt[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      warp_mma16(tt, T + (16 * bi) * kLd + 16 * bi, kLd, zw, 17, lane);
+      float* out = T + (16 * bi) * kLd + 16 * bj;
 #pragma unroll
-      for (int mm = 0; mm < 16; ++mm)
-        acc = fmaf(T[(16 * bi + r) * 64 + 16 * bi + mm], Z[(blk << 8) + (mm << 4) + cc], acc);
-      T[(16 * bi + r) * 64 + 16 * bj + cc] = -acc;
+      for (int nt = 0; nt < 2; ++nt) {
+        out[g * kLd + 8 * nt + 2 * tg] = -tt[nt][0];
+        out[g * kLd + 8 * nt + 2 * tg + 1] = -tt[nt][1];
+        out[(g + 8) * kLd + 8 * nt + 2 * tg] = -tt[nt][2];
+        out[(g + 8) * kLd + 8 * nt + 2 * tg + 1] = -tt[nt][3];
+      }
+      __syncwarp();
     }
     named_bar_sync(kBarPrep, 128);
   }
@@ -203,7 +250,8 @@ __device__ void invert_unit_lower64(const float* A, float* T, float* Z, int tid)
 
 __global__ void __launch_bounds__(kThreads, 1)
     gdn_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                       const __grid_constant__ CUtensorMap tmV, const PrefillParams p) {
+                       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
+                       const PrefillParams p) {
   extern __shared__ __align__(1024) unsigned char smem[];
   const int h = blockIdx.x;
   const int b = blockIdx.y;
@@ -214,7 +262,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lt = tid & 127;   // thread index inside the warpgroup == TMEM lane
   uint64_t* tma_bar = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* full_bar = tma_bar + 2;
-  uint64_t* empty_bar = tma_bar + 4;
   uint64_t* mma_p = tma_bar + 6;
   uint64_t* mma_r = tma_bar + 7;
   uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + kOffTslot);
@@ -225,10 +272,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tmap(&tmQ);
     prefetch_tmap(&tmK);
     prefetch_tmap(&tmV);
+    prefetch_tmap(&tmO);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tma_bar[i], 1);
       mbar_init(&full_bar[i], 128);
-      mbar_init(&empty_bar[i], 1);
     }
     mbar_init(mma_p, 1);
     mbar_init(mma_r, 1);
@@ -245,6 +292,26 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
   const uint32_t my_lane = tm + lane_base;
 
+  // TMA of chunk c's Q/K/V tiles into slot c & 1 (issued by one thread).
+  auto issue_chunk = [&](int c) {
+    const int s = c & 1;
+    unsigned char* slot = smem + kOffSlot0 + s * kSlotBytes;
+    mbar_arrive_expect_tx(&tma_bar[s], 6 * kBox);
+    tma_load_3d(slot + kSlX, &tmQ, hk * kDK, c * kC, b, &tma_bar[s]);
+    tma_load_3d(slot + kSlX + kBox, &tmK, hk * kDK, c * kC, b, &tma_bar[s]);
+    tma_load_3d(slot + kSlY, &tmQ, hk * kDK + 64, c * kC, b, &tma_bar[s]);
+    tma_load_3d(slot + kSlY + kBox, &tmK, hk * kDK + 64, c * kC, b, &tma_bar[s]);
+    tma_load_3d(slot + kSlV, &tmV, h * kDV, c * kC, b, &tma_bar[s]);
+    tma_load_3d(slot + kSlV + kBox, &tmV, h * kDV + 64, c * kC, b, &tma_bar[s]);
+  };
+  auto load_gates = [&](int c, float& gv, float& bv) {
+    const int t = c * kC + lt;
+    const bool ok = t < p.T;
+    const int64_t gi = static_cast<int64_t>(b) * p.gs_b + static_cast<int64_t>(t) * p.gs_t + h;
+    gv = ok ? p.g[gi] : 0.f;
+    bv = ok ? p.beta[gi] : 0.f;
+  };
+
   if (wg == 0) {
     // =================================================================== prep
     float* graw = reinterpret_cast<float*>(smem + kOffGraw);
@@ -253,43 +320,31 @@ __global__ void __launch_bounds__(kThreads, 1)
     float* sq = reinterpret_cast<float*>(smem + kOffSq);
     float* sk = reinterpret_cast<float*>(smem + kOffSk);
     uint32_t ph_p = 0;
+    if (lt == 0) {
+      issue_chunk(0);
+      if (nchunks > 1) issue_chunk(1);
+    }
+    float g_next = 0.f, b_next = 0.f;
+    if (lt < kC) load_gates(0, g_next, b_next);
     for (int c = 0; c < nchunks; ++c) {
       const int s = c & 1;
       unsigned char* slot = smem + kOffSlot0 + s * kSlotBytes;
       const uint32_t aslot = sbase + kOffSlot0 + s * kSlotBytes;
-      if (lt == 0) {
-        if (c >= 2) mbar_wait_bounded(&empty_bar[s], ((c - 2) >> 1) & 1, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
-        mbar_arrive_expect_tx(&tma_bar[s], 6 * kBox);
-        tma_load_3d(slot + kSlX, &tmQ, hk * kDK, c * kC, b, &tma_bar[s]);
-        tma_load_3d(slot + kSlX + kBox, &tmK, hk * kDK, c * kC, b, &tma_bar[s]);
-        tma_load_3d(slot + kSlY, &tmQ, hk * kDK + 64, c * kC, b, &tma_bar[s]);
-        tma_load_3d(slot + kSlY + kBox, &tmK, hk * kDK + 64, c * kC, b, &tma_bar[s]);
-        tma_load_3d(slot + kSlV, &tmV, h * kDV, c * kC, b, &tma_bar[s]);
-        tma_load_3d(slot + kSlV + kBox, &tmV, h * kDV + 64, c * kC, b, &tma_bar[s]);
-      }
+      float gscan = 0.f;
       if (lt < kC) {
-        const int t = c * kC + lt;
-        const bool ok = t < p.T;
-        const int64_t gi = static_cast<int64_t>(b) * p.gs_b + static_cast<int64_t>(t) * p.gs_t + h;
-        graw[lt] = ok ? p.g[gi] : 0.f;
-        bet[lt] = ok ? p.beta[gi] : 0.f;
+        // inclusive scan of the chunk's log decays inside each of the two warps
+        gscan = g_next;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const float up = __shfl_up_sync(0xffffffffu, gscan, o);
+          if ((lt & 31) >= o) gscan += up;
+        }
+        if (lt == 31) graw[0] = gscan;  // warp 0 total
+        bet[lt] = b_next;
+        if (c + 1 < nchunks) load_gates(c + 1, g_next, b_next);  // in flight during this chunk
       }
       mbar_wait_bounded(&tma_bar[s], (c >> 1) & 1, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
-      named_bar_sync(kBarPrep, 128);
-      if (lt < kC) {
-        float acc = 0.f;
-        for (int m = 0; m <= lt; ++m) acc += graw[m];
-        gam[lt] = acc * kLog2e;
-      }
-      {
-        const int r = lt & 63;
-        const uint32_t off = lt >= 64 ? kBox : 0;
-        const float rn = rsqrtf(sumsq_row(slot + kSlX + off, slot + kSlY + off, r) + 1e-6f);
-        if (lt < 64) sq[r] = rn; else sk[r] = rn;
-      }
-      named_bar_sync(kBarPrep, 128);
-
-      // ---- G = [Q;K] K^T
+      // ---- G = [Q;K] K^T (raw q, k) runs while the gates and norms are formed
       if (lt == 0) {
         tc::fence_after_sync();
         const uint32_t id = tc::idesc_bf16(128, 64, false, false);
@@ -299,6 +354,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc::commit(mma_p);
       }
+      named_bar_sync(kBarPrep, 128);
+      if (lt < kC) gam[lt] = (lt >= 32 ? gscan + graw[0] : gscan) * kLog2e;
+      {
+        const int r = lt & 63;
+        const uint32_t off = lt >= 64 ? kBox : 0;
+        const float rn = rsqrtf(sumsq_row(slot + kSlX + off, slot + kSlY + off, r) + 1e-6f);
+        if (lt < 64) sq[r] = rn; else sk[r] = rn;
+      }
+      named_bar_sync(kBarPrep, 128);
+
       mbar_wait_bounded(mma_p, ph_p, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
       ph_p ^= 1u;
       tc::fence_after_sync();
@@ -325,31 +390,31 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int j = 0; j < 64; ++j) {
             const float val = bi * v[j] * sk[j] * exp2f(gi - gam[j]);
-            A[i * 64 + j] = (j < i) ? val : 0.f;
+            A[i * kLd + j] = (j < i) ? val : 0.f;
           }
         }
       }
       tc::fence_before_sync();
       named_bar_sync(kBarPrep, 128);  // G consumed, A complete
-      {
-        // Qr = diag(e^gamma s_q 128^-0.5) Q, rows split over the two boxes
-        const int r = lt & 63;
-        const float sc = exp2f(gam[r]) * sq[r] * kQScale;
-        scale_row_bf16(slot + (lt < 64 ? kSlX : kSlY), r, sc);
-      }
+      // Qr = diag(e^gamma s_q 128^-0.5) Q (both 64-dim boxes of row r), done by
+      // the threads idle during the diagonal-block substitution
       invert_unit_lower64(reinterpret_cast<const float*>(smem + kOffAT), reinterpret_cast<float*>(smem + kOffTf),
-                          reinterpret_cast<float*>(smem + kOffZ), lt);
+                          reinterpret_cast<float*>(smem + kOffZ), lt, [&](int r) {
+                            const float sc = exp2f(gam[r]) * sq[r] * kQScale;
+                            scale_row_bf16(slot + kSlX, r, sc);
+                            scale_row_bf16(slot + kSlY, r, sc);
+                          });
       {
         const int i = lt & 63;
         const float* T = reinterpret_cast<const float*>(smem + kOffTf);
         float v[64];
         if (lt < 64) {
 #pragma unroll
-          for (int j = 0; j < 64; ++j) v[j] = T[i * 64 + j] * bet[j] * exp2f(gam[j]) * sk[j];
+          for (int j = 0; j < 64; ++j) v[j] = T[i * kLd + j] * bet[j] * exp2f(gam[j]) * sk[j];
           store_row_bf16<64>(smem + kOffAT, i, 0, v);  // TW
         } else {
 #pragma unroll
-          for (int j = 0; j < 64; ++j) v[j] = T[i * 64 + j] * bet[j];
+          for (int j = 0; j < 64; ++j) v[j] = T[i * kLd + j] * bet[j];
           store_row_bf16<64>(smem + kOffAT + kBox, i, 0, v);  // TU
         }
       }
@@ -418,6 +483,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait_bounded(&full_bar[s], (c >> 1) & 1, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
       tc::fence_after_sync();
       const float eC = scal[0];
+      // the previous chunk's output store must have read the staging tile
+      // (it shares SMEM with the bf16 state written next)
+      if (lt == 0) bulk_wait_read0();
+      named_bar_sync(kBarRec, 128);
 
       // ---- bf16(S_c) -> SMEM, S^T *= e^gamma_C in TMEM
       for (int k0 = 0; k0 < kDK; k0 += 32) {
@@ -486,28 +555,36 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait_bounded(mma_r, ph_r, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
       ph_r ^= 1u;
       tc::fence_after_sync();
-      if (lt == 0) mbar_arrive(&empty_bar[s]);  // the slot is consumed
+      // every read of this slot is complete: refill it with chunk c + 2
+      if (lt == 0 && c + 2 < nchunks) issue_chunk(c + 2);
 
-      // ---- output (lane = dv)
+      // ---- output: O^T (lane = dv) -> bf16 [64 tokens][128 dv] staging tile
+      // (two 64-dv boxes, 128-byte swizzled) -> one TMA tensor store per box;
+      // rows past the sequence end are clipped by the tensor map.
       {
-        const int t0 = c * kC;
-        __nv_bfloat16* orow = p.out + static_cast<int64_t>(b) * p.os_b + h * kDV + lt;
+        unsigned char* stg = smem + kOffST;
+        unsigned char* box = stg + (lt >> 6) * kBox;
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
           float o[32];
           tc::ld32(my_lane + kTmO + 32 * half, o);
           tc::wait_ld();
-#pragma unroll 8
-          for (int i = 0; i < 32; ++i) {
-            const int t = t0 + 32 * half + i;
-            if (t < p.T) orow[static_cast<int64_t>(t) * p.os_t] = __float2bfloat16_rn(o[i]);
-          }
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            *reinterpret_cast<__nv_bfloat16*>(box + tc::sw128_off(32 * half + i, lt & 63)) = __float2bfloat16_rn(o[i]);
+        }
+        fence_proxy_async_smem();
+        tc::fence_before_sync();
+        named_bar_sync(kBarRec, 128);  // O, X and the V' tiles are free; staging is written
+        tc::fence_after_sync();
+        if (lt == 0) {
+          tma_store_3d(&tmO, stg, h * kDV, c * kC, b);
+          tma_store_3d(&tmO, stg + kBox, h * kDV + 64, c * kC, b);
+          bulk_commit_group();
         }
       }
-      tc::fence_before_sync();
-      named_bar_sync(kBarRec, 128);  // O, X and the SMEM S^T / V' tiles are free again
-      tc::fence_after_sync();
     }
+    if (lt == 0) bulk_wait_all0();
     {
       float* sf = p.final_state + (static_cast<int64_t>(b) * p.Hv + h) * kDK * kDV;
       for (int k0 = 0; k0 < kDK; k0 += 32) {
@@ -568,6 +645,17 @@ extern "C" int ria_gdn_chunk_prefill(const void* q, int64_t q_stride_b, int64_t 
     if (rc) return rc;
   }
 
+  CUtensorMap tmO;
+  {
+    if (!ria::aligned(out, 16) || (o_stride_t % 8) || (o_stride_b % 8))
+      return ria::fail(RIA_ERR_INVALID, "ria_gdn_chunk_prefill: out must be 16-byte aligned with 16-byte strides");
+    const uint64_t dims[3] = {static_cast<uint64_t>(v_row), static_cast<uint64_t>(seq_len),
+                              static_cast<uint64_t>(batch)};
+    const uint64_t so[2] = {static_cast<uint64_t>(o_stride_t) * 2, static_cast<uint64_t>(o_stride_b) * 2};
+    int rc = ria::encode_bf16_sw128_map(&tmO, out, 3, dims, so, box);
+    if (rc) return rc;
+  }
+
   PrefillParams p;
   p.g = g;
   p.beta = beta;
@@ -586,6 +674,6 @@ extern "C" int ria_gdn_chunk_prefill(const void* q, int64_t q_stride_b, int64_t 
   cudaError_t e = cudaFuncSetAttribute(gdn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
   if (e != cudaSuccess) return ria::fail(RIA_ERR_CUDA, "ria_gdn_chunk_prefill: smem attribute: %s", cudaGetErrorString(e));
   gdn_prefill_kernel<<<dim3(num_v_heads, batch), kThreads, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(tmQ, tmK,
-                                                                                                          tmV, p);
+                                                                                                          tmV, tmO, p);
   return ria::check_launch("ria_gdn_chunk_prefill");
 }
