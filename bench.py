@@ -367,6 +367,70 @@ def config1_latency(device, iters=50):
             "kernel_gbs": kbytes / (kms * 1e6), "split_pages": launch.split_pages, "splits": launch.max_splits}
 
 
+PREFILL_FLOP_PER_CHUNK_HEAD = 11_534_336  # 2C^2(3d + 2d) + 6 C d^2 with C = 64, d = 128
+
+
+def config2_prefill(device, iters=5, warmup=3):
+    """Benchmark configuration 2: chunked Gated DeltaNet prefill, 8 sequences x
+    8192 tokens, 16 key / 32 value heads, chunk 64, bf16 inputs, fp32 final
+    state.  Tensor-bound: reported against the bf16 dense peak."""
+    import torch.nn.functional as F
+
+    from ria_b200 import _ext
+    from ria_b200.prefill import chunk_gated_delta_rule
+
+    B, T, Hk, Hv = 8, 8192, 16, 32
+    g0 = torch.Generator(device=device)
+    g0.manual_seed(2)
+    q = torch.randn(B, T, Hk, 128, device=device, generator=g0).to(torch.bfloat16)
+    k = torch.randn(B, T, Hk, 128, device=device, generator=g0).to(torch.bfloat16)
+    v = torch.randn(B, T, Hv, 128, device=device, generator=g0).to(torch.bfloat16)
+    a_log = torch.rand(Hv, device=device, generator=g0) * 2.7
+    dt_bias = torch.rand(Hv, device=device, generator=g0) * 2 - 1
+    g = (-torch.exp(a_log) * F.softplus(torch.randn(B, T, Hv, device=device, generator=g0) + dt_bias)).float()
+    beta = torch.sigmoid(torch.randn(B, T, Hv, device=device, generator=g0)).float()
+    out = torch.empty(B, T, Hv, 128, dtype=torch.bfloat16, device=device)
+    fs = torch.empty(B, Hv, 128, 128, dtype=torch.float32, device=device)
+    for _ in range(warmup):
+        chunk_gated_delta_rule(q, k, v, g, beta, None, fs, out)
+    hook = EventHook(timed=("gdn_prefill",))
+    _ext.launch_hook = hook
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(device)
+    s.record()
+    for _ in range(iters):
+        chunk_gated_delta_rule(q, k, v, g, beta, None, fs, out)
+    e.record()
+    torch.cuda.synchronize(device)
+    _ext.launch_hook = None
+    ms = s.elapsed_time(e) / iters
+    kms, _ = hook.mean_ms("gdn_prefill")
+    flops = B * Hv * ((T + 63) // 64) * PREFILL_FLOP_PER_CHUNK_HEAD
+    p = peaks()
+    cpu = None
+    if int(os.environ.get("WORLD_SIZE", "1")) == 1:
+        # the reference's chunked rule (oracle restatement of transformers'
+        # torch_chunk_gated_delta_rule) on the host cores, bounded sample
+        from oracle import attention_oracle as O
+
+        torch.set_num_threads(os.cpu_count() or 1)
+        Ts = 1024
+        qc, kc, vc = (x[:1, :Ts].float().cpu() for x in (q, k, v))
+        qc = qc.repeat_interleave(Hv // Hk, 2)
+        kc = kc.repeat_interleave(Hv // Hk, 2)
+        gc, bc = g[:1, :Ts].cpu(), beta[:1, :Ts].cpu()
+        t0 = time.perf_counter()
+        O.chunk_gated_delta_rule(qc, kc, vc, gc, bc)
+        dt = time.perf_counter() - t0
+        cpu = {"value": Ts / dt, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+               "sample": f"1 x {Ts} tokens x {Hv} heads through the chunked rule (fp32, chunk 64)"}
+    return {"workload": "config2: chunked DeltaNet prefill 8 x 8192, 32 heads, chunk 64", "tokens_per_s": B * T / (ms * 1e-3),
+            "cpu_baseline": cpu,
+            "ms": ms, "kernel_ms": kms, "flop": flops,
+            "roofline": {"bound": "tensor", "achieved": flops / (kms * 1e9), "peak": p["bf16_tflops"],
+                         "unit": "TFLOP/s", "frac": flops / (kms * 1e9) / p["bf16_tflops"], "peak_source": p["source"]}}
+
+
 # --------------------------------------------------------------------------- CPU reference (oracle port)
 def cpu_reference(args, steps, warmup, sample):
     """router-ia's layer algorithm on the host cores, one sequence at a time
@@ -463,6 +527,7 @@ def main():
         line = run_ours(args, rank, world, device)
         if rank == 0 and not args.no_extras:
             line["config1_gqa_b1_l4096"] = config1_latency(device)
+            line["config2_prefill"] = config2_prefill(device)
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_reference(args, steps=2, warmup=1, sample=args.cpu_sample)
         if rank == 0:

@@ -170,6 +170,30 @@ RIA_API int ria_gdn_chunk_prefill(const void* q, int64_t q_stride_b, int64_t q_s
                                   int64_t o_stride_b, int64_t o_stride_t, int32_t batch, int32_t seq_len,
                                   int32_t num_k_heads, int32_t num_v_heads, ria_stream_t stream);
 
+/* ------------------------------------------------------------------------
+ * K4: GQA prefill of T new tokens per sequence (batch B, same T).
+ *
+ * Replaces T token-by-token _full_stateful calls (qwen36_attention_cache.py:
+ * 285-324; prompt loop qwen36_chat_batch.py:255-258) for one layer: q/k RMSNorm
+ * (1+w), partial RoPE at positions[b] + t, the new K/V appended to the paged
+ * cache at index seq_lens[b] + t, causal softmax(q K^T / 16) V over the cached
+ * prefix and the new tokens, sigmoid gate.
+ *
+ * q [B, T, 16*512] bf16 (q | gate per head), k, v [B, T, 2*256] bf16, with
+ * element strides *_stride_b / *_stride_t (16-byte aligned); pools, block table
+ * as for ria_gqa_decode_paged (blocks for all T new tokens must be mapped);
+ * seq_lens [B] cached tokens before the prompt; positions [B] absolute
+ * position of prompt token 0; out [B, T, 4096] bf16; workspace at least
+ * ria_gqa_prefill_workspace_bytes(B, T) bytes (normalised q). */
+RIA_API int64_t ria_gqa_prefill_workspace_bytes(int32_t batch, int32_t seq_len);
+RIA_API int ria_gqa_prefill(const void* q, int64_t q_stride_b, int64_t q_stride_t, const void* k, int64_t k_stride_b,
+                            int64_t k_stride_t, const void* v, int64_t v_stride_b, int64_t v_stride_t,
+                            const float* q_norm_weight, const float* k_norm_weight, const float* inv_freq,
+                            void* k_pool, void* v_pool, int64_t pool_tokens, const int32_t* block_table,
+                            int32_t block_table_stride, const int32_t* seq_lens, const int32_t* positions, void* out,
+                            int64_t out_stride_b, int64_t out_stride_t, void* workspace, int64_t workspace_bytes,
+                            int32_t batch, int32_t seq_len, ria_stream_t stream);
+
 /* Diagnostic (no counterpart in the reference): one CTA computes
  * d[128 x n] = a[128 x k] * b[k x n] (row-major fp32 in/out, bf16 operands)
  * with tcgen05 MMAs whose A / B operands are staged K-major (0) or MN-major (1)

@@ -223,6 +223,33 @@ def gqa_kernel_ref(q_gate, k, v, w: dict, k_cache, v_cache, position: int):
     return out.reshape(HQ * D), kk, vv
 
 
+def gqa_prefill_ref(q_gate, k, v, w: dict, k_cache, v_cache, pos0: int):
+    """T prompt tokens of one sequence through the GQA boundary at once: the
+    result of T consecutive ``gqa_kernel_ref`` steps (token t at position
+    pos0 + t sees the cache and the new tokens 0..t).  q_gate (T, 16*512),
+    k, v (T, 512) bf16 values; caches (2, L0, 256).  Returns (out (T, 4096)
+    fp32, k_new (2, T, 256), v_new (2, T, 256))."""
+    T = q_gate.shape[0]
+    qg = q_gate.float().reshape(T, HQ, 2 * D)
+    q, gate = qg[..., :D], qg[..., D:]
+    q = rmsnorm(q, w["self_attn.q_norm.weight"].float())
+    kk = rmsnorm(k.float().reshape(T, HKV, D), w["self_attn.k_norm.weight"].float())
+    q = torch.stack([apply_rope(q[t], pos0 + t) for t in range(T)])
+    kk = torch.stack([apply_rope(kk[t], pos0 + t) for t in range(T)])
+    vv = v.float().reshape(T, HKV, D)
+    kc = torch.cat((k_cache.float(), kk.transpose(0, 1)), dim=1)  # (2, L0 + T, 256)
+    vc = torch.cat((v_cache.float(), vv.transpose(0, 1)), dim=1)
+    L0 = k_cache.shape[1]
+    k_exp = kc.repeat_interleave(GROUPS, dim=0)  # (16, L, 256)
+    v_exp = vc.repeat_interleave(GROUPS, dim=0)
+    scores = torch.einsum("thd,hld->thl", q, k_exp) * (D ** -0.5)
+    keypos = torch.arange(L0 + T)
+    allowed = keypos[None, :] <= (L0 + torch.arange(T))[:, None]  # (T, L)
+    scores = scores.masked_fill(~allowed[:, None, :], float("-inf"))
+    out = torch.einsum("thl,hld->thd", torch.softmax(scores, dim=-1), v_exp) * torch.sigmoid(gate)
+    return out.reshape(T, HQ * D), kk.transpose(0, 1), vv.transpose(0, 1)
+
+
 # --------------------------------------------------------------------------- gated delta rule (core)
 def recurrent_gated_delta_rule(q, k, v, g, beta, initial_state=None, dtype=torch.float32, l2=True):
     """Token-by-token rule. q, k (B, T, H, Dk); v (B, T, H, Dv); g, beta (B, T, H).

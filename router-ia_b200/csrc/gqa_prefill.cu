@@ -1,0 +1,482 @@
+// K4: GQA prefill -- a prompt of T tokens through one full-attention layer:
+// per-head q/k RMSNorm (1+w), partial RoPE, KV append into the paged cache,
+// causal attention over the cached prefix plus the new tokens, sigmoid gate.
+//
+// Reference semantics: router-ia runs a prompt token by token through
+// _full_stateful (qwen36_attention_cache.py:285-324); token t attends to every
+// cached token and to the new tokens 0..t (its own key included), with q/k
+// norms, RoPE at position tokens_seen, softmax(q K^T / 16) V and the gate
+// exactly as in the decode step.  This kernel computes all T tokens at once.
+//
+// B200 design
+//   * gqa_prefill_prep: one CTA per token; q/k RMSNorm + RoPE (in-kernel
+//     sincosf, host inverse frequencies), the normalised q (x 1/16) to a bf16
+//     workspace, K and V appended to the 64-token pages.
+//   * gqa_prefill_attn: one CTA per (128-token query tile, query head,
+//     sequence).  S = Q K^T (M = 128 tokens, N = 64 keys, K = 256) and
+//     O += P V (M = 128, N = 256, K = 64) are tcgen05 UMMAs with bf16 operands
+//     in 128-byte-swizzled SMEM (Q and the K/V pages by TMA, no multicast) and
+//     fp32 accumulators in TMEM.  The softmax runs on CUDA cores, one query
+//     row per thread (= TMEM lane); O is rescaled in TMEM only when a row's
+//     running maximum grows by more than 8 (log2 units), so most tiles touch
+//     only S.  K/V pages are double-buffered; the gated bf16 output leaves by
+//     TMA tensor store.
+#include <mutex>
+
+#include "ria_capi_internal.h"
+#include "ria_common.cuh"
+#include "tcgen05.cuh"
+
+namespace {
+
+constexpr int kHq = 16;
+constexpr int kHkv = 2;
+constexpr int kGroup = 8;
+constexpr int kD = 256;
+constexpr int kRope = 64;
+constexpr int kBlock = 64;
+constexpr int kTile = 128;  // query tokens per CTA
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kRescaleSlack = 8.0f;  // log2 units
+
+struct PrepParams {
+  const __nv_bfloat16* q;  // [B][T][16*512], per head: q 256 | gate 256
+  int64_t qs_b, qs_t;
+  const __nv_bfloat16* k;  // [B][T][2*256]
+  int64_t ks_b, ks_t;
+  const __nv_bfloat16* v;
+  int64_t vs_b, vs_t;
+  const float* q_norm_w;
+  const float* k_norm_w;
+  const float* inv_freq;
+  __nv_bfloat16* k_pool;
+  __nv_bfloat16* v_pool;
+  int64_t pool_tokens;
+  const int32_t* block_table;
+  int32_t bt_stride;
+  const int32_t* seq_lens;   // cached tokens before the prompt
+  const int32_t* positions;  // absolute position of prompt token 0
+  __nv_bfloat16* qbuf;       // [B][T][16][256]
+  int T;
+  int num_blocks;
+  unsigned int* err;
+};
+
+// RMSNorm (1+w) and partial RoPE of one 256-dim head row held as 8 values per
+// lane (lane l has dims 8l..8l+7); dims [0,64) rotate-half inside the slice.
+__device__ __forceinline__ void norm_rope_8(float (&x)[8], const float* w, const float* inv_freq, int pos, int lane) {
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) ss += x[i] * x[i];
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss * (1.0f / kD) + 1e-6f);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) x[i] = x[i] * r * (1.0f + w[lane * 8 + i]);
+  float partner[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float up = __shfl_down_sync(0xffffffffu, x[i], 4);
+    const float dn = __shfl_up_sync(0xffffffffu, x[i], 4);
+    partner[i] = (lane < 4) ? up : dn;
+  }
+  if (lane < 8) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int d = lane * 8 + i;
+      float sn, cs;
+      sincosf(static_cast<float>(pos) * inv_freq[d & 31], &sn, &cs);
+      x[i] = (d < 32) ? (x[i] * cs - partner[i] * sn) : (x[i] * cs + partner[i] * sn);
+    }
+  }
+}
+
+__device__ __forceinline__ void load8(const __nv_bfloat16* src, float (&x)[8]) {
+  const uint4 raw = *reinterpret_cast<const uint4*>(src);
+  const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(r2[i]);
+    x[2 * i] = f.x;
+    x[2 * i + 1] = f.y;
+  }
+}
+
+__device__ __forceinline__ uint4 pack8(const float (&x)[8], float s) {
+  uint4 u;
+  u.x = pack_bf16x2(x[0] * s, x[1] * s);
+  u.y = pack_bf16x2(x[2] * s, x[3] * s);
+  u.z = pack_bf16x2(x[4] * s, x[5] * s);
+  u.w = pack_bf16x2(x[6] * s, x[7] * s);
+  return u;
+}
+
+__global__ void __launch_bounds__(256) gqa_prefill_prep_kernel(const PrepParams p) {
+  const int t = blockIdx.x, b = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int L0 = p.seq_lens[b];
+  const int pos = p.positions[b] + t;
+  const int cidx = L0 + t;
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh) {
+    const int h = warp + 8 * hh;
+    float x[8];
+    load8(p.q + static_cast<int64_t>(b) * p.qs_b + static_cast<int64_t>(t) * p.qs_t + h * 2 * kD + lane * 8, x);
+    norm_rope_8(x, p.q_norm_w, p.inv_freq, pos, lane);
+    *reinterpret_cast<uint4*>(p.qbuf + ((static_cast<int64_t>(b) * p.T + t) * kHq + h) * kD + lane * 8) =
+        pack8(x, 0.0625f);
+  }
+  if (warp < 4) {
+    const int lp = cidx / kBlock;
+    const int phys = (lp < p.bt_stride) ? p.block_table[static_cast<int64_t>(b) * p.bt_stride + lp] : -1;
+    if (phys < 0 || phys >= p.num_blocks) {
+      if (lane == 0) ria_set_error(p.err, RIA_DEVERR_BAD_BLOCK);
+      return;
+    }
+    const int kvh = warp & 1;
+    const int64_t row = static_cast<int64_t>(kvh) * p.pool_tokens + static_cast<int64_t>(phys) * kBlock + (cidx % kBlock);
+    if (warp < 2) {
+      float x[8];
+      load8(p.k + static_cast<int64_t>(b) * p.ks_b + static_cast<int64_t>(t) * p.ks_t + kvh * kD + lane * 8, x);
+      norm_rope_8(x, p.k_norm_w, p.inv_freq, pos, lane);
+      *reinterpret_cast<uint4*>(p.k_pool + row * kD + lane * 8) = pack8(x, 1.0f);
+    } else {
+      *reinterpret_cast<uint4*>(p.v_pool + row * kD + lane * 8) = *reinterpret_cast<const uint4*>(
+          p.v + static_cast<int64_t>(b) * p.vs_b + static_cast<int64_t>(t) * p.vs_t + kvh * kD + lane * 8);
+    }
+  }
+}
+
+struct AttnParams {
+  const __nv_bfloat16* gate;  // q projection + 256: head h gate at [h*512, h*512+256)
+  int64_t gs_b, gs_t;
+  const int32_t* block_table;
+  int32_t bt_stride;
+  const int32_t* seq_lens;
+  int T;
+  int64_t pool_tokens;
+  int num_blocks;
+  unsigned int* err;
+};
+
+// SMEM map
+constexpr uint32_t kBox = 64 * 128;                // one [64 rows][64 bf16] box
+constexpr uint32_t kQBytes = 4 * 2 * kBox;         // Q: 4 boxes of [128 rows][128 B]
+constexpr uint32_t kKVBytes = 8 * kBox;            // K (4 boxes) + V (4 boxes), 64 keys
+constexpr uint32_t kOffQ = 0;
+constexpr uint32_t kOffKV = kQBytes;               // two buffers
+constexpr uint32_t kOffP = kOffKV + 2 * kKVBytes;  // P: [128 rows][64] bf16
+constexpr uint32_t kOffBar = kOffP + 2 * kBox;     // tma_q, tma_kv[2], bar_s, bar_pv
+constexpr uint32_t kOffTslot = kOffBar + 64;
+constexpr uint32_t kAttnSmem = kOffTslot + 16;
+constexpr uint32_t kTmS = 0, kTmO = 256;
+
+__global__ void __launch_bounds__(128, 1)
+    gqa_prefill_attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                            const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
+                            const AttnParams p) {
+  extern __shared__ __align__(1024) unsigned char smem[];
+  const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int kvh = h / kGroup;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int t0 = qt * kTile;
+  if (t0 >= p.T) return;
+  uint64_t* tma_q = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint64_t* tma_kv = tma_q + 1;
+  uint64_t* bar_s = tma_q + 3;
+  uint64_t* bar_pv = tma_q + 4;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + kOffTslot);
+  const uint32_t sbase = smem_u32(smem);
+  const int L0 = p.seq_lens[b];
+  const int last_q = min(t0 + kTile - 1, p.T - 1);
+  const int ntiles = (L0 + last_q) / kBlock + 1;
+  const int32_t* bt = p.block_table + static_cast<int64_t>(b) * p.bt_stride;
+
+  if (tid == 0) {
+    prefetch_tmap(&tmQ);
+    prefetch_tmap(&tmK);
+    prefetch_tmap(&tmV);
+    prefetch_tmap(&tmO);
+    for (int i = 0; i < 5; ++i) mbar_init(&tma_q[i], 1);
+    mbar_fence_init();
+  }
+  if (warp == 0) {
+    tc::tmem_alloc(tslot, 512);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tm = *tslot;
+  const uint32_t my_lane = tm + (static_cast<uint32_t>(warp * 32) << 16);
+
+  auto issue_kv = [&](int j) {
+    const int buf = j & 1;
+    const int lp = j;
+    int phys = (lp < p.bt_stride) ? bt[lp] : -1;
+    if (phys < 0 || phys >= p.num_blocks) {
+      ria_set_error(p.err, RIA_DEVERR_BAD_BLOCK);
+      phys = 0;
+    }
+    const int32_t row = static_cast<int32_t>(kvh * p.pool_tokens + static_cast<int64_t>(phys) * kBlock);
+    unsigned char* kv = smem + kOffKV + buf * kKVBytes;
+    mbar_arrive_expect_tx(&tma_kv[buf], kKVBytes);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      tma_load_2d(kv + i * kBox, &tmK, i * 64, row, &tma_kv[buf]);
+      tma_load_2d(kv + 4 * kBox + i * kBox, &tmV, i * 64, row, &tma_kv[buf]);
+    }
+  };
+  if (tid == 0) {
+    mbar_arrive_expect_tx(tma_q, kQBytes);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) tma_load_3d(smem + kOffQ + i * 2 * kBox, &tmQ, h * kD + i * 64, t0, b, tma_q);
+    issue_kv(0);
+  }
+
+  const int r = tid;  // query row = TMEM lane
+  const int qidx = L0 + t0 + r;  // cache index of this query token
+  const bool row_ok = (t0 + r) < p.T;
+  float m_used = -INFINITY, l = 0.f;
+  uint32_t ph_s = 0, ph_pv = 0;
+  mbar_wait_bounded(tma_q, 0, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
+
+  for (int j = 0; j < ntiles; ++j) {
+    const int buf = j & 1;
+    const uint32_t akv = sbase + kOffKV + buf * kKVBytes;
+    mbar_wait_bounded(&tma_kv[buf], (j >> 1) & 1, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
+    if (tid == 0) {
+      tc::fence_after_sync();
+      const uint32_t id = tc::idesc_bf16(128, 64, false, false);
+#pragma unroll
+      for (int ks = 0; ks < 16; ++ks) {
+        const uint32_t qa = sbase + kOffQ + (ks >> 2) * (2 * kBox) + (ks & 3) * 32;
+        const uint32_t kb = akv + (ks >> 2) * kBox + (ks & 3) * 32;
+        tc::mma_bf16(tm + kTmS, tc::sdesc_sw128(qa, 16, 1024), tc::sdesc_sw128(kb, 16, 1024), id, ks > 0);
+      }
+      tc::commit(bar_s);
+    }
+    mbar_wait_bounded(bar_s, ph_s, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
+    ph_s ^= 1u;
+    if (j > 0) {  // P V of the previous tile is done: O, P and its K/V buffer are free
+      mbar_wait_bounded(bar_pv, ph_pv, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
+      ph_pv ^= 1u;
+    }
+    tc::fence_after_sync();
+    if (tid == 0 && j + 1 < ntiles) issue_kv(j + 1);
+    // Page rows past the sequence end hold whatever the pool had: zero their V
+    // rows so that 0-probability keys cannot inject non-finite values into P V.
+    {
+      const int first_bad = L0 + p.T - j * kBlock;
+      if (first_bad < kBlock) {
+        unsigned char* vb = smem + kOffKV + buf * kKVBytes + 4 * kBox;
+        for (int idx = tid; idx < (kBlock - first_bad) * 32; idx += 128) {
+          const int row = first_bad + (idx >> 5), ch = idx & 31;
+          *reinterpret_cast<uint4*>(vb + (ch >> 3) * kBox + row * 128 + (ch & 7) * 16) = make_uint4(0, 0, 0, 0);
+        }
+      }
+    }
+
+    // ---- softmax of this row over 64 keys
+    float s[64];
+    tc::ld32(my_lane + kTmS, s);
+    tc::ld32(my_lane + kTmS + 32, s + 32);
+    tc::wait_ld();
+    float mx = -INFINITY;
+#pragma unroll
+    for (int c = 0; c < 64; ++c) {
+      const bool ok = row_ok && (j * kBlock + c) <= qidx;
+      s[c] = ok ? s[c] * kLog2e : -INFINITY;
+      mx = fmaxf(mx, s[c]);
+    }
+    if (mx > m_used + kRescaleSlack) {
+      const float f = (m_used == -INFINITY) ? 0.f : exp2f(m_used - mx);
+      if (j > 0 && m_used != -INFINITY) {
+        for (int c0 = 0; c0 < kD; c0 += 32) {
+          float o[32];
+          tc::ld32(my_lane + kTmO + c0, o);
+          tc::wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] *= f;
+          tc::st32(my_lane + kTmO + c0, o);
+        }
+        tc::wait_st();
+      }
+      l *= f;
+      m_used = mx;
+    }
+    const float mu = (m_used == -INFINITY) ? 0.f : m_used;
+    unsigned char* prow = smem + kOffP;
+#pragma unroll
+    for (int c = 0; c < 64; c += 8) {
+      float pv[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        pv[i] = exp2f(s[c + i] - mu);
+        l += pv[i];
+      }
+      uint4 u;
+      u.x = pack_bf16x2(pv[0], pv[1]);
+      u.y = pack_bf16x2(pv[2], pv[3]);
+      u.z = pack_bf16x2(pv[4], pv[5]);
+      u.w = pack_bf16x2(pv[6], pv[7]);
+      *reinterpret_cast<uint4*>(prow + tc::sw128_off(r, c)) = u;
+    }
+    fence_proxy_async_smem();
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    if (tid == 0) {
+      const uint32_t id = tc::idesc_bf16(128, 256, false, true);
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        tc::mma_bf16(tm + kTmO, tc::sdesc_sw128(sbase + kOffP + ks * 32, 16, 1024),
+                     tc::sdesc_sw128(akv + 4 * kBox + ks * 2048, kBox, 1024), id, j > 0 || ks > 0);
+      tc::commit(bar_pv);
+    }
+  }
+  mbar_wait_bounded(bar_pv, ph_pv, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
+  tc::fence_after_sync();
+
+  // ---- epilogue: O / l * sigmoid(gate) -> bf16 staging (reuses K/V buffer 0) -> TMA store
+  {
+    unsigned char* stg = smem + kOffKV;  // 4 boxes of [128 rows][128 B]
+    const float inv = (l > 0.f) ? 1.0f / l : 0.f;
+    const __nv_bfloat16* grow =
+        p.gate + static_cast<int64_t>(b) * p.gs_b + static_cast<int64_t>(row_ok ? t0 + r : t0) * p.gs_t + h * 2 * kD;
+    for (int c0 = 0; c0 < kD; c0 += 32) {
+      float o[32];
+      tc::ld32(my_lane + kTmO + c0, o);
+      tc::wait_ld();
+#pragma unroll
+      for (int i = 0; i < 32; i += 8) {
+        float gz[8];
+        load8(grow + c0 + i, gz);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[i + e] = o[i + e] * inv * (1.0f / (1.0f + expf(-gz[e])));
+        uint4 u;
+        u.x = pack_bf16x2(o[i], o[i + 1]);
+        u.y = pack_bf16x2(o[i + 2], o[i + 3]);
+        u.z = pack_bf16x2(o[i + 4], o[i + 5]);
+        u.w = pack_bf16x2(o[i + 6], o[i + 7]);
+        const int col = c0 + i;
+        *reinterpret_cast<uint4*>(stg + (col >> 6) * (2 * kBox) + tc::sw128_off(r, col & 63)) = u;
+      }
+    }
+    fence_proxy_async_smem();
+    tc::fence_before_sync();
+    __syncthreads();
+    if (tid == 0) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) tma_store_3d(&tmO, stg + i * 2 * kBox, h * kD + i * 64, t0, b);
+      bulk_commit_group();
+      bulk_wait_all0();
+    }
+  }
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tm, 512);
+}
+
+int pool_map(CUtensorMap* m, void* base, int64_t pool_tokens) {
+  const uint64_t dims[2] = {static_cast<uint64_t>(kD), static_cast<uint64_t>(kHkv * pool_tokens)};
+  const uint64_t strides[1] = {static_cast<uint64_t>(kD) * 2};
+  const uint32_t box[2] = {64, 64};
+  return ria::encode_bf16_sw128_map(m, base, 2, dims, strides, box);
+}
+
+}  // namespace
+
+extern "C" int64_t ria_gqa_prefill_workspace_bytes(int32_t batch, int32_t seq_len) {
+  if (batch <= 0 || seq_len <= 0) return 0;
+  return static_cast<int64_t>(batch) * seq_len * kHq * kD * 2;
+}
+
+extern "C" int ria_gqa_prefill(const void* q, int64_t q_stride_b, int64_t q_stride_t, const void* k, int64_t k_stride_b,
+                               int64_t k_stride_t, const void* v, int64_t v_stride_b, int64_t v_stride_t,
+                               const float* q_norm_weight, const float* k_norm_weight, const float* inv_freq,
+                               void* k_pool, void* v_pool, int64_t pool_tokens, const int32_t* block_table,
+                               int32_t block_table_stride, const int32_t* seq_lens, const int32_t* positions,
+                               void* out, int64_t out_stride_b, int64_t out_stride_t, void* workspace,
+                               int64_t workspace_bytes, int32_t batch, int32_t seq_len, ria_stream_t stream) {
+  if (batch < 0 || seq_len < 0) return ria::fail(RIA_ERR_INVALID, "ria_gqa_prefill: negative size");
+  if (batch == 0 || seq_len == 0) return RIA_OK;
+  if (!q || !k || !v || !q_norm_weight || !k_norm_weight || !inv_freq || !k_pool || !v_pool || !block_table ||
+      !seq_lens || !positions || !out || !workspace)
+    return ria::fail(RIA_ERR_INVALID, "ria_gqa_prefill: null pointer argument");
+  if (batch > 65535) return ria::fail(RIA_ERR_INVALID, "ria_gqa_prefill: batch too large");
+  if (pool_tokens <= 0 || pool_tokens % kBlock || kHkv * pool_tokens > INT32_MAX)
+    return ria::fail(RIA_ERR_INVALID, "ria_gqa_prefill: bad pool_tokens");
+  if (q_stride_t < kHq * 2 * kD || k_stride_t < kHkv * kD || v_stride_t < kHkv * kD || out_stride_t < kHq * kD)
+    return ria::fail(RIA_ERR_INVALID, "ria_gqa_prefill: token stride smaller than the row width");
+  if (!ria::aligned(q, 16) || !ria::aligned(k, 16) || !ria::aligned(v, 16) || !ria::aligned(out, 16) ||
+      !ria::aligned(k_pool, 16) || !ria::aligned(v_pool, 16) || !ria::aligned(workspace, 16) || (q_stride_t % 8) ||
+      (k_stride_t % 8) || (v_stride_t % 8) || (out_stride_t % 8) || (q_stride_b % 8) || (k_stride_b % 8) ||
+      (v_stride_b % 8) || (out_stride_b % 8))
+    return ria::fail(RIA_ERR_INVALID, "ria_gqa_prefill: tensors must be 16-byte aligned with 16-byte strides");
+  if (workspace_bytes < ria_gqa_prefill_workspace_bytes(batch, seq_len))
+    return ria::fail(RIA_ERR_INVALID, "ria_gqa_prefill: workspace needs %lld bytes",
+                     static_cast<long long>(ria_gqa_prefill_workspace_bytes(batch, seq_len)));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  unsigned int* err = ria::device_error_word();
+
+  PrepParams pp;
+  pp.q = static_cast<const __nv_bfloat16*>(q);
+  pp.qs_b = q_stride_b;
+  pp.qs_t = q_stride_t;
+  pp.k = static_cast<const __nv_bfloat16*>(k);
+  pp.ks_b = k_stride_b;
+  pp.ks_t = k_stride_t;
+  pp.v = static_cast<const __nv_bfloat16*>(v);
+  pp.vs_b = v_stride_b;
+  pp.vs_t = v_stride_t;
+  pp.q_norm_w = q_norm_weight;
+  pp.k_norm_w = k_norm_weight;
+  pp.inv_freq = inv_freq;
+  pp.k_pool = static_cast<__nv_bfloat16*>(k_pool);
+  pp.v_pool = static_cast<__nv_bfloat16*>(v_pool);
+  pp.pool_tokens = pool_tokens;
+  pp.block_table = block_table;
+  pp.bt_stride = block_table_stride;
+  pp.seq_lens = seq_lens;
+  pp.positions = positions;
+  pp.qbuf = static_cast<__nv_bfloat16*>(workspace);
+  pp.T = seq_len;
+  pp.num_blocks = static_cast<int>(pool_tokens / kBlock);
+  pp.err = err;
+  gqa_prefill_prep_kernel<<<dim3(seq_len, batch), 256, 0, st>>>(pp);
+  int rc = ria::check_launch("ria_gqa_prefill (prep)");
+  if (rc) return rc;
+
+  CUtensorMap tmQ, tmK, tmV, tmO;
+  {
+    const uint64_t dims[3] = {static_cast<uint64_t>(kHq * kD), static_cast<uint64_t>(seq_len),
+                              static_cast<uint64_t>(batch)};
+    const uint64_t sq[2] = {static_cast<uint64_t>(kHq * kD) * 2, static_cast<uint64_t>(seq_len) * kHq * kD * 2};
+    const uint64_t so[2] = {static_cast<uint64_t>(out_stride_t) * 2, static_cast<uint64_t>(out_stride_b) * 2};
+    const uint32_t box[3] = {64, kTile, 1};
+    rc = ria::encode_bf16_sw128_map(&tmQ, workspace, 3, dims, sq, box);
+    if (rc) return rc;
+    rc = ria::encode_bf16_sw128_map(&tmO, out, 3, dims, so, box);
+    if (rc) return rc;
+  }
+  rc = pool_map(&tmK, k_pool, pool_tokens);
+  if (rc) return rc;
+  rc = pool_map(&tmV, v_pool, pool_tokens);
+  if (rc) return rc;
+
+  AttnParams ap;
+  ap.gate = static_cast<const __nv_bfloat16*>(q) + kD;
+  ap.gs_b = q_stride_b;
+  ap.gs_t = q_stride_t;
+  ap.block_table = block_table;
+  ap.bt_stride = block_table_stride;
+  ap.seq_lens = seq_lens;
+  ap.T = seq_len;
+  ap.pool_tokens = pool_tokens;
+  ap.num_blocks = static_cast<int>(pool_tokens / kBlock);
+  ap.err = err;
+  cudaError_t e = cudaFuncSetAttribute(gqa_prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem);
+  if (e != cudaSuccess) return ria::fail(RIA_ERR_CUDA, "ria_gqa_prefill: smem attribute: %s", cudaGetErrorString(e));
+  dim3 grid((seq_len + kTile - 1) / kTile, kHq, batch);
+  gqa_prefill_attn_kernel<<<grid, 128, kAttnSmem, st>>>(tmQ, tmK, tmV, tmO, ap);
+  return ria::check_launch("ria_gqa_prefill (attention)");
+}

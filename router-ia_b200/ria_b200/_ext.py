@@ -72,6 +72,13 @@ _SIGNATURES: dict[str, tuple[object, list]] = {
          c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int32, c_int32, c_int32, c_int32,
          c_void_p],
     ),
+    "ria_gqa_prefill_workspace_bytes": (c_int64, [c_int32, c_int32]),
+    "ria_gqa_prefill": (
+        c_int,
+        [c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_void_p, c_void_p,
+         c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_int32, c_void_p, c_void_p, c_void_p, c_int64, c_int64,
+         c_void_p, c_int64, c_int32, c_int32, c_void_p],
+    ),
     "ria_umma_selftest": (c_int, [c_int32, c_int32, c_int32, c_int32, c_void_p, c_void_p, c_void_p, c_void_p]),
     "ria_advance_positions": (c_int, [c_void_p, c_void_p, c_int32, c_void_p]),
     "ria_rmsnorm_rows": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int32, c_int32, c_void_p]),
@@ -222,6 +229,26 @@ def gdn_chunk_prefill(q, k, v, g, beta, initial_state, final_state, out):
             v.stride(0), v.stride(1), g.data_ptr(), beta.data_ptr(), g.stride(0), g.stride(1), _ptr(initial_state),
             final_state.data_ptr(), out.data_ptr(), out.stride(0), out.stride(1), B, T, Hk, Hv, _stream(q))
     _check(rc, "ria_gdn_chunk_prefill")
+
+
+def gqa_prefill(q, k, v, q_norm_w, k_norm_w, inv_freq, k_pool, v_pool, block_table, seq_lens, positions, out,
+                workspace=None):
+    """K4 (see ria_gqa_prefill): q [B, T, 8192], k, v [B, T, 512] bf16 views
+    with unit inner stride; out [B, T, 4096] bf16."""
+    _require_cuda(q, k, v, k_pool, v_pool, block_table, seq_lens, positions, out)
+    B, T = q.shape[0], q.shape[1]
+    need = int(lib().ria_gqa_prefill_workspace_bytes(B, T))
+    if workspace is None or workspace.numel() * workspace.element_size() < need:
+        workspace = torch.empty(max(need, 16) // 2, dtype=torch.bfloat16, device=q.device)
+    with _Hooked("gqa_prefill", 2):
+        rc = lib().ria_gqa_prefill(
+            q.data_ptr(), q.stride(0), q.stride(1), k.data_ptr(), k.stride(0), k.stride(1), v.data_ptr(),
+            v.stride(0), v.stride(1), q_norm_w.data_ptr(), k_norm_w.data_ptr(), inv_freq.data_ptr(),
+            k_pool.data_ptr(), v_pool.data_ptr(), k_pool.shape[1], block_table.data_ptr(), block_table.stride(0),
+            seq_lens.data_ptr(), positions.data_ptr(), out.data_ptr(), out.stride(0), out.stride(1),
+            workspace.data_ptr(), workspace.numel() * workspace.element_size(), B, T, _stream(q))
+    _check(rc, "ria_gqa_prefill")
+    return workspace
 
 
 def umma_selftest(a, b, a_mn_major: bool, b_mn_major: bool):
