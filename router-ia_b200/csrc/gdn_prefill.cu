@@ -118,7 +118,9 @@ __device__ __forceinline__ float sumsq_row(const unsigned char* box0, const unsi
     const unsigned char* rowp = (part ? box1 : box0) + r * 128;
 #pragma unroll
     for (int ch = 0; ch < 8; ++ch) {
-      const uint4 u = *reinterpret_cast<const uint4*>(rowp + ch * 16);
+      // visit the row's 16-byte chunks in swizzled order so that the 32 lanes
+      // (32 different rows) spread over all banks
+      const uint4 u = *reinterpret_cast<const uint4*>(rowp + ((ch ^ (r & 7)) << 4));
       const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -135,7 +137,8 @@ __device__ __forceinline__ float sumsq_row(const unsigned char* box0, const unsi
 __device__ __forceinline__ void scale_row_bf16(unsigned char* box, int r, float s) {
   unsigned char* rowp = box + r * 128;
 #pragma unroll
-  for (int ch = 0; ch < 8; ++ch) {
+  for (int c = 0; c < 8; ++c) {
+    const int ch = c ^ (r & 7);  // bank-spread visiting order
     uint4 u = *reinterpret_cast<uint4*>(rowp + ch * 16);
     __nv_bfloat162* h2 = reinterpret_cast<__nv_bfloat162*>(&u);
 #pragma unroll

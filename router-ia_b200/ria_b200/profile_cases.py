@@ -103,6 +103,33 @@ def prefill_case(batch: int, seq: int, iters: int, device, hk: int = 16, hv: int
             "tflops": flops / (ms * 1e9)}
 
 
+def gqa_prefill_case(batch: int, seq: int, iters: int, device) -> dict:
+    """One GQA layer prefilling ``seq`` new tokens per sequence (empty cache):
+    causal attention FLOPs = 16 heads x 2 x 2 x 256 x seq(seq+1)/2 per sequence."""
+    w = GqaWeights.from_tensors(synthetic.layer_weights_on_device(3, device), device)
+    nb = (seq + 63) // 64
+    g0 = torch.Generator(device=device)
+    g0.manual_seed(3)
+    k_pool = torch.zeros(2, batch * nb * 64, 256, dtype=torch.bfloat16, device=device)
+    v_pool = torch.zeros_like(k_pool)
+    table = torch.arange(batch * nb, dtype=torch.int32, device=device).reshape(batch, nb)
+    q = torch.randn(batch, seq, C.FULL_Q_GATE_DIM, device=device, generator=g0).to(torch.bfloat16)
+    k = torch.randn(batch, seq, C.FULL_KV_DIM, device=device, generator=g0).to(torch.bfloat16)
+    v = torch.randn(batch, seq, C.FULL_KV_DIM, device=device, generator=g0).to(torch.bfloat16)
+    lens = torch.zeros(batch, dtype=torch.int32, device=device)
+    out = torch.empty(batch, seq, 4096, dtype=torch.bfloat16, device=device)
+    inv = rope_inv_freq(device)
+    ws = [None]
+
+    def run():
+        ws[0] = _ext.gqa_prefill(q, k, v, w.q_norm, w.k_norm, inv, k_pool, v_pool, table, lens, lens, out, ws[0])
+
+    ms = _time(run, iters, device)
+    flops = batch * 16 * 2 * 2 * 256 * seq * (seq + 1) / 2
+    return {"kernel": "gqa_prefill", "batch": batch, "seq": seq, "ms": ms, "tokens_per_s": batch * seq / (ms * 1e-3),
+            "tflops": flops / (ms * 1e9)}
+
+
 def _time(fn, iters, device):
     for _ in range(3):
         fn()
@@ -118,7 +145,7 @@ def _time(fn, iters, device):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--kernel", choices=("gdn", "gqa", "prefill", "all"), default="all")
+    ap.add_argument("--kernel", choices=("gdn", "gqa", "prefill", "gqa_prefill", "all"), default="all")
     ap.add_argument("--seq", type=int, default=8192)
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--len", type=int, default=4096)
@@ -131,6 +158,8 @@ def main():
     if args.kernel in ("gqa", "all"):
         print(gqa_case(args.batch if args.kernel == "gqa" else max(1, args.batch // 2), args.len, args.iters, dev),
               flush=True)
+    if args.kernel == "gqa_prefill":
+        print(gqa_prefill_case(args.batch, args.seq, args.iters, dev), flush=True)
     if args.kernel == "prefill":
         print(prefill_case(args.batch, args.seq, args.iters, dev), flush=True)
     if _ext.device_error():
