@@ -194,6 +194,29 @@ RIA_API int ria_gqa_prefill(const void* q, int64_t q_stride_b, int64_t q_stride_
                             int64_t out_stride_b, int64_t out_stride_t, void* workspace, int64_t workspace_bytes,
                             int32_t batch, int32_t seq_len, ria_stream_t stream);
 
+/* ------------------------------------------------------------------------
+ * Row kernels of the DeltaNet prompt path around K2 (the per-token arithmetic
+ * of _linear_stateful, qwen36_attention_cache.py:176-271, for T tokens).
+ */
+
+/* Causal depthwise conv (kernel 4) + SiLU over T tokens in bf16, continuing
+ * from conv_state [B, channels, 4] (updated to the last four inputs):
+ * x, out [B, T, channels] bf16 with element strides. */
+RIA_API int ria_conv1d_prefill(const void* x, int64_t x_stride_b, int64_t x_stride_t, void* conv_state,
+                               const void* weight, void* out, int64_t out_stride_b, int64_t out_stride_t,
+                               int32_t batch, int32_t seq_len, int32_t channels, ria_stream_t stream);
+
+/* g = -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b) for rows x heads:
+ * a, b bf16 rows (strides), g, beta f32 [rows, heads] (qwen36_attention_cache.py:242-250). */
+RIA_API int ria_gdn_gates(const void* a, int64_t a_stride, const void* b, int64_t b_stride, const float* a_log,
+                          const float* dt_bias, float* g, float* beta, int32_t rows, int32_t heads,
+                          ria_stream_t stream);
+
+/* Gated RMSNorm per 128-wide head (qwen36_gated_norm_probe.py:19-36):
+ * out = w * o * rsqrt(mean(o^2) + 1e-6) * silu(z); o, z, out bf16 rows. */
+RIA_API int ria_gated_rmsnorm(const void* o, int64_t o_stride, const void* z, int64_t z_stride, const float* weight,
+                              void* out, int64_t out_stride, int32_t rows, int32_t heads, ria_stream_t stream);
+
 /* Diagnostic (no counterpart in the reference): one CTA computes
  * d[128 x n] = a[128 x k] * b[k x n] (row-major fp32 in/out, bf16 operands)
  * with tcgen05 MMAs whose A / B operands are staged K-major (0) or MN-major (1)

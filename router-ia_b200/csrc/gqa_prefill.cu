@@ -79,13 +79,13 @@ __device__ __forceinline__ void norm_rope_8(float (&x)[8], const float* w, const
     const float dn = __shfl_up_sync(0xffffffffu, x[i], 4);
     partner[i] = (lane < 4) ? up : dn;
   }
-  if (lane < 8) {
+  if (lane < kRope / 8) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int d = lane * 8 + i;
       float sn, cs;
-      sincosf(static_cast<float>(pos) * inv_freq[d & 31], &sn, &cs);
-      x[i] = (d < 32) ? (x[i] * cs - partner[i] * sn) : (x[i] * cs + partner[i] * sn);
+      sincosf(static_cast<float>(pos) * inv_freq[d & (kRope / 2 - 1)], &sn, &cs);
+      x[i] = (d < kRope / 2) ? (x[i] * cs - partner[i] * sn) : (x[i] * cs + partner[i] * sn);
     }
   }
 }

@@ -1,0 +1,155 @@
+// Row kernels of a Gated DeltaNet layer's prompt (prefill) path around K2:
+// the causal depthwise conv over T tokens with the rolling conv state, the
+// decay / beta gates, and the gated RMSNorm of the chunked rule's output.
+// Each restates, for T tokens at once, the per-token arithmetic of
+// router-ia's _linear_stateful (qwen36_attention_cache.py:176-271).
+#include "ria_capi_internal.h"
+#include "ria_common.cuh"
+
+namespace {
+
+constexpr int kConvTile = 256;  // tokens per CTA in the conv prefill
+
+// out[b, t, c] = silu(sum_j w[c, j] * h[t - 3 + j]) with h[-3..-1] taken from
+// the conv state (its last three entries) and the bf16 rounding of the conv
+// output and of the SiLU, as in the one-token step.  Reads the state only.
+__global__ void conv1d_prefill_kernel(const __nv_bfloat16* __restrict__ x, int64_t xs_b, int64_t xs_t,
+                                      const __nv_bfloat16* __restrict__ state, const __nv_bfloat16* __restrict__ w,
+                                      __nv_bfloat16* __restrict__ out, int64_t os_b, int64_t os_t, int T,
+                                      int channels) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  const int b = blockIdx.z;
+  if (c >= channels) return;
+  const int t0 = blockIdx.y * kConvTile;
+  const int t1 = min(T, t0 + kConvTile);
+  const __nv_bfloat16* st = state + (static_cast<int64_t>(b) * channels + c) * 4;
+  const __nv_bfloat16* xc = x + static_cast<int64_t>(b) * xs_b + c;
+  auto hist = [&](int t) -> float {  // input at token t (t < 0 reads the state)
+    return t >= 0 ? __bfloat162float(xc[static_cast<int64_t>(t) * xs_t]) : __bfloat162float(st[4 + t]);
+  };
+  const float w0 = __bfloat162float(w[c * 4 + 0]), w1 = __bfloat162float(w[c * 4 + 1]);
+  const float w2 = __bfloat162float(w[c * 4 + 2]), w3 = __bfloat162float(w[c * 4 + 3]);
+  float h0 = hist(t0 - 3), h1 = hist(t0 - 2), h2 = hist(t0 - 1);
+  __nv_bfloat16* oc = out + static_cast<int64_t>(b) * os_b + c;
+  for (int t = t0; t < t1; ++t) {
+    const float h3 = __bfloat162float(xc[static_cast<int64_t>(t) * xs_t]);
+    float acc = w0 * h0;
+    acc = fmaf(w1, h1, acc);
+    acc = fmaf(w2, h2, acc);
+    acc = fmaf(w3, h3, acc);
+    const float y = bf16_round(acc);
+    oc[static_cast<int64_t>(t) * os_t] = __float2bfloat16_rn(y / (1.0f + expf(-y)));
+    h0 = h1;
+    h1 = h2;
+    h2 = h3;
+  }
+}
+
+// New conv state = the last four inputs of [state, x_0 .. x_{T-1}]; runs after
+// conv1d_prefill_kernel so that every read of the old state came first.
+__global__ void conv1d_state_kernel(const __nv_bfloat16* __restrict__ x, int64_t xs_b, int64_t xs_t,
+                                    __nv_bfloat16* state, int T, int channels) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  const int b = blockIdx.y;
+  if (c >= channels) return;
+  __nv_bfloat16* st = state + (static_cast<int64_t>(b) * channels + c) * 4;
+  const __nv_bfloat16* xc = x + static_cast<int64_t>(b) * xs_b + c;
+  __nv_bfloat16 s[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int t = T - 4 + i;
+    s[i] = t >= 0 ? xc[static_cast<int64_t>(t) * xs_t] : st[4 + t];  // t < 0: shifted old entry
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) st[i] = s[i];
+}
+
+__device__ __forceinline__ float softplus_torch(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
+
+// g = -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b); rows x heads.
+__global__ void gdn_gates_kernel(const __nv_bfloat16* __restrict__ a, int64_t as, const __nv_bfloat16* __restrict__ bb,
+                                 int64_t bs, const float* __restrict__ a_log, const float* __restrict__ dt_bias,
+                                 float* __restrict__ g, float* __restrict__ beta, int rows, int heads) {
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= rows * heads) return;
+  const int r = idx / heads, h = idx % heads;
+  const float av = __bfloat162float(a[static_cast<int64_t>(r) * as + h]);
+  const float bv = __bfloat162float(bb[static_cast<int64_t>(r) * bs + h]);
+  g[idx] = -expf(a_log[h]) * softplus_torch(av + dt_bias[h]);
+  beta[idx] = 1.0f / (1.0f + expf(-bv));
+}
+
+// out = w * (o * rsqrt(mean(o^2) + 1e-6)) * silu(z) per 128-wide head,
+// qwen36_gated_norm_probe.py:19-36.  One warp per (row, head).
+__global__ void gated_rmsnorm_kernel(const __nv_bfloat16* __restrict__ o, int64_t os, const __nv_bfloat16* __restrict__ z,
+                                     int64_t zs, const float* __restrict__ w, __nv_bfloat16* __restrict__ out,
+                                     int64_t outs, int rows, int heads) {
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (gw >= rows * heads) return;
+  const int r = gw / heads, h = gw % heads;
+  const __nv_bfloat16* orow = o + static_cast<int64_t>(r) * os + h * 128 + lane * 4;
+  const __nv_bfloat16* zrow = z + static_cast<int64_t>(r) * zs + h * 128 + lane * 4;
+  float v[4], zz[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[i] = __bfloat162float(orow[i]);
+    zz[i] = __bfloat162float(zrow[i]);
+  }
+  const float ss = warp_sum(v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3]);
+  const float rn = rsqrtf(ss * (1.0f / 128) + 1e-6f);
+  __nv_bfloat16* dst = out + static_cast<int64_t>(r) * outs + h * 128 + lane * 4;
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    dst[i] = __float2bfloat16_rn(w[lane * 4 + i] * (v[i] * rn) * (zz[i] / (1.0f + expf(-zz[i]))));
+}
+
+}  // namespace
+
+extern "C" int ria_conv1d_prefill(const void* x, int64_t x_stride_b, int64_t x_stride_t, void* conv_state,
+                                  const void* weight, void* out, int64_t out_stride_b, int64_t out_stride_t,
+                                  int32_t batch, int32_t seq_len, int32_t channels, ria_stream_t stream) {
+  if (batch < 0 || seq_len < 0 || channels <= 0) return ria::fail(RIA_ERR_INVALID, "ria_conv1d_prefill: bad sizes");
+  if (batch == 0 || seq_len == 0) return RIA_OK;
+  if (!x || !conv_state || !weight || !out) return ria::fail(RIA_ERR_INVALID, "ria_conv1d_prefill: null pointer");
+  if (batch > 65535 || (seq_len + kConvTile - 1) / kConvTile > 65535)
+    return ria::fail(RIA_ERR_INVALID, "ria_conv1d_prefill: grid too large");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(x);
+  __nv_bfloat16* sb = static_cast<__nv_bfloat16*>(conv_state);
+  dim3 grid((channels + 255) / 256, (seq_len + kConvTile - 1) / kConvTile, batch);
+  conv1d_prefill_kernel<<<grid, 256, 0, st>>>(xb, x_stride_b, x_stride_t, sb, static_cast<const __nv_bfloat16*>(weight),
+                                              static_cast<__nv_bfloat16*>(out), out_stride_b, out_stride_t, seq_len,
+                                              channels);
+  int rc = ria::check_launch("ria_conv1d_prefill");
+  if (rc) return rc;
+  conv1d_state_kernel<<<dim3((channels + 255) / 256, batch), 256, 0, st>>>(xb, x_stride_b, x_stride_t, sb, seq_len,
+                                                                           channels);
+  return ria::check_launch("ria_conv1d_prefill (state)");
+}
+
+extern "C" int ria_gdn_gates(const void* a, int64_t a_stride, const void* b, int64_t b_stride, const float* a_log,
+                             const float* dt_bias, float* g, float* beta, int32_t rows, int32_t heads,
+                             ria_stream_t stream) {
+  if (rows < 0 || heads <= 0) return ria::fail(RIA_ERR_INVALID, "ria_gdn_gates: bad sizes");
+  if (rows == 0) return RIA_OK;
+  if (!a || !b || !a_log || !dt_bias || !g || !beta) return ria::fail(RIA_ERR_INVALID, "ria_gdn_gates: null pointer");
+  const int64_t n = static_cast<int64_t>(rows) * heads;
+  gdn_gates_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(a), a_stride, static_cast<const __nv_bfloat16*>(b), b_stride, a_log, dt_bias,
+      g, beta, rows, heads);
+  return ria::check_launch("ria_gdn_gates");
+}
+
+extern "C" int ria_gated_rmsnorm(const void* o, int64_t o_stride, const void* z, int64_t z_stride,
+                                 const float* weight, void* out, int64_t out_stride, int32_t rows, int32_t heads,
+                                 ria_stream_t stream) {
+  if (rows < 0 || heads <= 0) return ria::fail(RIA_ERR_INVALID, "ria_gated_rmsnorm: bad sizes");
+  if (rows == 0) return RIA_OK;
+  if (!o || !z || !weight || !out) return ria::fail(RIA_ERR_INVALID, "ria_gated_rmsnorm: null pointer");
+  const int64_t warps = static_cast<int64_t>(rows) * heads;
+  gated_rmsnorm_kernel<<<static_cast<unsigned>((warps * 32 + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(o), o_stride, static_cast<const __nv_bfloat16*>(z), z_stride, weight,
+      static_cast<__nv_bfloat16*>(out), out_stride, rows, heads);
+  return ria::check_launch("ria_gated_rmsnorm");
+}

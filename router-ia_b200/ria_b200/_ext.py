@@ -79,6 +79,14 @@ _SIGNATURES: dict[str, tuple[object, list]] = {
          c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_int32, c_void_p, c_void_p, c_void_p, c_int64, c_int64,
          c_void_p, c_int64, c_int32, c_int32, c_void_p],
     ),
+    "ria_conv1d_prefill": (
+        c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int32, c_int32, c_int32,
+                c_void_p]),
+    "ria_gdn_gates": (
+        c_int, [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32,
+                c_void_p]),
+    "ria_gated_rmsnorm": (
+        c_int, [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int32, c_int32, c_void_p]),
     "ria_umma_selftest": (c_int, [c_int32, c_int32, c_int32, c_int32, c_void_p, c_void_p, c_void_p, c_void_p]),
     "ria_advance_positions": (c_int, [c_void_p, c_void_p, c_int32, c_void_p]),
     "ria_rmsnorm_rows": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int32, c_int32, c_void_p]),
@@ -249,6 +257,36 @@ def gqa_prefill(q, k, v, q_norm_w, k_norm_w, inv_freq, k_pool, v_pool, block_tab
             workspace.data_ptr(), workspace.numel() * workspace.element_size(), B, T, _stream(q))
     _check(rc, "ria_gqa_prefill")
     return workspace
+
+
+def conv1d_prefill(x, conv_state, weight, out):
+    """x, out [B, T, C] bf16 (unit channel stride); conv_state [B, C, 4] bf16."""
+    _require_cuda(x, conv_state, weight, out)
+    B, T, Cc = x.shape
+    with _Hooked("conv1d_prefill", 2):
+        rc = lib().ria_conv1d_prefill(x.data_ptr(), x.stride(0), x.stride(1), conv_state.data_ptr(), weight.data_ptr(),
+                                      out.data_ptr(), out.stride(0), out.stride(1), B, T, Cc, _stream(x))
+    _check(rc, "ria_conv1d_prefill")
+
+
+def gdn_gates(a, b, a_log, dt_bias, g, beta):
+    """a, b [rows, heads] bf16 views; g, beta [rows, heads] f32 contiguous."""
+    _require_cuda(a, b, g, beta)
+    rows, heads = a.shape
+    with _Hooked("gdn_gates"):
+        rc = lib().ria_gdn_gates(a.data_ptr(), a.stride(0), b.data_ptr(), b.stride(0), a_log.data_ptr(),
+                                 dt_bias.data_ptr(), g.data_ptr(), beta.data_ptr(), rows, heads, _stream(a))
+    _check(rc, "ria_gdn_gates")
+
+
+def gated_rmsnorm(o, z, weight, out):
+    """o, z, out [rows, heads*128] bf16 views (unit inner stride)."""
+    _require_cuda(o, z, weight, out)
+    rows, width = o.shape
+    with _Hooked("gated_rmsnorm"):
+        rc = lib().ria_gated_rmsnorm(o.data_ptr(), o.stride(0), z.data_ptr(), z.stride(0), weight.data_ptr(),
+                                     out.data_ptr(), out.stride(0), rows, width // 128, _stream(o))
+    _check(rc, "ria_gated_rmsnorm")
 
 
 def umma_selftest(a, b, a_mn_major: bool, b_mn_major: bool):

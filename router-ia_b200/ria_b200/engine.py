@@ -96,6 +96,58 @@ def gqa_decode(x: torch.Tensor, w: GqaWeights, k_pool: torch.Tensor, v_pool: tor
     return out
 
 
+def deltanet_prefill(x: torch.Tensor, w: DeltaNetWeights, rec: torch.Tensor, conv: torch.Tensor) -> torch.Tensor:
+    """T prompt tokens of B sequences through one DeltaNet layer at once:
+    x [B, T, 2048] fp32 -> residual [B, T, 2048] fp32; ``rec`` [B, 32, 128, 128]
+    and ``conv`` [B, 8192, 4] continue from and end at the sequences' state.
+    Same arithmetic as T decode steps, with the recurrence in chunked form
+    (K2) instead of token by token."""
+    B, T, _ = x.shape
+    xf = x.reshape(B * T, C.HIDDEN)
+    h = torch.empty(B * T, C.HIDDEN, dtype=torch.bfloat16, device=x.device)
+    _ext.rmsnorm_rows(xf, w.in_norm, h)
+    proj = F.linear(h, w.w_in)
+    mixed = proj.view(B, T, C.DN_PROJ_WIDTH)[:, :, C.DN_PROJ_QKV[0]:C.DN_PROJ_QKV[1]]
+    y = torch.empty(B, T, C.LINEAR_CONV_DIM, dtype=torch.bfloat16, device=x.device)
+    _ext.conv1d_prefill(mixed, conv, w.conv_w, y)
+    q = y[:, :, :C.LINEAR_KEY_DIM].unflatten(2, (C.LINEAR_NUM_K_HEADS, C.LINEAR_HEAD_DIM))
+    k = y[:, :, C.LINEAR_KEY_DIM:2 * C.LINEAR_KEY_DIM].unflatten(2, (C.LINEAR_NUM_K_HEADS, C.LINEAR_HEAD_DIM))
+    v = y[:, :, 2 * C.LINEAR_KEY_DIM:].unflatten(2, (C.LINEAR_NUM_V_HEADS, C.LINEAR_HEAD_DIM))
+    g = torch.empty(B * T, C.LINEAR_NUM_V_HEADS, dtype=torch.float32, device=x.device)
+    beta = torch.empty_like(g)
+    _ext.gdn_gates(proj[:, C.DN_PROJ_A[0]:C.DN_PROJ_A[1]], proj[:, C.DN_PROJ_B[0]:C.DN_PROJ_B[1]], w.a_log,
+                   w.dt_bias, g, beta)
+    o = torch.empty(B, T, C.LINEAR_NUM_V_HEADS, C.LINEAR_HEAD_DIM, dtype=torch.bfloat16, device=x.device)
+    _ext.gdn_chunk_prefill(q, k, v, g.view(B, T, -1), beta.view(B, T, -1), rec, rec, o)
+    gated = torch.empty(B * T, C.LINEAR_VALUE_DIM, dtype=torch.bfloat16, device=x.device)
+    _ext.gated_rmsnorm(o.view(B * T, C.LINEAR_VALUE_DIM), proj[:, C.DN_PROJ_Z[0]:C.DN_PROJ_Z[1]], w.norm_w, gated)
+    out_p = F.linear(gated, w.w_out)
+    out = torch.empty(B * T, C.HIDDEN, dtype=torch.float32, device=x.device)
+    _ext.residual_add(xf, out_p, out)
+    return out.view(B, T, C.HIDDEN)
+
+
+def gqa_prefill(x: torch.Tensor, w: GqaWeights, k_pool: torch.Tensor, v_pool: torch.Tensor,
+                block_table: torch.Tensor, inv_freq: torch.Tensor, seq_lens: torch.Tensor, positions: torch.Tensor,
+                workspace: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """T prompt tokens of B sequences through one GQA layer (K4): x
+    [B, T, 2048] fp32 -> (residual [B, T, 2048] fp32, workspace); K/V appended
+    at seq_lens[b] + t, RoPE at positions[b] + t."""
+    B, T, _ = x.shape
+    xf = x.reshape(B * T, C.HIDDEN)
+    h = torch.empty(B * T, C.HIDDEN, dtype=torch.bfloat16, device=x.device)
+    _ext.rmsnorm_rows(xf, w.in_norm, h)
+    proj = F.linear(h, w.w_in).view(B, T, C.GQA_PROJ_WIDTH)
+    attn = torch.empty(B, T, C.FULL_Q_DIM, dtype=torch.bfloat16, device=x.device)
+    workspace = _ext.gqa_prefill(proj[:, :, C.GQA_PROJ_Q[0]:C.GQA_PROJ_Q[1]], proj[:, :, C.GQA_PROJ_K[0]:C.GQA_PROJ_K[1]],
+                                 proj[:, :, C.GQA_PROJ_V[0]:C.GQA_PROJ_V[1]], w.q_norm, w.k_norm, inv_freq, k_pool,
+                                 v_pool, block_table, seq_lens, positions, attn, workspace)
+    o = F.linear(attn.view(B * T, C.FULL_Q_DIM), w.w_out)
+    out = torch.empty(B * T, C.HIDDEN, dtype=torch.float32, device=x.device)
+    _ext.residual_add(xf, o, out)
+    return out.view(B, T, C.HIDDEN), workspace
+
+
 class BlockAllocator:
     """Free list of physical KV blocks shared by every GQA layer's pool."""
 
@@ -203,6 +255,34 @@ class BatchedAttentionState:
         if grew:
             self.block_table.copy_(self._table_host)
         return self.plan()
+
+    def prefill(self, x: torch.Tensor) -> torch.Tensor:
+        """T prompt tokens for every sequence at once: x [B, T, 2048] fp32 ->
+        [B, T, 2048] fp32, every layer's state advanced by T tokens.  Equals T
+        calls of ``step`` (router-ia's prompt loop, qwen36_chat_batch.py:
+        255-258) with the DeltaNet recurrence in chunked form (K2) and the GQA
+        layers through the causal prefill kernel (K4)."""
+        B, T, _ = x.shape
+        if B != self.batch:
+            raise ValueError(f"prefill expects all {self.batch} sequences, got {B}")
+        for i, n in enumerate(self.lengths):
+            self.reserve(i, n + T)
+        self.block_table.copy_(self._table_host)
+        self.seq_lens.copy_(torch.tensor(self.lengths, dtype=torch.int32))
+        self.positions.copy_(torch.tensor(self.positions_host, dtype=torch.int32))
+        ws = None
+        for layer in sorted(self.layers):
+            w = self.layers[layer]
+            if isinstance(w, DeltaNetWeights):
+                x = deltanet_prefill(x, w, self.rec[layer], self.conv[layer])
+            else:
+                x, ws = gqa_prefill(x, w, self.k_pool[layer], self.v_pool[layer], self.block_table, self.inv_freq,
+                                    self.seq_lens, self.positions, ws)
+        self.lengths = [n + T for n in self.lengths]
+        self.positions_host = [p + T for p in self.positions_host]
+        self.seq_lens.copy_(torch.tensor(self.lengths, dtype=torch.int32))
+        self.positions.copy_(torch.tensor(self.positions_host, dtype=torch.int32))
+        return x
 
     def step(self, x: torch.Tensor, launch: GqaLaunch | None = None, advance: bool = True) -> torch.Tensor:
         """Run every layer once for the batch: x [B, 2048] fp32 -> [B, 2048] fp32.
