@@ -391,15 +391,16 @@ def config2_prefill(device, iters=5, warmup=3):
     beta = torch.sigmoid(torch.randn(B, T, Hv, device=device, generator=g0)).float()
     out = torch.empty(B, T, Hv, 128, dtype=torch.bfloat16, device=device)
     fs = torch.empty(B, Hv, 128, 128, dtype=torch.float32, device=device)
+    ws = torch.empty(_ext.gdn_chunk_prefill_workspace_bytes(B, T, Hv), dtype=torch.uint8, device=device)
     for _ in range(warmup):
-        chunk_gated_delta_rule(q, k, v, g, beta, None, fs, out)
+        chunk_gated_delta_rule(q, k, v, g, beta, None, fs, out, ws)
     hook = EventHook(timed=("gdn_prefill",))
     _ext.launch_hook = hook
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize(device)
     s.record()
     for _ in range(iters):
-        chunk_gated_delta_rule(q, k, v, g, beta, None, fs, out)
+        chunk_gated_delta_rule(q, k, v, g, beta, None, fs, out, ws)
     e.record()
     torch.cuda.synchronize(device)
     _ext.launch_hook = None

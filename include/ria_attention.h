@@ -162,13 +162,21 @@ RIA_API int32_t ria_gqa_decode_split_pages(int64_t total_blocks, int32_t num_kv_
  * initial_state [B, num_v_heads, 128 k, 128 v] f32 or NULL (zeros);
  * final_state   same layout (may alias initial_state): the state after T tokens,
  *      in the decode kernel's layout;
- * out  [B, T, num_v_heads, 128] bf16 (o_stride_b / o_stride_t). */
+ * out  [B, T, num_v_heads, 128] bf16 (o_stride_b / o_stride_t);
+ * workspace: 16-byte aligned device scratch for the per-chunk matrices (W, U,
+ *      the causal score tile and the chunk scalars, 41,600 bytes per sequence,
+ *      value head and chunk).  ria_gdn_chunk_prefill_workspace_bytes() gives the
+ *      size for the whole prompt; a smaller workspace (at least one chunk for
+ *      every sequence and head) makes the call run the prompt in blocks of
+ *      chunks, carrying the state through final_state. */
+RIA_API int64_t ria_gdn_chunk_prefill_workspace_bytes(int32_t batch, int32_t seq_len, int32_t num_v_heads);
 RIA_API int ria_gdn_chunk_prefill(const void* q, int64_t q_stride_b, int64_t q_stride_t, const void* k,
                                   int64_t k_stride_b, int64_t k_stride_t, const void* v, int64_t v_stride_b,
                                   int64_t v_stride_t, const float* g, const float* beta, int64_t gb_stride_b,
                                   int64_t gb_stride_t, const float* initial_state, float* final_state, void* out,
-                                  int64_t o_stride_b, int64_t o_stride_t, int32_t batch, int32_t seq_len,
-                                  int32_t num_k_heads, int32_t num_v_heads, ria_stream_t stream);
+                                  int64_t o_stride_b, int64_t o_stride_t, void* workspace, int64_t workspace_bytes,
+                                  int32_t batch, int32_t seq_len, int32_t num_k_heads, int32_t num_v_heads,
+                                  ria_stream_t stream);
 
 /* ------------------------------------------------------------------------
  * K4: GQA prefill of T new tokens per sequence (batch B, same T).
@@ -221,8 +229,10 @@ RIA_API int ria_gated_rmsnorm(const void* o, int64_t o_stride, const void* z, in
  * d[128 x n] = a[128 x k] * b[k x n] (row-major fp32 in/out, bf16 operands)
  * with tcgen05 MMAs whose A / B operands are staged K-major (0) or MN-major (1)
  * in 128-byte-swizzled shared memory -- the operand layouts the prefill
- * kernels use.  n, k in {64, 128}.  Used by the tests to pin the descriptor
- * encodings against a reference matmul. */
+ * kernels use.  a_mn_major: 0 = A K-major in shared memory, 1 = MN-major,
+ * 2 = A in tensor memory (bf16 pairs per 32-bit column).  n, k in {64, 128}.
+ * Used by the tests to pin the descriptor encodings against a reference
+ * matmul. */
 RIA_API int ria_umma_selftest(int32_t a_mn_major, int32_t b_mn_major, int32_t n, int32_t k, const float* a,
                               const float* b, float* d, ria_stream_t stream);
 

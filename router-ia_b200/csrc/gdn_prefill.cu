@@ -11,22 +11,35 @@
 //   V' = U - W S,   O = diag(e^gamma) Q S + (Q K^T o causal decay) V'
 //   S <- e^gamma_C S + K^T diag(e^(gamma_C - gamma)) V'
 //
-// B200 design: one CTA per (sequence, value head), two warpgroups.
-//   * Warpgroup 0 (prep) works one chunk ahead on everything that does not
-//     depend on the state: TMA loads of the Q/K/V tiles (3-D tensor maps, no
-//     multicast), gates and norms, G = [Q;K] K^T on the tensor cores, the
-//     causal score tile P and the 64x64 unit-lower-triangular inverse (CUDA
-//     cores, 16x16 blocks), W^T = K^T TW^T and U^T = V^T TU^T on the tensor
-//     cores, and the row-scaled Q (the output scale e^gamma s_q 128^-0.5 moved
-//     onto Q so both output products share one accumulator).
-//   * Warpgroup 1 (recurrence) owns the fp32 state S^T in TMEM:
-//     X = S^T W^T and O = S^T Qr^T, V'^T = U^T - X, O += V'^T P^T and
-//     S^T = e^gamma_C S^T + V's^T K, then the bf16 output.
-//   The two hand chunks over through a two-slot SMEM ring: prep arrives on a
-//   "full" mbarrier when a slot is ready, and the recurrence refills a slot
-//   with the TMA of chunk c + 2 as soon as its MMAs have read it.  Every product is an M = 128 UMMA
-//   (tcgen05.mma cta_group::1, bf16 operands in 128-byte-swizzled SMEM, fp32
-//   accumulation in TMEM); all waits are bounded.
+// B200 design: everything that does not depend on the state is chunk-parallel
+// and runs in its own kernel, so the state recurrence is a short chain of
+// tensor-core steps.
+//   * gdn_chunk_prep_kernel: one 128-thread CTA per (chunk, value head,
+//     sequence), three CTAs per SM.  TMA loads of the Q/K tiles (3-D tensor
+//     maps, no multicast), gates and norms, G = [Q;K] K^T on the tensor cores,
+//     the causal score tile P and A, the 64x64 unit-lower-triangular inverse
+//     (16x16 diagonal blocks by substitution, off-diagonal blocks by tf32
+//     mma.sync), then W^T = K^T TW^T and U^T = V^T TU^T on the tensor cores.
+//     Writes one 41,600-byte record per (sequence, head, chunk) to the
+//     workspace: W^T [128 dk][64] bf16, U^T [128 dv][64] bf16, P [64][64] bf16
+//     and the chunk scalars (e^gamma_C, the per-token state-update scale
+//     s_k e^(gamma_C - gamma), the per-token output scale e^gamma s_q 128^-0.5).
+//   * gdn_chunk_recurrence_kernel: one 256-thread CTA per (sequence, value
+//     head).  The fp32 state S^T (lane = dv, column = dk) stays in TMEM for
+//     the whole prompt; per chunk: bf16 copy of S^T into TMEM, X = S^T W^T and
+//     O = S^T Qr^T with the A operand read from TMEM, V'^T = U^T - X (raw and
+//     column-scaled, both back into TMEM as bf16), S^T += V's^T K and
+//     O += V'^T P^T.  The chunk's operands (Q, K, W^T, U^T, P, scalars) arrive
+//     by TMA through a three-slot ring refilled as soon as a chunk's MMAs are
+//     complete; O is double-buffered in TMEM so the output of chunk c-1 is
+//     written while chunk c's MMAs run.
+// When the workspace holds fewer chunks than the prompt, the host runs the
+// pair over blocks of chunks with the state carried in final_state.  Every
+// product is an M = 128 UMMA (tcgen05.mma cta_group::1 kind::f16, fp32
+// accumulation in TMEM); every wait is bounded.
+#include <algorithm>
+#include <climits>
+
 #include "ria_capi_internal.h"
 #include "ria_common.cuh"
 #include "tcgen05.cuh"
@@ -36,52 +49,57 @@ namespace {
 constexpr int kC = 64;
 constexpr int kDK = 128;
 constexpr int kDV = 128;
-constexpr int kThreads = 256;
 constexpr float kQScale = 0.08838834764831845f;  // 128 ** -0.5
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr uint32_t kBox = 8192;  // 64 rows x 128 bytes, 128-byte swizzled
+constexpr int kLd = 65;          // padded fp32 row of A and T (bank-conflict free)
 
-// SMEM map (bytes).  A chunk slot holds X = [Q dims 0-63 | K dims 0-63],
-// Y = [Q dims 64-127 | K dims 64-127], V (then U^T bf16 [128 dv][64]), W^T
-// bf16 [128 dk][64] (MN-major B), P bf16 [64][64], and the chunk scalars.
-// Every box is 64 rows x 128 bytes, 128-byte swizzled.
-constexpr uint32_t kBox = 8192;
-constexpr uint32_t kSlX = 0, kSlY = 2 * kBox, kSlV = 4 * kBox, kSlWT = 6 * kBox, kSlP = 8 * kBox;
-constexpr uint32_t kSlScal = 9 * kBox;  // eC, colscale[64]
+// Workspace record of one (sequence, value head, chunk).
+constexpr uint32_t kRecWT = 0;         // W^T [128 dk][64 tokens] bf16
+constexpr uint32_t kRecUT = 16384;     // U^T [128 dv][64 tokens] bf16
+constexpr uint32_t kRecP = 32768;      // P [64 t][64 j] bf16
+constexpr uint32_t kRecScal = 40960;   // f32: [0] e^gamma_C, [4..67] state scale, [68..131] output scale
+constexpr uint32_t kScalBytes = 528;   // 132 floats
+constexpr uint32_t kRecBytes = 41600;  // 325 rows of 128 bytes
+constexpr uint32_t kRecRows = kRecBytes / 128;
+
+// ---------------------------------------------------------------- prep SMEM
+// X = [Q dims 0-63 | K dims 0-63], Y = [Q dims 64-127 | K dims 64-127].  Once
+// G and the norms are done the Q boxes are reused: P is staged in the first
+// for its TMA store, then V (dims 0-63, 64-127) is loaded over both.  The A
+// region later holds TW | TU and then the W^T staging tile, the T region the
+// U^T staging tile.
+constexpr uint32_t kPX = 0, kPY = 2 * kBox;
+constexpr uint32_t kPA = 4 * kBox;    // fp32 A [64][kLd]
+constexpr uint32_t kPT = kPA + 17 * 1024;  // fp32 T [64][kLd] (1024-byte aligned)
+constexpr uint32_t kPMisc = kPT + 64 * kLd * 4;
+constexpr uint32_t kPGam = kPMisc, kPBet = kPMisc + 256, kPSq = kPMisc + 512, kPSk = kPMisc + 768,
+                   kPGraw = kPMisc + 1024, kPEbk = kPMisc + 1280;
+constexpr uint32_t kPBar = kPMisc + 1536;  // tma_qk, tma_v, mma, tslot
+constexpr uint32_t kPSmem = kPBar + 32;
+static_assert(kPA % 1024 == 0 && kPT % 1024 == 0, "staging tiles need 1024-byte alignment");
+static_assert(64 * kLd * 4 <= kPT - kPA, "A region");
+static_assert(kPSmem * 3 <= 227 * 1024, "three prep CTAs per SM");
+
+// ---------------------------------------------------------------- recurrence SMEM
+constexpr uint32_t kSlQ = 0;            // Q dims 0-63 | 64-127 (scaled in place to Qr)
+constexpr uint32_t kSlK = 2 * kBox;     // K dims 0-63 | 64-127
+constexpr uint32_t kSlWT = 4 * kBox;    // W^T, two 64-row boxes
+constexpr uint32_t kSlUT = 6 * kBox;    // U^T, two 64-row boxes
+constexpr uint32_t kSlP = 8 * kBox;     // P
+constexpr uint32_t kSlScal = 9 * kBox;  // chunk scalars
 constexpr uint32_t kSlotBytes = 9 * kBox + 1024;
-constexpr uint32_t kOffSlot0 = 0;
-constexpr int kLd = 65;                            // padded fp32 row of A and T (bank-conflict free)
-constexpr uint32_t kOffAT = 2 * kSlotBytes;        // fp32 A [64][kLd], then TW | TU bf16
-constexpr uint32_t kOffTf = kOffAT + 64 * kLd * 4; // fp32 T [64][kLd]
-constexpr uint32_t kOffST = kOffAT + 33 * 1024;    // bf16 S^T [128][128] (two boxes); later VN | VNS, O staging
-constexpr uint32_t kOffMisc = kOffST + 4 * kBox;
-constexpr uint32_t kOffGraw = kOffMisc;
-constexpr uint32_t kOffGam = kOffMisc + 256;  // gamma * log2(e)
-constexpr uint32_t kOffBet = kOffMisc + 512;
-constexpr uint32_t kOffSq = kOffMisc + 768;
-constexpr uint32_t kOffSk = kOffMisc + 1024;
-constexpr uint32_t kOffZ = kOffMisc + 1280;  // inversion scratch, 4 warps x 16 x 17 f32
-constexpr uint32_t kOffBar = kOffZ + 4 * 16 * 17 * 4;   // tma[2] full[2] (unused x2) mma_p mma_r
-constexpr uint32_t kOffTslot = kOffBar + 64;
-constexpr uint32_t kSmemBytes = kOffTslot + 16;
+constexpr int kSlots = 3;
+constexpr uint32_t kRBar = kSlots * kSlotBytes;  // full[3], bar_x, bar_s, bar_o, tslot
+constexpr uint32_t kRSmem = kRBar + 128;
+constexpr uint32_t kChunkTx = 9 * kBox + kScalBytes;
+static_assert(kRSmem <= 227 * 1024, "recurrence SMEM");
 
-// TMEM columns
-constexpr uint32_t kTmS = 0, kTmX = 128, kTmO = 192, kTmG = 256, kTmWT = 320, kTmUT = 384;
+// Recurrence TMEM columns: S^T fp32, X, O (two buffers), bf16 S^T (two
+// buffers), bf16 V'^T, bf16 V's^T -- all 512 columns.
+constexpr uint32_t kTS = 0, kTX = 128, kTO = 192, kTSb = 320, kTV = 448, kTVs = 480;
 
-constexpr uint32_t kBarPrep = 1, kBarRec = 2;
-
-struct PrefillParams {
-  const float* g;  // [B][T][Hv] log decay
-  const float* beta;
-  int64_t gs_b, gs_t;
-  const float* init_state;  // [B][Hv][128 k][128 v] or null (zeros)
-  float* final_state;
-  __nv_bfloat16* out;  // [B][T][Hv][128]
-  int64_t os_b, os_t;
-  int T;
-  int Hv;
-  int group;  // value heads per key head
-  unsigned int* err;
-};
+constexpr uint32_t kBarPrep = 1;
 
 template <int N>
 __device__ __forceinline__ void store_row_bf16(unsigned char* tile, int row, int col0, const float* v) {
@@ -133,7 +151,7 @@ __device__ __forceinline__ float sumsq_row(const unsigned char* box0, const unsi
   return ss;
 }
 
-// Multiply the 128 bf16 of row r (two boxes) by s in place.
+// Multiply the 64 bf16 of row r of a 128-byte-swizzled box by s in place.
 __device__ __forceinline__ void scale_row_bf16(unsigned char* box, int r, float s) {
   unsigned char* rowp = box + r * 128;
 #pragma unroll
@@ -186,14 +204,15 @@ __device__ __forceinline__ void warp_mma16(float (&d)[2][4], const float* X, int
   }
 }
 
-// T = (I + A)^-1 for strictly-lower A (fp32 [64][kLd]) by the 128 prep
-// threads.  The four 16x16 diagonal blocks are inverted by substitution
-// (threads 0-63, one column each; threads 64-127 meanwhile scale Q rows and
-// clear the upper blocks).  Off-diagonal blocks follow in order of distance d
-// from the diagonal, one warp per block, on the tensor cores (tf32 in, fp32
-// accumulate): T_ij = -T_ii (sum_{m=j}^{i-1} A_im T_mj).
-template <class Side>
-__device__ void invert_unit_lower64(const float* A, float* T, float* Z, int tid, Side&& side_work) {
+// T = (I + A)^-1 for strictly-lower A (fp32 [64][kLd]) by 128 threads.  The
+// four 16x16 diagonal blocks are inverted by substitution (threads 0-63, one
+// column each; threads 64-127 meanwhile clear the upper blocks).  Off-diagonal
+// blocks follow in order of distance d from the diagonal, one warp per block,
+// on the tensor cores (tf32 in, fp32 accumulate):
+// T_ij = -T_ii (sum_{m=j}^{i-1} A_im T_mj).  Warp w's 16x16 scratch is A's
+// block (0, w + 1), above the diagonal and never read as A.
+__device__ void invert_unit_lower64(float* A, float* T, int tid) {
+  const int warp = tid >> 5, lane = tid & 31;
   if (tid < 64) {
     const int d = tid >> 4, jj = tid & 15, j = 16 * d + jj;
     float col[16];
@@ -214,12 +233,10 @@ __device__ void invert_unit_lower64(const float* A, float* T, float* Z, int tid,
       const int bj = blk < 3 ? blk + 1 : (blk < 5 ? blk - 1 : 3);
       T[(16 * bi + ((e >> 4) & 15)) * kLd + 16 * bj + (e & 15)] = 0.f;
     }
-    side_work(tid - 64);
   }
   named_bar_sync(kBarPrep, 128);
-  const int warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, tg = lane & 3;
-  float* zw = Z + warp * 16 * 17;  // warp-private 16x16 (row stride 17)
+  float* zw = A + 16 * (warp + 1);  // warp-private 16x16 (row stride kLd)
 #pragma unroll
   for (int dist = 1; dist < 4; ++dist) {
     if (warp < 4 - dist) {
@@ -229,14 +246,14 @@ __device__ void invert_unit_lower64(const float* A, float* T, float* Z, int tid,
         warp_mma16(acc, A + (16 * bi) * kLd + 16 * mb, kLd, T + (16 * mb) * kLd + 16 * bj, kLd, lane);
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt) {
-        zw[g * 17 + 8 * nt + 2 * tg] = acc[nt][0];
-        zw[g * 17 + 8 * nt + 2 * tg + 1] = acc[nt][1];
-        zw[(g + 8) * 17 + 8 * nt + 2 * tg] = acc[nt][2];
-        zw[(g + 8) * 17 + 8 * nt + 2 * tg + 1] = acc[nt][3];
+        zw[g * kLd + 8 * nt + 2 * tg] = acc[nt][0];
+        zw[g * kLd + 8 * nt + 2 * tg + 1] = acc[nt][1];
+        zw[(g + 8) * kLd + 8 * nt + 2 * tg] = acc[nt][2];
+        zw[(g + 8) * kLd + 8 * nt + 2 * tg + 1] = acc[nt][3];
       }
       __syncwarp();
       float tt[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-      warp_mma16(tt, T + (16 * bi) * kLd + 16 * bi, kLd, zw, 17, lane);
+      warp_mma16(tt, T + (16 * bi) * kLd + 16 * bi, kLd, zw, kLd, lane);
       float* out = T + (16 * bi) * kLd + 16 * bj;
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt) {
@@ -251,38 +268,303 @@ __device__ void invert_unit_lower64(const float* A, float* T, float* Z, int tid,
   }
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
-    gdn_prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
-                       const PrefillParams p) {
+struct PrepParams {
+  const float* g;  // [B][T][Hv] log decay
+  const float* beta;
+  int64_t gs_b, gs_t;
+  unsigned char* ws;  // records [B][Hv][nblk]
+  int T;
+  int Hv;
+  int group;  // value heads per key head
+  int c0;     // first chunk of this block
+  int nblk;   // records per (sequence, head) in the workspace
+  unsigned int* err;
+};
+
+__global__ void __launch_bounds__(128, 3)
+    gdn_chunk_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                          const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmW,
+                          const PrepParams p) {
+  extern __shared__ __align__(1024) unsigned char smem[];
+  const int cl = blockIdx.x;
+  const int c = p.c0 + cl;
+  const int h = blockIdx.y;
+  const int b = blockIdx.z;
+  const int hk = h / p.group;
+  const int lt = threadIdx.x;
+  const int warp = lt >> 5;
+  uint64_t* tma_qk = reinterpret_cast<uint64_t*>(smem + kPBar);
+  uint64_t* tma_v = tma_qk + 1;
+  uint64_t* mma = tma_qk + 2;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + kPBar + 24);
+  float* gam = reinterpret_cast<float*>(smem + kPGam);  // gamma * log2(e)
+  float* bet = reinterpret_cast<float*>(smem + kPBet);
+  float* sq = reinterpret_cast<float*>(smem + kPSq);
+  float* sk = reinterpret_cast<float*>(smem + kPSk);
+  float* graw = reinterpret_cast<float*>(smem + kPGraw);
+  float* ebk = reinterpret_cast<float*>(smem + kPEbk);  // beta e^gamma s_k per column
+  const uint32_t sbase = smem_u32(smem);
+  const int64_t rec_idx = static_cast<int64_t>(b * p.Hv + h) * p.nblk + cl;
+  unsigned char* rec = p.ws + rec_idx * static_cast<int64_t>(kRecBytes);
+  const int32_t rec_row = static_cast<int32_t>(rec_idx * kRecRows);
+
+  if (lt == 0) {
+    prefetch_tmap(&tmQ);
+    prefetch_tmap(&tmK);
+    prefetch_tmap(&tmV);
+    prefetch_tmap(&tmW);
+    mbar_init(tma_qk, 1);
+    mbar_init(tma_v, 1);
+    mbar_init(mma, 1);
+    mbar_fence_init();
+    mbar_arrive_expect_tx(tma_qk, 4 * kBox);
+    tma_load_3d(smem + kPX, &tmQ, hk * kDK, c * kC, b, tma_qk);
+    tma_load_3d(smem + kPX + kBox, &tmK, hk * kDK, c * kC, b, tma_qk);
+    tma_load_3d(smem + kPY, &tmQ, hk * kDK + 64, c * kC, b, tma_qk);
+    tma_load_3d(smem + kPY + kBox, &tmK, hk * kDK + 64, c * kC, b, tma_qk);
+  }
+  if (warp == 0) {
+    tc::tmem_alloc(tslot, 128);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tm = *tslot;
+  const uint32_t my_lane = tm + (static_cast<uint32_t>(warp * 32) << 16);
+  constexpr uint32_t kTmG = 0, kTmW = 64, kTmU = 0;  // U^T reuses G's columns
+
+  // gates: inclusive scan of the chunk's log decays inside each of the two warps
+  float gscan = 0.f, bv = 0.f;
+  if (lt < kC) {
+    const int t = c * kC + lt;
+    const bool ok = t < p.T;
+    const int64_t gi = static_cast<int64_t>(b) * p.gs_b + static_cast<int64_t>(t) * p.gs_t + h;
+    gscan = ok ? p.g[gi] : 0.f;
+    bv = ok ? p.beta[gi] : 0.f;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float up = __shfl_up_sync(0xffffffffu, gscan, o);
+      if ((lt & 31) >= o) gscan += up;
+    }
+    if (lt == 31) graw[0] = gscan;  // warp 0 total
+  }
+  mbar_wait_bounded(tma_qk, 0, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
+  // ---- G = [Q;K] K^T (raw q, k) runs while the gates and norms are formed
+  if (lt == 0) {
+    tc::fence_after_sync();
+    const uint32_t id = tc::idesc_bf16(128, 64, false, false);
+    for (int ks = 0; ks < 8; ++ks) {
+      const uint32_t kb = sbase + (ks < 4 ? kPX : kPY) + (ks & 3) * 32;
+      tc::mma_bf16(tm + kTmG, tc::sdesc_sw128(kb, 16, 1024), tc::sdesc_sw128(kb + kBox, 16, 1024), id, ks > 0);
+    }
+    tc::commit(mma);
+  }
+  named_bar_sync(kBarPrep, 128);
+  if (lt < kC) {
+    gam[lt] = (lt >= 32 ? gscan + graw[0] : gscan) * kLog2e;
+    bet[lt] = bv;
+  }
+  {
+    const int r = lt & 63;
+    const uint32_t off = lt >= 64 ? kBox : 0;
+    const float rn = rsqrtf(sumsq_row(smem + kPX + off, smem + kPY + off, r) + 1e-6f);
+    if (lt < 64) sq[r] = rn; else sk[r] = rn;
+  }
+  named_bar_sync(kBarPrep, 128);
+  mbar_wait_bounded(mma, 0, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
+  tc::fence_after_sync();
+  if (lt < kC) ebk[lt] = bet[lt] * exp2f(gam[lt]) * sk[lt];
+
+  // ---- P rows (lanes 0-63) staged over the Q box, A rows (lanes 64-127) to
+  // SMEM.  Rows 0-31 have no entries in columns 32-63 (causal), so warps 0
+  // and 2 skip them.
+  {
+    float v[64];
+    tc::ld32(my_lane + kTmG, v);
+    tc::ld32(my_lane + kTmG + 32, v + 32);
+    tc::wait_ld();
+    const bool upper = (lt & 32) != 0;
+    if (lt < 64) {
+      const int i = lt;
+      const float gi = gam[i], si = sq[i] * kQScale;
+#pragma unroll
+      for (int j = 0; j < 64; ++j) {
+        if (j < 32 || upper) {
+          const float val = v[j] * si * sk[j] * exp2f(gi - gam[j]);
+          v[j] = (j <= i) ? val : 0.f;
+        } else {
+          v[j] = 0.f;
+        }
+      }
+      store_row_bf16<64>(smem + kPX, i, 0, v);
+    } else {
+      const int i = lt - 64;
+      const float gi = gam[i], bi = bet[i] * sk[i];
+      float* A = reinterpret_cast<float*>(smem + kPA);
+#pragma unroll
+      for (int j = 0; j < 64; ++j) {
+        float val = 0.f;
+        if (j < 32 || upper) val = bi * v[j] * sk[j] * exp2f(gi - gam[j]);
+        A[i * kLd + j] = (j < i) ? val : 0.f;
+      }
+    }
+  }
+  fence_proxy_async_smem();
+  tc::fence_before_sync();
+  named_bar_sync(kBarPrep, 128);  // G consumed, A complete, P staged
+  // P to the record; once the store has read the staging tile, V comes in
+  // over the Q boxes (dims 0-63 over X, 64-127 over Y).  Thread 64 issues it:
+  // threads 0-63 run the diagonal-block substitution meanwhile.
+  if (lt == 64) {
+    tma_store_2d(&tmW, smem + kPX, 0, rec_row + 256);
+    bulk_commit_group();
+    bulk_wait_read0();
+    mbar_arrive_expect_tx(tma_v, 2 * kBox);
+    tma_load_3d(smem + kPX, &tmV, h * kDV, c * kC, b, tma_v);
+    tma_load_3d(smem + kPY, &tmV, h * kDV + 64, c * kC, b, tma_v);
+  }
+  invert_unit_lower64(reinterpret_cast<float*>(smem + kPA), reinterpret_cast<float*>(smem + kPT), lt);
+  {
+    const int i = lt & 63;
+    const float* T = reinterpret_cast<const float*>(smem + kPT);
+    float v[64];
+    if (lt < 64) {
+#pragma unroll
+      for (int j = 0; j < 64; ++j) v[j] = T[i * kLd + j] * ebk[j];
+      store_row_bf16<64>(smem + kPA, i, 0, v);  // TW
+    } else {
+#pragma unroll
+      for (int j = 0; j < 64; ++j) v[j] = T[i * kLd + j] * bet[j];
+      store_row_bf16<64>(smem + kPA + kBox, i, 0, v);  // TU
+    }
+  }
+  fence_proxy_async_smem();
+  tc::fence_before_sync();
+  named_bar_sync(kBarPrep, 128);
+  tc::fence_after_sync();
+
+  // ---- W^T = K^T TW^T, U^T = V^T TU^T (A operands MN-major from the TMA tiles)
+  mbar_wait_bounded(tma_v, 0, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
+  if (lt == 0) {
+    tc::fence_after_sync();
+    const uint32_t id = tc::idesc_bf16(128, 64, true, false);
+    for (int ks = 0; ks < 4; ++ks)
+      tc::mma_bf16(tm + kTmW, tc::sdesc_sw128(sbase + kPX + kBox + ks * 2048, kPY - kPX, 1024),
+                   tc::sdesc_sw128(sbase + kPA + ks * 32, 16, 1024), id, ks > 0);
+    for (int ks = 0; ks < 4; ++ks)
+      tc::mma_bf16(tm + kTmU, tc::sdesc_sw128(sbase + kPX + ks * 2048, kPY - kPX, 1024),
+                   tc::sdesc_sw128(sbase + kPA + kBox + ks * 32, 16, 1024), id, ks > 0);
+    tc::commit(mma);
+  }
+  {
+    float* scal = reinterpret_cast<float*>(rec + kRecScal);
+    const float gC = gam[kC - 1];
+    if (lt < kC) {
+      scal[4 + lt] = sk[lt] * exp2f(gC - gam[lt]);
+      scal[68 + lt] = exp2f(gam[lt]) * sq[lt] * kQScale;
+    }
+    if (lt < 4) scal[lt] = lt == 0 ? exp2f(gC) : 0.f;
+  }
+  mbar_wait_bounded(mma, 1, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
+  tc::fence_after_sync();
+  {  // W^T (row = dk) and U^T (row = dv) staged over TW|TU and T, then TMA-stored
+    float v[64];
+    tc::ld32(my_lane + kTmW, v);
+    tc::ld32(my_lane + kTmW + 32, v + 32);
+    tc::wait_ld();
+    store_row_bf16<64>(smem + kPA, lt, 0, v);
+    tc::ld32(my_lane + kTmU, v);
+    tc::ld32(my_lane + kTmU + 32, v + 32);
+    tc::wait_ld();
+    store_row_bf16<64>(smem + kPT, lt, 0, v);
+  }
+  fence_proxy_async_smem();
+  tc::fence_before_sync();
+  __syncthreads();
+  if (lt == 0) {
+    tma_store_2d(&tmW, smem + kPA, 0, rec_row);
+    tma_store_2d(&tmW, smem + kPA + kBox, 0, rec_row + 64);
+    tma_store_2d(&tmW, smem + kPT, 0, rec_row + 128);
+    tma_store_2d(&tmW, smem + kPT + kBox, 0, rec_row + 192);
+    bulk_commit_group();
+    bulk_wait_all0();
+  }
+  if (lt == 64) bulk_wait_all0();  // the P store
+  if (warp == 0) tc::tmem_dealloc(tm, 128);
+}
+
+struct RecParams {
+  const unsigned char* ws;
+  const float* init_state;  // [B][Hv][128 k][128 v] or null (zeros)
+  float* final_state;
+  int T;
+  int Hv;
+  int group;
+  int c0;
+  int nblk;
+  unsigned int* err;
+};
+
+__device__ __forceinline__ void pack16(const float* v, uint32_t* pk) {
+#pragma unroll
+  for (int j = 0; j < 16; ++j) pk[j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
+}
+
+__global__ void __launch_bounds__(256, 1)
+    gdn_chunk_recurrence_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                                const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmO,
+                                const RecParams p) {
   extern __shared__ __align__(1024) unsigned char smem[];
   const int h = blockIdx.x;
   const int b = blockIdx.y;
   const int hk = h / p.group;
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
-  const int wg = tid >> 7;    // 0: prep, 1: recurrence
-  const int lt = tid & 127;   // thread index inside the warpgroup == TMEM lane
-  uint64_t* tma_bar = reinterpret_cast<uint64_t*>(smem + kOffBar);
-  uint64_t* full_bar = tma_bar + 2;
-  uint64_t* mma_p = tma_bar + 6;
-  uint64_t* mma_r = tma_bar + 7;
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + kOffTslot);
+  const int wg = tid >> 7;   // column half handled by this warpgroup
+  const int lt = tid & 127;  // TMEM lane = dv
+  const int lane = tid & 31;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kRBar);
+  uint64_t* bar_x = full + kSlots;
+  uint64_t* bar_s = bar_x + 1;
+  uint64_t* bar_o = bar_x + 2;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bar_x + 3);
   const uint32_t sbase = smem_u32(smem);
   const int nchunks = (p.T + kC - 1) / kC;
+  const int n = min(p.nblk, nchunks - p.c0);
+  const int64_t rec0 = static_cast<int64_t>(b * p.Hv + h) * p.nblk;
+  constexpr int kStoreTid = 128;  // issues output stores and refills (warp 4)
+
+  // TMA of block-local chunk j's operands into slot j % 3 (one thread).
+  auto issue = [&](int j) {
+    const int s = j % kSlots;
+    unsigned char* slot = smem + s * kSlotBytes;
+    const int c = p.c0 + j;
+    const int32_t row = static_cast<int32_t>((rec0 + j) * kRecRows);
+    mbar_arrive_expect_tx(&full[s], kChunkTx);
+    tma_load_3d(slot + kSlQ, &tmQ, hk * kDK, c * kC, b, &full[s]);
+    tma_load_3d(slot + kSlQ + kBox, &tmQ, hk * kDK + 64, c * kC, b, &full[s]);
+    tma_load_3d(slot + kSlK, &tmK, hk * kDK, c * kC, b, &full[s]);
+    tma_load_3d(slot + kSlK + kBox, &tmK, hk * kDK + 64, c * kC, b, &full[s]);
+    tma_load_2d(slot + kSlWT, &tmW, 0, row, &full[s]);
+    tma_load_2d(slot + kSlWT + kBox, &tmW, 0, row + 64, &full[s]);
+    tma_load_2d(slot + kSlUT, &tmW, 0, row + 128, &full[s]);
+    tma_load_2d(slot + kSlUT + kBox, &tmW, 0, row + 192, &full[s]);
+    tma_load_2d(slot + kSlP, &tmW, 0, row + 256, &full[s]);
+    bulk_g2s(slot + kSlScal, p.ws + (rec0 + j) * static_cast<int64_t>(kRecBytes) + kRecScal, kScalBytes, &full[s]);
+  };
 
   if (tid == 0) {
     prefetch_tmap(&tmQ);
     prefetch_tmap(&tmK);
-    prefetch_tmap(&tmV);
+    prefetch_tmap(&tmW);
     prefetch_tmap(&tmO);
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&tma_bar[i], 1);
-      mbar_init(&full_bar[i], 128);
-    }
-    mbar_init(mma_p, 1);
-    mbar_init(mma_r, 1);
+    for (int i = 0; i < kSlots; ++i) mbar_init(&full[i], 1);
+    mbar_init(bar_x, 1);
+    mbar_init(bar_s, 1);
+    mbar_init(bar_o, 1);
     mbar_fence_init();
+    for (int j = 0; j < min(n, kSlots); ++j) issue(j);
   }
   if (warp == 0) {
     tc::tmem_alloc(tslot, 512);
@@ -292,311 +574,177 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tm = *tslot;
-  const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
-  const uint32_t my_lane = tm + lane_base;
+  const uint32_t my_lane = tm + (static_cast<uint32_t>((warp & 3) * 32) << 16);
 
-  // TMA of chunk c's Q/K/V tiles into slot c & 1 (issued by one thread).
-  auto issue_chunk = [&](int c) {
-    const int s = c & 1;
-    unsigned char* slot = smem + kOffSlot0 + s * kSlotBytes;
-    mbar_arrive_expect_tx(&tma_bar[s], 6 * kBox);
-    tma_load_3d(slot + kSlX, &tmQ, hk * kDK, c * kC, b, &tma_bar[s]);
-    tma_load_3d(slot + kSlX + kBox, &tmK, hk * kDK, c * kC, b, &tma_bar[s]);
-    tma_load_3d(slot + kSlY, &tmQ, hk * kDK + 64, c * kC, b, &tma_bar[s]);
-    tma_load_3d(slot + kSlY + kBox, &tmK, hk * kDK + 64, c * kC, b, &tma_bar[s]);
-    tma_load_3d(slot + kSlV, &tmV, h * kDV, c * kC, b, &tma_bar[s]);
-    tma_load_3d(slot + kSlV + kBox, &tmV, h * kDV + 64, c * kC, b, &tma_bar[s]);
-  };
-  auto load_gates = [&](int c, float& gv, float& bv) {
-    const int t = c * kC + lt;
-    const bool ok = t < p.T;
-    const int64_t gi = static_cast<int64_t>(b) * p.gs_b + static_cast<int64_t>(t) * p.gs_t + h;
-    gv = ok ? p.g[gi] : 0.f;
-    bv = ok ? p.beta[gi] : 0.f;
-  };
-
-  if (wg == 0) {
-    // =================================================================== prep
-    float* graw = reinterpret_cast<float*>(smem + kOffGraw);
-    float* gam = reinterpret_cast<float*>(smem + kOffGam);
-    float* bet = reinterpret_cast<float*>(smem + kOffBet);
-    float* sq = reinterpret_cast<float*>(smem + kOffSq);
-    float* sk = reinterpret_cast<float*>(smem + kOffSk);
-    uint32_t ph_p = 0;
-    if (lt == 0) {
-      issue_chunk(0);
-      if (nchunks > 1) issue_chunk(1);
+  {  // initial state: warpgroup wg loads dk columns [64 wg, 64 wg + 64)
+    const float* s0 = p.init_state ? p.init_state + static_cast<int64_t>(b * p.Hv + h) * kDK * kDV : nullptr;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int k0 = 64 * wg + 32 * half;
+      float v[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = s0 ? s0[(k0 + i) * kDV + lt] : 0.f;
+      tc::st32(my_lane + kTS + k0, v);
     }
-    float g_next = 0.f, b_next = 0.f;
-    if (lt < kC) load_gates(0, g_next, b_next);
-    for (int c = 0; c < nchunks; ++c) {
-      const int s = c & 1;
-      unsigned char* slot = smem + kOffSlot0 + s * kSlotBytes;
-      const uint32_t aslot = sbase + kOffSlot0 + s * kSlotBytes;
-      float gscan = 0.f;
-      if (lt < kC) {
-        // inclusive scan of the chunk's log decays inside each of the two warps
-        gscan = g_next;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const float up = __shfl_up_sync(0xffffffffu, gscan, o);
-          if ((lt & 31) >= o) gscan += up;
-        }
-        if (lt == 31) graw[0] = gscan;  // warp 0 total
-        bet[lt] = b_next;
-        if (c + 1 < nchunks) load_gates(c + 1, g_next, b_next);  // in flight during this chunk
-      }
-      mbar_wait_bounded(&tma_bar[s], (c >> 1) & 1, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
-      // ---- G = [Q;K] K^T (raw q, k) runs while the gates and norms are formed
-      if (lt == 0) {
-        tc::fence_after_sync();
-        const uint32_t id = tc::idesc_bf16(128, 64, false, false);
-        for (int ks = 0; ks < 8; ++ks) {
-          const uint32_t kb = aslot + (ks < 4 ? kSlX : kSlY) + (ks & 3) * 32;
-          tc::mma_bf16(tm + kTmG, tc::sdesc_sw128(kb, 16, 1024), tc::sdesc_sw128(kb + kBox, 16, 1024), id, ks > 0);
-        }
-        tc::commit(mma_p);
-      }
-      named_bar_sync(kBarPrep, 128);
-      if (lt < kC) gam[lt] = (lt >= 32 ? gscan + graw[0] : gscan) * kLog2e;
-      {
-        const int r = lt & 63;
-        const uint32_t off = lt >= 64 ? kBox : 0;
-        const float rn = rsqrtf(sumsq_row(slot + kSlX + off, slot + kSlY + off, r) + 1e-6f);
-        if (lt < 64) sq[r] = rn; else sk[r] = rn;
-      }
-      named_bar_sync(kBarPrep, 128);
+    tc::wait_st();
+  }
 
-      mbar_wait_bounded(mma_p, ph_p, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
-      ph_p ^= 1u;
-      tc::fence_after_sync();
-
-      // ---- P rows (lanes 0-63), A rows (lanes 64-127); then Q rows scaled in place
-      {
-        float v[64];
-        tc::ld32(my_lane + kTmG, v);
-        tc::ld32(my_lane + kTmG + 32, v + 32);
-        tc::wait_ld();
-        if (lt < 64) {
-          const int i = lt;
-          const float gi = gam[i], si = sq[i] * kQScale;
+  // Output of block-local chunk j, step 1 (all threads): O^T (lane = dv) from
+  // TMEM buffer j & 1 into a [64 tokens][128 dv] bf16 staging tile (two
+  // 128-byte-swizzled 64-dv boxes) in the W^T region of chunk j's slot, whose
+  // MMAs are then all complete.  Lane pairs swap halves so that every SMEM
+  // store is a bf16 pair.
+  auto stage_output = [&](int j) {
+    mbar_wait_bounded(bar_o, j & 1, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
+    tc::fence_after_sync();
+    float o[32];
+    tc::ld32(my_lane + kTO + 64 * (j & 1) + 32 * wg, o);
+    tc::wait_ld();
+    unsigned char* stg = smem + (j % kSlots) * kSlotBytes + kSlWT + (lt >> 6) * kBox;
+    const bool odd = lane & 1;
+    const int col = (lt & 63) & ~1;
 #pragma unroll
-          for (int j = 0; j < 64; ++j) {
-            const float val = v[j] * si * sk[j] * exp2f(gi - gam[j]);
-            v[j] = (j <= i) ? val : 0.f;
-          }
-          store_row_bf16<64>(slot + kSlP, i, 0, v);
-        } else {
-          const int i = lt - 64;
-          const float gi = gam[i], bi = bet[i] * sk[i];
-          float* A = reinterpret_cast<float*>(smem + kOffAT);
-#pragma unroll
-          for (int j = 0; j < 64; ++j) {
-            const float val = bi * v[j] * sk[j] * exp2f(gi - gam[j]);
-            A[i * kLd + j] = (j < i) ? val : 0.f;
-          }
-        }
-      }
-      tc::fence_before_sync();
-      named_bar_sync(kBarPrep, 128);  // G consumed, A complete
-      // Qr = diag(e^gamma s_q 128^-0.5) Q (both 64-dim boxes of row r), done by
-      // the threads idle during the diagonal-block substitution
-      invert_unit_lower64(reinterpret_cast<const float*>(smem + kOffAT), reinterpret_cast<float*>(smem + kOffTf),
-                          reinterpret_cast<float*>(smem + kOffZ), lt, [&](int r) {
-                            const float sc = exp2f(gam[r]) * sq[r] * kQScale;
-                            scale_row_bf16(slot + kSlX, r, sc);
-                            scale_row_bf16(slot + kSlY, r, sc);
-                          });
-      {
-        const int i = lt & 63;
-        const float* T = reinterpret_cast<const float*>(smem + kOffTf);
-        float v[64];
-        if (lt < 64) {
-#pragma unroll
-          for (int j = 0; j < 64; ++j) v[j] = T[i * kLd + j] * bet[j] * exp2f(gam[j]) * sk[j];
-          store_row_bf16<64>(smem + kOffAT, i, 0, v);  // TW
-        } else {
-#pragma unroll
-          for (int j = 0; j < 64; ++j) v[j] = T[i * kLd + j] * bet[j];
-          store_row_bf16<64>(smem + kOffAT + kBox, i, 0, v);  // TU
-        }
-      }
-      fence_proxy_async_smem();
-      tc::fence_before_sync();
-      named_bar_sync(kBarPrep, 128);
-      tc::fence_after_sync();
-
-      // ---- W^T = K^T TW^T, U^T = V^T TU^T (A operands MN-major from the TMA tiles)
-      if (lt == 0) {
-        tc::fence_after_sync();
-        const uint32_t id = tc::idesc_bf16(128, 64, true, false);
-        for (int ks = 0; ks < 4; ++ks)
-          tc::mma_bf16(tm + kTmWT, tc::sdesc_sw128(aslot + kSlX + kBox + ks * 2048, kSlY - kSlX, 1024),
-                       tc::sdesc_sw128(sbase + kOffAT + ks * 32, 16, 1024), id, ks > 0);
-        for (int ks = 0; ks < 4; ++ks)
-          tc::mma_bf16(tm + kTmUT, tc::sdesc_sw128(aslot + kSlV + ks * 2048, kBox, 1024),
-                       tc::sdesc_sw128(sbase + kOffAT + kBox + ks * 32, 16, 1024), id, ks > 0);
-        tc::commit(mma_p);
-      }
-      mbar_wait_bounded(mma_p, ph_p, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
-      ph_p ^= 1u;
-      tc::fence_after_sync();
-      {
-        float v[64];
-        tc::ld32(my_lane + kTmWT, v);
-        tc::ld32(my_lane + kTmWT + 32, v + 32);
-        tc::wait_ld();
-        store_row_bf16<64>(slot + kSlWT, lt, 0, v);  // row = dk
-        tc::ld32(my_lane + kTmUT, v);
-        tc::ld32(my_lane + kTmUT + 32, v + 32);
-        tc::wait_ld();
-        store_row_bf16<64>(slot + kSlV, lt, 0, v);  // U^T row = dv (V tile is consumed)
-      }
-      {
-        float* scal = reinterpret_cast<float*>(slot + kSlScal);
-        const float gC = gam[kC - 1];
-        if (lt < kC) scal[4 + lt] = sk[lt] * exp2f(gC - gam[lt]);
-        if (lt == 0) scal[0] = exp2f(gC);
-      }
-      fence_proxy_async_smem();
-      tc::fence_before_sync();
-      mbar_arrive(&full_bar[s]);
-      // prep-private SMEM (gates, A/T scratch) is rewritten next chunk only
-      // after this barrier
-      named_bar_sync(kBarPrep, 128);
+    for (int i = 0; i < 16; ++i) {
+      const float send = odd ? o[2 * i] : o[2 * i + 1];
+      const float recv = __shfl_xor_sync(0xffffffffu, send, 1);
+      const int t = 32 * wg + 2 * i + (odd ? 1 : 0);
+      const uint32_t pk = odd ? pack_bf16x2(recv, o[2 * i + 1]) : pack_bf16x2(o[2 * i], recv);
+      *reinterpret_cast<uint32_t*>(stg + tc::sw128_off(t, col)) = pk;
     }
-  } else {
-    // =================================================================== recurrence
+    fence_proxy_async_smem();
+  };
+  // Step 2 (one thread, after a barrier): TMA tensor stores of the staging
+  // tile (rows past the prompt end are clipped by the tensor map); once the
+  // stores have read it, the slot is refilled with chunk j + 3.
+  auto store_output = [&](int j) {
+    const unsigned char* stg = smem + (j % kSlots) * kSlotBytes + kSlWT;
+    const int c = p.c0 + j;
+    tma_store_3d(&tmO, stg, h * kDV, c * kC, b);
+    tma_store_3d(&tmO, stg + kBox, h * kDV + 64, c * kC, b);
+    bulk_commit_group();
+    bulk_wait_read0();
+    if (j + kSlots < n) issue(j + kSlots);
+  };
+
+  for (int j = 0; j < n; ++j) {
+    const int s = j % kSlots;
+    unsigned char* slot = smem + s * kSlotBytes;
+    const uint32_t aslot = sbase + s * kSlotBytes;
+    const float* scal = reinterpret_cast<const float*>(slot + kSlScal);
+    const uint32_t sb = kTSb + 64 * (j & 1);  // this chunk's bf16 S^T buffer
+    mbar_wait_bounded(&full[s], (j / kSlots) & 1, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
+    const float eC = scal[0];
+
+    // ---- bf16 S^T into TMEM (A operand of X and O), S^T *= e^gamma_C; Q rows -> Qr
     {
-      const float* s0 = p.init_state ? p.init_state + (static_cast<int64_t>(b) * p.Hv + h) * kDK * kDV : nullptr;
-      for (int k0 = 0; k0 < kDK; k0 += 32) {
-        float v[32];
+      const int k0 = 64 * wg;
+      float v[64];
+      uint32_t pk[16];
+      tc::ld32(my_lane + kTS + k0, v);
+      tc::ld32(my_lane + kTS + k0 + 32, v + 32);
+      tc::wait_ld();
+      pack16(v, pk);
+      tc::st16(my_lane + sb + k0 / 2, pk);
+      pack16(v + 32, pk);
+      tc::st16(my_lane + sb + k0 / 2 + 16, pk);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = s0 ? s0[(k0 + i) * kDV + lt] : 0.f;
-        tc::st32(my_lane + kTmS + k0, v);
+      for (int i = 0; i < 64; ++i) v[i] *= eC;
+      tc::st32(my_lane + kTS + k0, v);
+      tc::st32(my_lane + kTS + k0 + 32, v + 32);
+    }
+    {  // Qr = diag(output scale) Q: thread -> (row, 64-dim box, half of the row)
+      const int r = tid & 63;
+      unsigned char* rowp = slot + kSlQ + ((tid >> 6) & 1) * kBox + r * 128;
+      const float sc = scal[68 + r];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int ch = (4 * (tid >> 7) + c) ^ (r & 7);
+        uint4 u = *reinterpret_cast<uint4*>(rowp + ch * 16);
+        __nv_bfloat162* h2 = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(h2[e]);
+          h2[e] = __floats2bfloat162_rn(f.x * sc, f.y * sc);
+        }
+        *reinterpret_cast<uint4*>(rowp + ch * 16) = u;
       }
+    }
+    tc::wait_st();
+    fence_proxy_async_smem();
+    tc::fence_before_sync();
+    __syncthreads();
+
+    // ---- X = S^T W^T; meanwhile the previous chunk's output goes to staging
+    if (tid == 0) {
+      tc::fence_after_sync();
+      const uint32_t idX = tc::idesc_bf16(128, 64, false, true);
+      for (int ks = 0; ks < 8; ++ks)
+        tc::mma_bf16_ts(tm + kTX, tm + sb + ks * 8, tc::sdesc_sw128(aslot + kSlWT + ks * 2048, kBox, 1024), idX,
+                        ks > 0);
+      tc::commit(bar_x);
+    }
+    if (j > 0) stage_output(j - 1);
+
+    // ---- V'^T = U^T - X: raw (for O) and column-scaled (for the state), bf16 into TMEM
+    mbar_wait_bounded(bar_x, j & 1, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
+    tc::fence_after_sync();
+    {
+      float x[32], u[32];
+      uint32_t pk[16];
+      tc::ld32(my_lane + kTX + 32 * wg, x);
+      load_row_bf16<32>(slot + kSlUT, lt, 32 * wg, u);
+      tc::wait_ld();
+#pragma unroll
+      for (int i = 0; i < 32; ++i) u[i] -= x[i];
+      pack16(u, pk);
+      tc::st16(my_lane + kTV + 16 * wg, pk);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) u[i] *= scal[4 + 32 * wg + i];
+      pack16(u, pk);
+      tc::st16(my_lane + kTVs + 16 * wg, pk);
       tc::wait_st();
     }
-    uint32_t ph_r = 0;
-    for (int c = 0; c < nchunks; ++c) {
-      const int s = c & 1;
-      unsigned char* slot = smem + kOffSlot0 + s * kSlotBytes;
-      const uint32_t aslot = sbase + kOffSlot0 + s * kSlotBytes;
-      const float* scal = reinterpret_cast<const float*>(slot + kSlScal);
-      mbar_wait_bounded(&full_bar[s], (c >> 1) & 1, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
-      tc::fence_after_sync();
-      const float eC = scal[0];
-      // the previous chunk's output store must have read the staging tile
-      // (it shares SMEM with the bf16 state written next)
-      if (lt == 0) bulk_wait_read0();
-      named_bar_sync(kBarRec, 128);
+    tc::fence_before_sync();
+    __syncthreads();
 
-      // ---- bf16(S_c) -> SMEM, S^T *= e^gamma_C in TMEM
-      for (int k0 = 0; k0 < kDK; k0 += 32) {
-        float v[32];
-        tc::ld32(my_lane + kTmS + k0, v);
-        tc::wait_ld();
-        store_row_bf16<32>(smem + kOffST + (k0 >> 6) * (2 * kBox), lt, k0 & 63, v);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] *= eC;
-        tc::st32(my_lane + kTmS + k0, v);
-      }
-      tc::wait_st();
-      fence_proxy_async_smem();
-      tc::fence_before_sync();
-      named_bar_sync(kBarRec, 128);
+    // ---- S^T += V's^T K first (the next chunk waits only for it), then
+    // O = S^T Qr^T + V'^T P^T from the old S^T's bf16 copy
+    if (tid == 0) {
       tc::fence_after_sync();
-
-      // ---- X = S^T W^T and O = S^T Qr^T
-      if (lt == 0) {
-        const uint32_t idX = tc::idesc_bf16(128, 64, false, true);
-        const uint32_t idO = tc::idesc_bf16(128, 64, false, false);
-        for (int ks = 0; ks < 8; ++ks) {
-          const uint32_t sa = sbase + kOffST + (ks >> 2) * (2 * kBox) + (ks & 3) * 32;
-          tc::mma_bf16(tm + kTmX, tc::sdesc_sw128(sa, 16, 1024),
-                       tc::sdesc_sw128(aslot + kSlWT + ks * 2048, 2 * kBox, 1024), idX, ks > 0);
-          const uint32_t qb = aslot + (ks < 4 ? kSlX : kSlY) + (ks & 3) * 32;
-          tc::mma_bf16(tm + kTmO, tc::sdesc_sw128(sa, 16, 1024), tc::sdesc_sw128(qb, 16, 1024), idO, ks > 0);
-        }
-        tc::commit(mma_r);
-      }
-      mbar_wait_bounded(mma_r, ph_r, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
-      ph_r ^= 1u;
-      tc::fence_after_sync();
-
-      // ---- V'^T = U^T - X: raw for O, column-scaled for the state update
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        float u[32], x[32];
-        tc::ld32(my_lane + kTmX + 32 * half, x);
-        load_row_bf16<32>(slot + kSlV, lt, 32 * half, u);
-        tc::wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) u[i] -= x[i];
-        store_row_bf16<32>(smem + kOffST, lt, 32 * half, u);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) u[i] *= scal[4 + 32 * half + i];
-        store_row_bf16<32>(smem + kOffST + 2 * kBox, lt, 32 * half, u);
-      }
-      fence_proxy_async_smem();
-      tc::fence_before_sync();
-      named_bar_sync(kBarRec, 128);
-      tc::fence_after_sync();
-
-      // ---- O += V'^T P^T and S^T += V's^T K
-      if (lt == 0) {
-        const uint32_t idO = tc::idesc_bf16(128, 64, false, false);
-        for (int ks = 0; ks < 4; ++ks)
-          tc::mma_bf16(tm + kTmO, tc::sdesc_sw128(sbase + kOffST + ks * 32, 16, 1024),
-                       tc::sdesc_sw128(aslot + kSlP + ks * 32, 16, 1024), idO, true);
-        const uint32_t idS = tc::idesc_bf16(128, 128, false, true);
-        for (int ks = 0; ks < 4; ++ks)
-          tc::mma_bf16(tm + kTmS, tc::sdesc_sw128(sbase + kOffST + 2 * kBox + ks * 32, 16, 1024),
-                       tc::sdesc_sw128(aslot + kSlX + kBox + ks * 2048, kSlY - kSlX, 1024), idS, true);
-        tc::commit(mma_r);
-      }
-      mbar_wait_bounded(mma_r, ph_r, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
-      ph_r ^= 1u;
-      tc::fence_after_sync();
-      // every read of this slot is complete: refill it with chunk c + 2
-      if (lt == 0 && c + 2 < nchunks) issue_chunk(c + 2);
-
-      // ---- output: O^T (lane = dv) -> bf16 [64 tokens][128 dv] staging tile
-      // (two 64-dv boxes, 128-byte swizzled) -> one TMA tensor store per box;
-      // rows past the sequence end are clipped by the tensor map.
-      {
-        unsigned char* stg = smem + kOffST;
-        unsigned char* box = stg + (lt >> 6) * kBox;
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          float o[32];
-          tc::ld32(my_lane + kTmO + 32 * half, o);
-          tc::wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            *reinterpret_cast<__nv_bfloat16*>(box + tc::sw128_off(32 * half + i, lt & 63)) = __float2bfloat16_rn(o[i]);
-        }
-        fence_proxy_async_smem();
-        tc::fence_before_sync();
-        named_bar_sync(kBarRec, 128);  // O, X and the V' tiles are free; staging is written
-        tc::fence_after_sync();
-        if (lt == 0) {
-          tma_store_3d(&tmO, stg, h * kDV, c * kC, b);
-          tma_store_3d(&tmO, stg + kBox, h * kDV + 64, c * kC, b);
-          bulk_commit_group();
-        }
-      }
+      const uint32_t idS = tc::idesc_bf16(128, 128, false, true);
+      for (int ks = 0; ks < 4; ++ks)
+        tc::mma_bf16_ts(tm + kTS, tm + kTVs + ks * 8, tc::sdesc_sw128(aslot + kSlK + ks * 2048, kBox, 1024), idS,
+                        true);
+      tc::commit(bar_s);
+      const uint32_t idO = tc::idesc_bf16(128, 64, false, false);
+      const uint32_t od = tm + kTO + 64 * (j & 1);
+      for (int ks = 0; ks < 8; ++ks)
+        tc::mma_bf16_ts(od, tm + sb + ks * 8,
+                        tc::sdesc_sw128(aslot + kSlQ + (ks >> 2) * kBox + (ks & 3) * 32, 16, 1024), idO, ks > 0);
+      for (int ks = 0; ks < 4; ++ks)
+        tc::mma_bf16_ts(od, tm + kTV + ks * 8, tc::sdesc_sw128(aslot + kSlP + ks * 32, 16, 1024), idO, true);
+      tc::commit(bar_o);
     }
-    if (lt == 0) bulk_wait_all0();
-    {
-      float* sf = p.final_state + (static_cast<int64_t>(b) * p.Hv + h) * kDK * kDV;
-      for (int k0 = 0; k0 < kDK; k0 += 32) {
-        float v[32];
-        tc::ld32(my_lane + kTmS + k0, v);
-        tc::wait_ld();
+    if (tid == kStoreTid && j > 0) store_output(j - 1);
+    mbar_wait_bounded(bar_s, j & 1, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
+    tc::fence_after_sync();
+  }
+  if (n > 0) {
+    stage_output(n - 1);
+    __syncthreads();
+    if (tid == kStoreTid) store_output(n - 1);
+  }
+  if (tid == kStoreTid) bulk_wait_all0();
+  {
+    float* sf = p.final_state + static_cast<int64_t>(b * p.Hv + h) * kDK * kDV;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) sf[(k0 + i) * kDV + lt] = v[i];
-      }
+    for (int half = 0; half < 2; ++half) {
+      const int k0 = 64 * wg + 32 * half;
+      float v[32];
+      tc::ld32(my_lane + kTS + k0, v);
+      tc::wait_ld();
+#pragma unroll
+      for (int i = 0; i < 32; ++i) sf[(k0 + i) * kDV + lt] = v[i];
     }
   }
   tc::fence_before_sync();
@@ -606,20 +754,26 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 }  // namespace
 
+extern "C" int64_t ria_gdn_chunk_prefill_workspace_bytes(int32_t batch, int32_t seq_len, int32_t num_v_heads) {
+  if (batch <= 0 || seq_len <= 0 || num_v_heads <= 0) return 0;
+  return static_cast<int64_t>(batch) * num_v_heads * ((seq_len + kC - 1) / kC) * kRecBytes;
+}
+
 extern "C" int ria_gdn_chunk_prefill(const void* q, int64_t q_stride_b, int64_t q_stride_t, const void* k,
                                      int64_t k_stride_b, int64_t k_stride_t, const void* v, int64_t v_stride_b,
                                      int64_t v_stride_t, const float* g, const float* beta, int64_t gb_stride_b,
                                      int64_t gb_stride_t, const float* initial_state, float* final_state, void* out,
-                                     int64_t o_stride_b, int64_t o_stride_t, int32_t batch, int32_t seq_len,
-                                     int32_t num_k_heads, int32_t num_v_heads, ria_stream_t stream) {
+                                     int64_t o_stride_b, int64_t o_stride_t, void* workspace, int64_t workspace_bytes,
+                                     int32_t batch, int32_t seq_len, int32_t num_k_heads, int32_t num_v_heads,
+                                     ria_stream_t stream) {
   if (batch < 0 || seq_len < 0) return ria::fail(RIA_ERR_INVALID, "ria_gdn_chunk_prefill: negative size");
   if (batch == 0 || seq_len == 0) return RIA_OK;
-  if (!q || !k || !v || !g || !beta || !final_state || !out)
+  if (!q || !k || !v || !g || !beta || !final_state || !out || !workspace)
     return ria::fail(RIA_ERR_INVALID, "ria_gdn_chunk_prefill: null pointer argument");
   if (num_k_heads < 1 || num_v_heads < num_k_heads || num_v_heads % num_k_heads)
     return ria::fail(RIA_ERR_INVALID, "ria_gdn_chunk_prefill: %d value heads do not group over %d key heads",
                      num_v_heads, num_k_heads);
-  if (batch > 65535) return ria::fail(RIA_ERR_INVALID, "ria_gdn_chunk_prefill: batch too large");
+  if (batch > 65535 || num_v_heads > 65535) return ria::fail(RIA_ERR_INVALID, "ria_gdn_chunk_prefill: grid too large");
   const int64_t qk_row = static_cast<int64_t>(num_k_heads) * kDK, v_row = static_cast<int64_t>(num_v_heads) * kDV;
   if (q_stride_t < qk_row || k_stride_t < qk_row || v_stride_t < v_row || o_stride_t < v_row ||
       gb_stride_t < num_v_heads)
@@ -627,8 +781,22 @@ extern "C" int ria_gdn_chunk_prefill(const void* q, int64_t q_stride_b, int64_t 
   if (!ria::aligned(q, 16) || !ria::aligned(k, 16) || !ria::aligned(v, 16) || (q_stride_t % 8) ||
       (k_stride_t % 8) || (v_stride_t % 8) || (q_stride_b % 8) || (k_stride_b % 8) || (v_stride_b % 8))
     return ria::fail(RIA_ERR_INVALID, "ria_gdn_chunk_prefill: q/k/v must be 16-byte aligned with 16-byte strides");
+  if (!ria::aligned(out, 16) || (o_stride_t % 8) || (o_stride_b % 8))
+    return ria::fail(RIA_ERR_INVALID, "ria_gdn_chunk_prefill: out must be 16-byte aligned with 16-byte strides");
+  if (!ria::aligned(workspace, 16))
+    return ria::fail(RIA_ERR_INVALID, "ria_gdn_chunk_prefill: workspace must be 16-byte aligned");
+  const int nchunks = (seq_len + kC - 1) / kC;
+  const size_t per_chunk = static_cast<size_t>(batch) * num_v_heads * kRecBytes;
+  // records per (sequence, head): as many chunks as the workspace holds, with
+  // the workspace's row count inside the tensor map's 32-bit coordinates
+  const size_t row_cap = static_cast<size_t>(INT32_MAX) / (static_cast<size_t>(batch) * num_v_heads * kRecRows);
+  const size_t ws = workspace_bytes > 0 ? static_cast<size_t>(workspace_bytes) : 0;
+  const int nblk = static_cast<int>(std::min<size_t>({static_cast<size_t>(nchunks), ws / per_chunk, row_cap}));
+  if (nblk < 1)
+    return ria::fail(RIA_ERR_INVALID, "ria_gdn_chunk_prefill: workspace of %zu bytes is below one chunk (%zu bytes)",
+                     ws, per_chunk);
 
-  CUtensorMap tmQ, tmK, tmV;
+  CUtensorMap tmQ, tmK, tmV, tmW, tmO;
   const uint32_t box[3] = {64, 64, 1};
   {
     const uint64_t dims[3] = {static_cast<uint64_t>(qk_row), static_cast<uint64_t>(seq_len),
@@ -647,36 +815,57 @@ extern "C" int ria_gdn_chunk_prefill(const void* q, int64_t q_stride_b, int64_t 
     int rc = ria::encode_bf16_sw128_map(&tmV, v, 3, dims, sv, box);
     if (rc) return rc;
   }
-
-  CUtensorMap tmO;
   {
-    if (!ria::aligned(out, 16) || (o_stride_t % 8) || (o_stride_b % 8))
-      return ria::fail(RIA_ERR_INVALID, "ria_gdn_chunk_prefill: out must be 16-byte aligned with 16-byte strides");
     const uint64_t dims[3] = {static_cast<uint64_t>(v_row), static_cast<uint64_t>(seq_len),
                               static_cast<uint64_t>(batch)};
     const uint64_t so[2] = {static_cast<uint64_t>(o_stride_t) * 2, static_cast<uint64_t>(o_stride_b) * 2};
     int rc = ria::encode_bf16_sw128_map(&tmO, out, 3, dims, so, box);
     if (rc) return rc;
   }
+  {
+    const uint64_t dims[2] = {64, static_cast<uint64_t>(batch) * num_v_heads * nblk * kRecRows};
+    const uint64_t sw[1] = {128};
+    int rc = ria::encode_bf16_sw128_map(&tmW, workspace, 2, dims, sw, box);
+    if (rc) return rc;
+  }
 
-  PrefillParams p;
-  p.g = g;
-  p.beta = beta;
-  p.gs_b = gb_stride_b;
-  p.gs_t = gb_stride_t;
-  p.init_state = initial_state;
-  p.final_state = final_state;
-  p.out = static_cast<__nv_bfloat16*>(out);
-  p.os_b = o_stride_b;
-  p.os_t = o_stride_t;
-  p.T = seq_len;
-  p.Hv = num_v_heads;
-  p.group = num_v_heads / num_k_heads;
-  p.err = ria::device_error_word();
+  PrepParams pp;
+  pp.g = g;
+  pp.beta = beta;
+  pp.gs_b = gb_stride_b;
+  pp.gs_t = gb_stride_t;
+  pp.ws = static_cast<unsigned char*>(workspace);
+  pp.T = seq_len;
+  pp.Hv = num_v_heads;
+  pp.group = num_v_heads / num_k_heads;
+  pp.nblk = nblk;
+  pp.err = ria::device_error_word();
+  RecParams rp;
+  rp.ws = static_cast<const unsigned char*>(workspace);
+  rp.final_state = final_state;
+  rp.T = seq_len;
+  rp.Hv = num_v_heads;
+  rp.group = pp.group;
+  rp.nblk = nblk;
+  rp.err = pp.err;
 
-  cudaError_t e = cudaFuncSetAttribute(gdn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  cudaError_t e = cudaFuncSetAttribute(gdn_chunk_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(gdn_chunk_recurrence_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRSmem);
   if (e != cudaSuccess) return ria::fail(RIA_ERR_CUDA, "ria_gdn_chunk_prefill: smem attribute: %s", cudaGetErrorString(e));
-  gdn_prefill_kernel<<<dim3(num_v_heads, batch), kThreads, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(tmQ, tmK,
-                                                                                                          tmV, tmO, p);
-  return ria::check_launch("ria_gdn_chunk_prefill");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  for (int c0 = 0; c0 < nchunks; c0 += nblk) {
+    const int nc = std::min(nblk, nchunks - c0);
+    pp.c0 = c0;
+    gdn_chunk_prep_kernel<<<dim3(nc, num_v_heads, batch), 128, kPSmem, st>>>(tmQ, tmK, tmV, tmW, pp);
+    int rc = ria::check_launch("ria_gdn_chunk_prefill (prep)");
+    if (rc) return rc;
+    rp.c0 = c0;
+    rp.init_state = c0 == 0 ? initial_state : final_state;
+    gdn_chunk_recurrence_kernel<<<dim3(num_v_heads, batch), 256, kRSmem, st>>>(tmQ, tmK, tmW, tmO, rp);
+    rc = ria::check_launch("ria_gdn_chunk_prefill (recurrence)");
+    if (rc) return rc;
+  }
+  return RIA_OK;
 }
+

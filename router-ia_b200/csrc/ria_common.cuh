@@ -4,7 +4,7 @@
 // copies (the TMA engine), tensor-map tiled copies, ldmatrix/movmatrix and the
 // bf16 mma.sync shape used by the decode kernels.  Every wait on an mbarrier is
 // bounded: after RIA_SPIN_LIMIT polls the kernel records an error code in
-// g_ria_device_error and carries on, so a lost copy can never hang the GPU.
+// the device error word and carries on, so a lost copy can never hang the GPU.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -121,6 +121,12 @@ __device__ __forceinline__ void tma_store_3d(const void* tmap, const void* smem_
                                              int32_t c2) {
   asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(tmap),
                "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(smem_src))
+               : "memory");
+}
+// 2-D tiled tensor store shared -> global (bulk-group completion), same rules.
+__device__ __forceinline__ void tma_store_2d(const void* tmap, const void* smem_src, int32_t c0, int32_t c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%1, %2}], [%3];" ::"l"(tmap),
+               "r"(c0), "r"(c1), "r"(smem_u32(smem_src))
                : "memory");
 }
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }

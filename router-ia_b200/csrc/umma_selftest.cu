@@ -1,8 +1,10 @@
 // Self-test of the tcgen05 operand layouts used by the prefill kernels:
 // D[128 x N] = A[128 x K] * B[K x N] with bf16 operands staged in shared
-// memory in K-major or MN-major 128-byte-swizzled tiles, fp32 accumulation in
+// memory in K-major or MN-major 128-byte-swizzled tiles, or A held in TMEM
+// (a_mode 2: bf16 pairs packed into 32-bit columns), fp32 accumulation in
 // TMEM, and the result read back with tcgen05.ld.  Every address the MMA reads
-// lies inside the two 32 KiB operand regions of this CTA.
+// lies inside the two 32 KiB operand regions or the 256-column TMEM
+// allocation of this CTA.
 #include "ria_capi_internal.h"
 #include "ria_common.cuh"
 #include "tcgen05.cuh"
@@ -12,7 +14,7 @@ namespace {
 constexpr int kM = 128;
 constexpr int kRegion = 32768;
 
-__global__ void __launch_bounds__(128, 1) umma_selftest_kernel(int a_mn, int b_mn, int n, int k, const float* A,
+__global__ void __launch_bounds__(128, 1) umma_selftest_kernel(int a_mode, int b_mn, int n, int k, const float* A,
                                                                const float* B, float* D, unsigned int* err) {
   extern __shared__ __align__(1024) unsigned char smem[];
   unsigned char* sa = smem;
@@ -22,8 +24,10 @@ __global__ void __launch_bounds__(128, 1) umma_selftest_kernel(int a_mn, int b_m
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
 
+  const bool a_mn = a_mode == 1, a_tmem = a_mode == 2;
+  constexpr uint32_t kAcol = 128;  // TMEM column of A in mode 2 (D uses 0..127)
   // Stage A (kM x k) and B (k x n) as bf16 in the requested layouts.
-  for (int idx = tid; idx < kM * k; idx += blockDim.x) {
+  for (int idx = tid; idx < (a_tmem ? 0 : kM * k); idx += blockDim.x) {
     const int m = idx / k, kk = idx % k;
     const __nv_bfloat16 v = __float2bfloat16_rn(A[idx]);
     uint32_t off;
@@ -49,13 +53,25 @@ __global__ void __launch_bounds__(128, 1) umma_selftest_kernel(int a_mn, int b_m
     mbar_fence_init();
   }
   if (warp == 0) {
-    tc::tmem_alloc(tslot, 128);
+    tc::tmem_alloc(tslot, 256);
     tc::tmem_relinquish();
   }
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tbase = *tslot;
+  if (a_tmem) {  // thread = row m = TMEM lane; 16 packed columns per store
+    for (int j0 = 0; j0 < k / 2; j0 += 16) {
+      uint32_t r[16];
+      for (int j = 0; j < 16; ++j)
+        r[j] = pack_bf16x2(A[tid * k + 2 * (j0 + j)], A[tid * k + 2 * (j0 + j) + 1]);
+      tc::st16(tc::taddr(tbase, warp * 32, kAcol + j0), r);
+    }
+    tc::wait_st();
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+  }
 
   if (tid == 0) {
     const uint32_t idesc = tc::idesc_bf16(kM, n, a_mn, b_mn);
@@ -70,7 +86,10 @@ __global__ void __launch_bounds__(128, 1) umma_selftest_kernel(int a_mn, int b_m
         bd = tc::sdesc_sw128(bbase + (ks >> 2) * (n * 128) + (ks & 3) * 32, 16, 1024);
       else
         bd = tc::sdesc_sw128(bbase + ks * 2048, k * 128, 1024);
-      tc::mma_bf16(tbase, ad, bd, idesc, ks > 0);
+      if (a_tmem)
+        tc::mma_bf16_ts(tbase, tbase + kAcol + ks * 8, bd, idesc, ks > 0);
+      else
+        tc::mma_bf16(tbase, ad, bd, idesc, ks > 0);
     }
     tc::commit(bar);
   }
@@ -86,7 +105,7 @@ __global__ void __launch_bounds__(128, 1) umma_selftest_kernel(int a_mn, int b_m
   }
   tc::fence_before_sync();
   __syncthreads();
-  if (warp == 0) tc::tmem_dealloc(tbase, 128);
+  if (warp == 0) tc::tmem_dealloc(tbase, 256);
 }
 
 }  // namespace
@@ -95,11 +114,12 @@ extern "C" int ria_umma_selftest(int32_t a_mn_major, int32_t b_mn_major, int32_t
                                  const float* b, float* d, ria_stream_t stream) {
   if ((n != 64 && n != 128) || (k != 64 && k != 128))
     return ria::fail(RIA_ERR_INVALID, "ria_umma_selftest: n and k must be 64 or 128");
+  if (a_mn_major < 0 || a_mn_major > 2) return ria::fail(RIA_ERR_INVALID, "ria_umma_selftest: a_mode must be 0, 1 or 2");
   if (!a || !b || !d) return ria::fail(RIA_ERR_INVALID, "ria_umma_selftest: null pointer");
   const int smem = 2 * kRegion + 64;
   cudaError_t e = cudaFuncSetAttribute(umma_selftest_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return ria::fail(RIA_ERR_CUDA, "ria_umma_selftest: %s", cudaGetErrorString(e));
-  umma_selftest_kernel<<<1, 128, smem, static_cast<cudaStream_t>(stream)>>>(a_mn_major != 0, b_mn_major != 0, n, k, a,
+  umma_selftest_kernel<<<1, 128, smem, static_cast<cudaStream_t>(stream)>>>(a_mn_major, b_mn_major != 0, n, k, a,
                                                                            b, d, ria::device_error_word());
   return ria::check_launch("ria_umma_selftest");
 }

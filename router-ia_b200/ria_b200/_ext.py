@@ -66,11 +66,12 @@ _SIGNATURES: dict[str, tuple[object, list]] = {
          c_int64, c_void_p, c_int32, c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_int64, c_int32, c_int32,
          c_int32, c_void_p],
     ),
+    "ria_gdn_chunk_prefill_workspace_bytes": (c_int64, [c_int32, c_int32, c_int32]),
     "ria_gdn_chunk_prefill": (
         c_int,
         [c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_void_p, c_void_p,
-         c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int32, c_int32, c_int32, c_int32,
-         c_void_p],
+         c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int32, c_int32,
+         c_int32, c_int32, c_void_p],
     ),
     "ria_gqa_prefill_workspace_bytes": (c_int64, [c_int32, c_int32]),
     "ria_gqa_prefill": (
@@ -216,9 +217,18 @@ def gqa_decode_paged_static(q, k, v, q_norm_w, k_norm_w, inv_freq, k_pool, v_poo
     _check(rc, "ria_gqa_decode_paged_static")
 
 
-def gdn_chunk_prefill(q, k, v, g, beta, initial_state, final_state, out):
+GDN_PREFILL_WORKSPACE_CAP = 2 << 30  # bytes; longer prompts run in blocks of chunks
+
+
+def gdn_chunk_prefill_workspace_bytes(batch: int, seq_len: int, num_v_heads: int) -> int:
+    return int(lib().ria_gdn_chunk_prefill_workspace_bytes(int(batch), int(seq_len), int(num_v_heads)))
+
+
+def gdn_chunk_prefill(q, k, v, g, beta, initial_state, final_state, out, workspace=None):
     """K2 (see ria_gdn_chunk_prefill).  q, k [B, T, Hk, 128] bf16; v, out
-    [B, T, Hv, 128] bf16; g, beta [B, T, Hv] f32; states [B, Hv, 128, 128] f32."""
+    [B, T, Hv, 128] bf16; g, beta [B, T, Hv] f32; states [B, Hv, 128, 128] f32.
+    ``workspace``: uint8 CUDA tensor (allocated here when None, up to
+    GDN_PREFILL_WORKSPACE_CAP bytes); returned for reuse."""
     _require_cuda(q, k, v, g, beta, final_state, out)
     B, T, Hk, dk = q.shape
     Hv = v.shape[2]
@@ -231,12 +241,19 @@ def gdn_chunk_prefill(q, k, v, g, beta, initial_state, final_state, out):
         raise ValueError("final_state: contiguous [B, Hv, 128, 128] float32")
     if initial_state is not None and (initial_state.dtype != torch.float32 or not initial_state.is_contiguous()):
         raise ValueError("initial_state: contiguous [B, Hv, 128, 128] float32")
+    if workspace is None:
+        need = gdn_chunk_prefill_workspace_bytes(B, T, Hv)
+        one_chunk = gdn_chunk_prefill_workspace_bytes(B, 1, Hv)
+        size = max(one_chunk, min(need, GDN_PREFILL_WORKSPACE_CAP // one_chunk * one_chunk)) if need else 16
+        workspace = torch.empty(size, dtype=torch.uint8, device=q.device)
     with _Hooked("gdn_prefill"):
         rc = lib().ria_gdn_chunk_prefill(
             q.data_ptr(), q.stride(0), q.stride(1), k.data_ptr(), k.stride(0), k.stride(1), v.data_ptr(),
             v.stride(0), v.stride(1), g.data_ptr(), beta.data_ptr(), g.stride(0), g.stride(1), _ptr(initial_state),
-            final_state.data_ptr(), out.data_ptr(), out.stride(0), out.stride(1), B, T, Hk, Hv, _stream(q))
+            final_state.data_ptr(), out.data_ptr(), out.stride(0), out.stride(1), workspace.data_ptr(),
+            workspace.numel() * workspace.element_size(), B, T, Hk, Hv, _stream(q))
     _check(rc, "ria_gdn_chunk_prefill")
+    return workspace
 
 
 def gqa_prefill(q, k, v, q_norm_w, k_norm_w, inv_freq, k_pool, v_pool, block_table, seq_lens, positions, out,
@@ -289,9 +306,10 @@ def gated_rmsnorm(o, z, weight, out):
     _check(rc, "ria_gated_rmsnorm")
 
 
-def umma_selftest(a, b, a_mn_major: bool, b_mn_major: bool):
+def umma_selftest(a, b, a_mn_major: int, b_mn_major: bool):
     """d = a @ b through one tcgen05 MMA chain (a: [128, k], b: [k, n] fp32
-    CUDA tensors; operands rounded to bf16)."""
+    CUDA tensors; operands rounded to bf16).  a_mn_major: 0 K-major, 1
+    MN-major (shared memory), 2 A held in tensor memory."""
     _require_cuda(a, b)
     a = a.float().contiguous()
     b = b.float().contiguous()

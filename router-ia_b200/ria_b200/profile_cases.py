@@ -92,9 +92,10 @@ def prefill_case(batch: int, seq: int, iters: int, device, hk: int = 16, hv: int
     beta = torch.sigmoid(torch.randn(batch, seq, hv, device=device, generator=g0)).float()
     out = torch.empty(batch, seq, hv, 128, dtype=torch.bfloat16, device=device)
     fs = torch.empty(batch, hv, 128, 128, dtype=torch.float32, device=device)
+    ws = torch.empty(_ext.gdn_chunk_prefill_workspace_bytes(batch, seq, hv), dtype=torch.uint8, device=device)
 
     def run():
-        chunk_gated_delta_rule(q, k, v, g, beta, None, fs, out)
+        chunk_gated_delta_rule(q, k, v, g, beta, None, fs, out, ws)
 
     ms = _time(run, iters, device)
     chunks = batch * hv * ((seq + 63) // 64)

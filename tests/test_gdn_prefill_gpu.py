@@ -38,11 +38,14 @@ def make_inputs(B, T, Hk, Hv, seed):
     return q, k, v, g.float(), beta.float()
 
 
-def run_case(dev, B, T, Hk, Hv, seed, with_state=False):
+def run_case(dev, B, T, Hk, Hv, seed, with_state=False, ws_chunks=None):
     q, k, v, g, beta = make_inputs(B, T, Hk, Hv, seed)
     s0 = (torch.randn(B, Hv, 128, 128, generator=torch.Generator().manual_seed(seed + 1)) * 0.1) if with_state else None
+    ws = None
+    if ws_chunks is not None:  # a workspace of ws_chunks chunks: the prompt runs in blocks
+        ws = torch.empty(_ext.gdn_chunk_prefill_workspace_bytes(B, 64 * ws_chunks, Hv), dtype=torch.uint8, device=dev)
     out, sf = chunk_gated_delta_rule(q.to(dev), k.to(dev), v.to(dev), g.to(dev), beta.to(dev),
-                                     None if s0 is None else s0.to(dev))
+                                     None if s0 is None else s0.to(dev), workspace=ws)
     grp = Hv // Hk
     ref_o, ref_s = O.recurrent_gated_delta_rule(q.float().repeat_interleave(grp, 2), k.float().repeat_interleave(grp, 2),
                                                 v.float(), g, beta, s0, dtype=torch.float64)
@@ -68,3 +71,18 @@ def test_initial_state(cuda_device):
 def test_long_sequence_state(cuda_device):
     errs = run_case(cuda_device, 1, 1024, 1, 2, seed=9)
     assert errs[0] < OUT_REL and errs[1] < OUT_MAX and errs[2] < STATE_REL, errs
+
+
+@pytest.mark.parametrize("ws_chunks", [1, 3])
+def test_blocked_workspace(cuda_device, ws_chunks):
+    """A workspace smaller than the prompt: blocks of chunks with the state
+    carried through final_state give the same result."""
+    errs = run_case(cuda_device, 2, 450, 1, 2, seed=11, with_state=True, ws_chunks=ws_chunks)
+    assert errs[0] < OUT_REL and errs[1] < OUT_MAX and errs[2] < STATE_REL, errs
+
+
+def test_workspace_too_small(cuda_device):
+    q, k, v, g, beta = (t.to(cuda_device) for t in make_inputs(1, 64, 1, 2, 0))
+    ws = torch.empty(1024, dtype=torch.uint8, device=cuda_device)
+    with pytest.raises(ValueError, match="workspace"):
+        chunk_gated_delta_rule(q, k, v, g, beta, workspace=ws)

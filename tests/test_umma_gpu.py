@@ -1,5 +1,5 @@
-"""tcgen05 operand layouts: every (A major, B major, N, K) combination the
-prefill kernels use, against a float64 matmul of the same bf16-rounded
+"""tcgen05 operand layouts: every (A major or A in TMEM, B major, N, K)
+combination the prefill kernels use, against a float64 matmul of the same bf16-rounded
 operands (fp32 accumulation: relative error ~1e-6)."""
 
 from __future__ import annotations
@@ -14,7 +14,7 @@ from ria_b200 import _ext
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("a_mn,b_mn,n,k", list(itertools.product([False, True], [False, True], [64, 128], [64, 128])))
+@pytest.mark.parametrize("a_mn,b_mn,n,k", list(itertools.product([0, 1, 2], [False, True], [64, 128], [64, 128])))
 def test_umma_layouts(cuda_device, a_mn, b_mn, n, k):
     g = torch.Generator().manual_seed(n * 7 + k + 100 * a_mn + 10 * b_mn)
     a = torch.randn(128, k, generator=g)
