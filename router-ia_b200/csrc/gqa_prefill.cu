@@ -13,14 +13,17 @@
 //     sincosf, host inverse frequencies), the normalised q (x 1/16) to a bf16
 //     workspace, K and V appended to the 64-token pages.
 //   * gqa_prefill_attn: one CTA per (128-token query tile, query head,
-//     sequence).  S = Q K^T (M = 128 tokens, N = 64 keys, K = 256) and
-//     O += P V (M = 128, N = 256, K = 64) are tcgen05 UMMAs with bf16 operands
-//     in 128-byte-swizzled SMEM (Q and the K/V pages by TMA, no multicast) and
-//     fp32 accumulators in TMEM.  The softmax runs on CUDA cores, one query
-//     row per thread (= TMEM lane); O is rescaled in TMEM only when a row's
-//     running maximum grows by more than 8 (log2 units), so most tiles touch
-//     only S.  K/V pages are double-buffered; the gated bf16 output leaves by
-//     TMA tensor store.
+//     sequence), key tiles of 128 (two pages).  Q is loaded once by TMA and
+//     moved into TMEM as bf16 pairs; a producer warp streams K tiles (double
+//     buffered) and V tiles straight from the pool pages by TMA (no
+//     multicast) and issues the tcgen05 UMMAs: S = Q K^T (M = 128 tokens,
+//     N = 128 keys, K = 256, A from TMEM) and O += P V (M = 128, N = 256,
+//     K = 128, P and V in 128-byte-swizzled SMEM), fp32 accumulators in TMEM.
+//     Four softmax warps own one query row each (= TMEM lane); they release
+//     S_j as soon as it is in registers, so S_{j+1} runs on the tensor core
+//     while they form P_j.  O is rescaled in TMEM only when a row's running
+//     maximum grows by more than 8 (log2 units).  The gated bf16 output
+//     leaves by TMA tensor store.
 #include <mutex>
 
 #include "ria_capi_internal.h"
@@ -158,46 +161,93 @@ struct AttnParams {
   unsigned int* err;
 };
 
-// SMEM map
-constexpr uint32_t kBox = 64 * 128;                // one [64 rows][64 bf16] box
-constexpr uint32_t kQBytes = 4 * 2 * kBox;         // Q: 4 boxes of [128 rows][128 B]
-constexpr uint32_t kKVBytes = 8 * kBox;            // K (4 boxes) + V (4 boxes), 64 keys
-constexpr uint32_t kOffQ = 0;
-constexpr uint32_t kOffKV = kQBytes;               // two buffers
-constexpr uint32_t kOffP = kOffKV + 2 * kKVBytes;  // P: [128 rows][64] bf16
-constexpr uint32_t kOffBar = kOffP + 2 * kBox;     // tma_q, tma_kv[2], bar_s, bar_pv
+// SMEM map: two K tiles and one V tile of 128 keys (two pages), each four
+// 16 KiB [128 rows][64 bf16] column chunks; P [128 rows][128 keys] bf16 as two
+// chunks.  Q arrives once by TMA into the second K tile and moves to TMEM.
+constexpr uint32_t kBox = 64 * 128;       // one [64 rows][64 bf16] TMA box
+constexpr uint32_t kChunk = 2 * kBox;     // [128 rows][64 bf16]
+constexpr int kKeys = 2 * kBlock;         // keys per tile
+constexpr uint32_t kOffK = 0;             // two tiles
+constexpr uint32_t kOffV = 8 * kChunk;
+constexpr uint32_t kOffP = 12 * kChunk;
+constexpr uint32_t kOffBar = 14 * kChunk;  // tma_q, tma_k[2], tma_v, bar_s, bar_pv, s_free, p_ready
 constexpr uint32_t kOffTslot = kOffBar + 64;
-constexpr uint32_t kAttnSmem = kOffTslot + 16;
-constexpr uint32_t kTmS = 0, kTmO = 256;
+constexpr uint32_t kOffXchg = kOffTslot + 16;  // [tile parity][half][row] partial maxima
+constexpr uint32_t kAttnSmem = kOffXchg + 2 * 2 * 128 * 4;
+static_assert(kAttnSmem <= 227 * 1024, "attention SMEM");
+// TMEM columns: O fp32 [128][256], S fp32 [128][128], Q bf16 pairs [128][128]
+constexpr uint32_t kTmO = 0, kTmS = 256, kTmQ = 384;
+constexpr int kAttnThreads = 320;  // warps 0-7: softmax half-rows; 8: S issue + K loads; 9: PV issue + V loads
+constexpr int kSoftmax = 256;
+constexpr uint32_t kBarRows = 1;  // named barrier of the softmax threads
 
-__global__ void __launch_bounds__(128, 1)
+__device__ __forceinline__ float ex2(float x) {  // 2^x (PTX ex2.approx, flush-to-zero)
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__global__ void __launch_bounds__(kAttnThreads, 1)
     gqa_prefill_attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                             const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
                             const AttnParams p) {
   extern __shared__ __align__(1024) unsigned char smem[];
   const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int kvh = h / kGroup;
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int t0 = qt * kTile;
   if (t0 >= p.T) return;
   uint64_t* tma_q = reinterpret_cast<uint64_t*>(smem + kOffBar);
-  uint64_t* tma_kv = tma_q + 1;
-  uint64_t* bar_s = tma_q + 3;
-  uint64_t* bar_pv = tma_q + 4;
+  uint64_t* tma_k = tma_q + 1;  // [2]
+  uint64_t* tma_v = tma_q + 3;
+  uint64_t* bar_s = tma_q + 4;
+  uint64_t* bar_pv = tma_q + 5;
+  uint64_t* s_free = tma_q + 6;
+  uint64_t* p_ready = tma_q + 7;
   uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + kOffTslot);
   const uint32_t sbase = smem_u32(smem);
   const int L0 = p.seq_lens[b];
   const int last_q = min(t0 + kTile - 1, p.T - 1);
-  const int ntiles = (L0 + last_q) / kBlock + 1;
+  const int last_key = L0 + last_q;  // the last key any row of this tile sees
+  const int ntiles = last_key / kKeys + 1;
   const int32_t* bt = p.block_table + static_cast<int64_t>(b) * p.bt_stride;
+
+  // Loads one K or V tile: the pages of keys [128 j, 128 j + 128) that some
+  // row of this query tile can see (pages past that are not loaded).
+  auto load_tile = [&](int j, uint32_t off, const CUtensorMap* map, uint64_t* bar) {
+    int npages = 0;
+    int32_t rows[2];
+    for (int pg = 0; pg < 2; ++pg) {
+      const int lp = 2 * j + pg;
+      if (lp * kBlock > last_key) break;
+      int phys = (lp < p.bt_stride) ? bt[lp] : -1;
+      if (phys < 0 || phys >= p.num_blocks) {
+        ria_set_error(p.err, RIA_DEVERR_BAD_BLOCK);
+        phys = 0;
+      }
+      rows[npages++] = static_cast<int32_t>(kvh * p.pool_tokens + static_cast<int64_t>(phys) * kBlock);
+    }
+    mbar_arrive_expect_tx(bar, npages * 4 * kBox);
+    for (int pg = 0; pg < npages; ++pg)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tma_load_2d(smem + off + c * kChunk + pg * kBox, map, c * 64, rows[pg], bar);
+  };
 
   if (tid == 0) {
     prefetch_tmap(&tmQ);
     prefetch_tmap(&tmK);
     prefetch_tmap(&tmV);
     prefetch_tmap(&tmO);
-    for (int i = 0; i < 5; ++i) mbar_init(&tma_q[i], 1);
+    for (int i = 0; i < 6; ++i) mbar_init(&tma_q[i], 1);
+    mbar_init(s_free, kSoftmax);
+    mbar_init(p_ready, kSoftmax);
     mbar_fence_init();
+    // Q (once, into the second K tile), K_0, V_0
+    mbar_arrive_expect_tx(tma_q, 4 * kChunk);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) tma_load_3d(smem + kOffK + 4 * kChunk + c * kChunk, &tmQ, h * kD + c * 64, t0, b, tma_q);
+    load_tile(0, kOffK, &tmK, &tma_k[0]);
+    load_tile(0, kOffV, &tmV, tma_v);
   }
   if (warp == 0) {
     tc::tmem_alloc(tslot, 512);
@@ -207,143 +257,191 @@ __global__ void __launch_bounds__(128, 1)
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tm = *tslot;
-  const uint32_t my_lane = tm + (static_cast<uint32_t>(warp * 32) << 16);
-
-  auto issue_kv = [&](int j) {
-    const int buf = j & 1;
-    const int lp = j;
-    int phys = (lp < p.bt_stride) ? bt[lp] : -1;
-    if (phys < 0 || phys >= p.num_blocks) {
-      ria_set_error(p.err, RIA_DEVERR_BAD_BLOCK);
-      phys = 0;
-    }
-    const int32_t row = static_cast<int32_t>(kvh * p.pool_tokens + static_cast<int64_t>(phys) * kBlock);
-    unsigned char* kv = smem + kOffKV + buf * kKVBytes;
-    mbar_arrive_expect_tx(&tma_kv[buf], kKVBytes);
+  if (warp < 8) {  // Q rows -> TMEM (bf16 pairs, the A operand of S = Q K^T); half-row each
+    mbar_wait_bounded(tma_q, 0, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
+    const uint32_t my_lane = tm + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    const int row = tid & 127;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      tma_load_2d(kv + i * kBox, &tmK, i * 64, row, &tma_kv[buf]);
-      tma_load_2d(kv + 4 * kBox + i * kBox, &tmV, i * 64, row, &tma_kv[buf]);
-    }
-  };
-  if (tid == 0) {
-    mbar_arrive_expect_tx(tma_q, kQBytes);
+    for (int cc = 0; cc < 2; ++cc) {
+      const int c = 2 * (tid >> 7) + cc;
+      const unsigned char* q = smem + kOffK + 4 * kChunk + c * kChunk;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) tma_load_3d(smem + kOffQ + i * 2 * kBox, &tmQ, h * kD + i * 64, t0, b, tma_q);
-    issue_kv(0);
-  }
-
-  const int r = tid;  // query row = TMEM lane
-  const int qidx = L0 + t0 + r;  // cache index of this query token
-  const bool row_ok = (t0 + r) < p.T;
-  float m_used = -INFINITY, l = 0.f;
-  uint32_t ph_s = 0, ph_pv = 0;
-  mbar_wait_bounded(tma_q, 0, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
-
-  for (int j = 0; j < ntiles; ++j) {
-    const int buf = j & 1;
-    const uint32_t akv = sbase + kOffKV + buf * kKVBytes;
-    mbar_wait_bounded(&tma_kv[buf], (j >> 1) & 1, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
-    if (tid == 0) {
-      tc::fence_after_sync();
-      const uint32_t id = tc::idesc_bf16(128, 64, false, false);
+      for (int half = 0; half < 2; ++half) {
+        uint32_t pk[16];
 #pragma unroll
-      for (int ks = 0; ks < 16; ++ks) {
-        const uint32_t qa = sbase + kOffQ + (ks >> 2) * (2 * kBox) + (ks & 3) * 32;
-        const uint32_t kb = akv + (ks >> 2) * kBox + (ks & 3) * 32;
-        tc::mma_bf16(tm + kTmS, tc::sdesc_sw128(qa, 16, 1024), tc::sdesc_sw128(kb, 16, 1024), id, ks > 0);
-      }
-      tc::commit(bar_s);
-    }
-    mbar_wait_bounded(bar_s, ph_s, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
-    ph_s ^= 1u;
-    if (j > 0) {  // P V of the previous tile is done: O, P and its K/V buffer are free
-      mbar_wait_bounded(bar_pv, ph_pv, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
-      ph_pv ^= 1u;
-    }
-    tc::fence_after_sync();
-    if (tid == 0 && j + 1 < ntiles) issue_kv(j + 1);
-    // Page rows past the sequence end hold whatever the pool had: zero their V
-    // rows so that 0-probability keys cannot inject non-finite values into P V.
-    {
-      const int first_bad = L0 + p.T - j * kBlock;
-      if (first_bad < kBlock) {
-        unsigned char* vb = smem + kOffKV + buf * kKVBytes + 4 * kBox;
-        for (int idx = tid; idx < (kBlock - first_bad) * 32; idx += 128) {
-          const int row = first_bad + (idx >> 5), ch = idx & 31;
-          *reinterpret_cast<uint4*>(vb + (ch >> 3) * kBox + row * 128 + (ch & 7) * 16) = make_uint4(0, 0, 0, 0);
+        for (int piece = 0; piece < 4; ++piece) {
+          const uint4 u = *reinterpret_cast<const uint4*>(q + tc::sw128_off(row, 32 * half + 8 * piece));
+          pk[4 * piece] = u.x;
+          pk[4 * piece + 1] = u.y;
+          pk[4 * piece + 2] = u.z;
+          pk[4 * piece + 3] = u.w;
         }
+        tc::st16(my_lane + kTmQ + 32 * c + 16 * half, pk);
       }
     }
-
-    // ---- softmax of this row over 64 keys
-    float s[64];
-    tc::ld32(my_lane + kTmS, s);
-    tc::ld32(my_lane + kTmS + 32, s + 32);
-    tc::wait_ld();
-    float mx = -INFINITY;
-#pragma unroll
-    for (int c = 0; c < 64; ++c) {
-      const bool ok = row_ok && (j * kBlock + c) <= qidx;
-      s[c] = ok ? s[c] * kLog2e : -INFINITY;
-      mx = fmaxf(mx, s[c]);
-    }
-    if (mx > m_used + kRescaleSlack) {
-      const float f = (m_used == -INFINITY) ? 0.f : exp2f(m_used - mx);
-      if (j > 0 && m_used != -INFINITY) {
-        for (int c0 = 0; c0 < kD; c0 += 32) {
-          float o[32];
-          tc::ld32(my_lane + kTmO + c0, o);
-          tc::wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] *= f;
-          tc::st32(my_lane + kTmO + c0, o);
-        }
-        tc::wait_st();
-      }
-      l *= f;
-      m_used = mx;
-    }
-    const float mu = (m_used == -INFINITY) ? 0.f : m_used;
-    unsigned char* prow = smem + kOffP;
-#pragma unroll
-    for (int c = 0; c < 64; c += 8) {
-      float pv[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        pv[i] = exp2f(s[c + i] - mu);
-        l += pv[i];
-      }
-      uint4 u;
-      u.x = pack_bf16x2(pv[0], pv[1]);
-      u.y = pack_bf16x2(pv[2], pv[3]);
-      u.z = pack_bf16x2(pv[4], pv[5]);
-      u.w = pack_bf16x2(pv[6], pv[7]);
-      *reinterpret_cast<uint4*>(prow + tc::sw128_off(r, c)) = u;
-    }
-    fence_proxy_async_smem();
-    tc::fence_before_sync();
-    __syncthreads();
-    tc::fence_after_sync();
-    if (tid == 0) {
-      const uint32_t id = tc::idesc_bf16(128, 256, false, true);
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks)
-        tc::mma_bf16(tm + kTmO, tc::sdesc_sw128(sbase + kOffP + ks * 32, 16, 1024),
-                     tc::sdesc_sw128(akv + 4 * kBox + ks * 2048, kBox, 1024), id, j > 0 || ks > 0);
-      tc::commit(bar_pv);
-    }
+    tc::wait_st();
   }
-  mbar_wait_bounded(bar_pv, ph_pv, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
+  tc::fence_before_sync();
+  __syncthreads();
   tc::fence_after_sync();
 
-  // ---- epilogue: O / l * sigmoid(gate) -> bf16 staging (reuses K/V buffer 0) -> TMA store
-  {
-    unsigned char* stg = smem + kOffKV;  // 4 boxes of [128 rows][128 B]
+  if (warp == 8) {
+    // ============================================================ S = Q K^T issue, K tiles
+    if (lane == 0) {
+      auto issue_s = [&](int j) {
+        tc::fence_after_sync();
+        const uint32_t id = tc::idesc_bf16(128, kKeys, false, false);
+        const uint32_t kt = sbase + kOffK + (j & 1) * 4 * kChunk;
+#pragma unroll
+        for (int ks = 0; ks < 16; ++ks)
+          tc::mma_bf16_ts(tm + kTmS, tm + kTmQ + ks * 8,
+                          tc::sdesc_sw128(kt + (ks >> 2) * kChunk + (ks & 3) * 32, 16, 1024), id, ks > 0);
+        tc::commit(bar_s);
+      };
+      if (ntiles > 1) load_tile(1, kOffK + 4 * kChunk, &tmK, &tma_k[1]);
+      mbar_wait_bounded(&tma_k[0], 0, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
+      issue_s(0);
+      for (int j = 0; j < ntiles; ++j) {
+        // the softmax rows hold S_j (so S_j is complete): S_{j+1} may overwrite
+        // it, and K_j's buffer takes K_{j+2}
+        mbar_wait_bounded(s_free, j & 1, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
+        if (j + 1 < ntiles) {
+          mbar_wait_bounded(&tma_k[(j + 1) & 1], ((j + 1) >> 1) & 1, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
+          issue_s(j + 1);
+        }
+        if (j + 2 < ntiles) load_tile(j + 2, kOffK + (j & 1) * 4 * kChunk, &tmK, &tma_k[j & 1]);
+      }
+    }
+  } else if (warp == 9) {
+    // ============================================================ O += P V issue, V tiles
+    for (int j = 0; j < ntiles; ++j) {
+      // V_j has landed: zero its rows past the sequence end (the pool holds
+      // anything there; 0-probability keys must not bring non-finite values)
+      mbar_wait_bounded(tma_v, j & 1, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
+      {
+        const int first_bad = L0 + p.T - j * kKeys;
+        if (first_bad < kKeys) {
+          const int r0 = max(first_bad, 0);
+          for (int idx = lane; idx < (kKeys - r0) * 32; idx += 32) {
+            const int row = r0 + (idx >> 5), ch = idx & 31;
+            *reinterpret_cast<uint4*>(smem + kOffV + (ch >> 3) * kChunk + row * 128 + (ch & 7) * 16) =
+                make_uint4(0, 0, 0, 0);
+          }
+          fence_proxy_async_smem();
+        }
+      }
+      __syncwarp();
+      if (lane == 0) {
+        // P_j is staged: O += P_j V_j; once it has read V_j, bring in V_{j+1}
+        mbar_wait_bounded(p_ready, j & 1, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
+        tc::fence_after_sync();
+        const uint32_t id = tc::idesc_bf16(128, 256, false, true);
+#pragma unroll
+        for (int ks = 0; ks < kKeys / 16; ++ks)
+          tc::mma_bf16(tm + kTmO, tc::sdesc_sw128(sbase + kOffP + (ks >> 2) * kChunk + (ks & 3) * 32, 16, 1024),
+                       tc::sdesc_sw128(sbase + kOffV + ks * 2048, kChunk, 1024), id, j > 0 || ks > 0);
+        tc::commit(bar_pv);
+        mbar_wait_bounded(bar_pv, j & 1, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
+        if (j + 1 < ntiles) load_tile(j + 1, kOffV, &tmV, tma_v);
+      }
+      __syncwarp();
+    }
+  } else {
+    // ============================================================ softmax rows
+    // Two threads per query row (= TMEM lane): half hf takes keys
+    // [64 hf, 64 hf + 64) of every tile and O columns [128 hf, 128 hf + 128).
+    const int r = tid & 127;
+    const int hf = tid >> 7;
+    const uint32_t my_lane = tm + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    const int qidx = L0 + t0 + r;  // cache index of this query token
+    const bool row_ok = (t0 + r) < p.T;
+    float* xchg = reinterpret_cast<float*>(smem + kOffXchg);  // [2][2][128]
+    float m_used = -INFINITY, l = 0.f;
+    for (int j = 0; j < ntiles; ++j) {
+      mbar_wait_bounded(bar_s, j & 1, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
+      tc::fence_after_sync();
+      float s[64];
+      tc::ld32(my_lane + kTmS + 64 * hf, s);
+      tc::ld32(my_lane + kTmS + 64 * hf + 32, s + 32);
+      tc::wait_ld();
+      tc::fence_before_sync();
+      mbar_arrive(s_free);
+      // causal / length mask only where the tile reaches past some row's last key
+      const bool full = (j + 1) * kKeys - 1 <= L0 + t0 && t0 + kTile <= p.T;
+      if (!full) {
+#pragma unroll
+        for (int c = 0; c < 64; ++c) {
+          const bool ok = row_ok && (j * kKeys + 64 * hf + c) <= qidx;
+          s[c] = ok ? s[c] : -INFINITY;
+        }
+      }
+      float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int c = 0; c < 64; ++c) m4[c & 3] = fmaxf(m4[c & 3], s[c]);
+      const float mine = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * kLog2e;
+      float* xt = xchg + (j & 1) * 256;  // a slot is rewritten only after the next tile's barrier
+      xt[hf * 128 + r] = mine;
+      named_bar_sync(kBarRows, kSoftmax);
+      const float mx = fmaxf(mine, xt[(hf ^ 1) * 128 + r]);
+      float f = 1.f;  // rescale of O and l when the running maximum moves
+      const bool rescale = mx > m_used + kRescaleSlack;
+      const bool scale_o = rescale && m_used != -INFINITY;  // O holds earlier tiles
+      if (rescale) {
+        f = (m_used == -INFINITY) ? 0.f : ex2(m_used - mx);
+        l *= f;
+        m_used = mx;
+      }
+      const float mu = (m_used == -INFINITY) ? 0.f : m_used;
+      float l4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int c = 0; c < 64; ++c) {
+        s[c] = ex2(fmaf(s[c], kLog2e, -mu));
+        l4[c & 3] += s[c];
+      }
+      l += (l4[0] + l4[1]) + (l4[2] + l4[3]);
+      // P_{j-1} V_{j-1} must be done: it reads the P staging tile, and writes O
+      if (j > 0) {
+        mbar_wait_bounded(bar_pv, (j - 1) & 1, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
+        tc::fence_after_sync();
+        if (scale_o) {
+          for (int c0 = 128 * hf; c0 < 128 * hf + 128; c0 += 32) {
+            float o[32];
+            tc::ld32(my_lane + kTmO + c0, o);
+            tc::wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] *= f;
+            tc::st32(my_lane + kTmO + c0, o);
+          }
+          tc::wait_st();
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < 64; c += 8) {
+        uint4 u;
+        u.x = pack_bf16x2(s[c], s[c + 1]);
+        u.y = pack_bf16x2(s[c + 2], s[c + 3]);
+        u.z = pack_bf16x2(s[c + 4], s[c + 5]);
+        u.w = pack_bf16x2(s[c + 6], s[c + 7]);
+        *reinterpret_cast<uint4*>(smem + kOffP + hf * kChunk + tc::sw128_off(r, c)) = u;
+      }
+      fence_proxy_async_smem();
+      tc::fence_before_sync();
+      mbar_arrive(p_ready);
+    }
+    mbar_wait_bounded(bar_pv, (ntiles - 1) & 1, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
+    tc::fence_after_sync();
+    // the two halves' sums (both use the same running maximum)
+    named_bar_sync(kBarRows, kSoftmax);  // every max exchange of the loop is read
+    xchg[hf * 128 + r] = l;
+    named_bar_sync(kBarRows, kSoftmax);
+    l += xchg[(hf ^ 1) * 128 + r];
+
+    // ---- epilogue: O / l * sigmoid(gate) -> bf16 staging over the first K tile -> TMA store
+    unsigned char* stg = smem + kOffK;  // 4 chunks of [128 rows][128 B]
     const float inv = (l > 0.f) ? 1.0f / l : 0.f;
     const __nv_bfloat16* grow =
         p.gate + static_cast<int64_t>(b) * p.gs_b + static_cast<int64_t>(row_ok ? t0 + r : t0) * p.gs_t + h * 2 * kD;
-    for (int c0 = 0; c0 < kD; c0 += 32) {
+    for (int c0 = 128 * hf; c0 < 128 * hf + 128; c0 += 32) {
       float o[32];
       tc::ld32(my_lane + kTmO + c0, o);
       tc::wait_ld();
@@ -359,18 +457,18 @@ __global__ void __launch_bounds__(128, 1)
         u.z = pack_bf16x2(o[i + 4], o[i + 5]);
         u.w = pack_bf16x2(o[i + 6], o[i + 7]);
         const int col = c0 + i;
-        *reinterpret_cast<uint4*>(stg + (col >> 6) * (2 * kBox) + tc::sw128_off(r, col & 63)) = u;
+        *reinterpret_cast<uint4*>(stg + (col >> 6) * kChunk + tc::sw128_off(r, col & 63)) = u;
       }
     }
     fence_proxy_async_smem();
-    tc::fence_before_sync();
-    __syncthreads();
-    if (tid == 0) {
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (tid == 0) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i) tma_store_3d(&tmO, stg + i * 2 * kBox, h * kD + i * 64, t0, b);
-      bulk_commit_group();
-      bulk_wait_all0();
-    }
+    for (int i = 0; i < 4; ++i) tma_store_3d(&tmO, smem + kOffK + i * kChunk, h * kD + i * 64, t0, b);
+    bulk_commit_group();
+    bulk_wait_all0();
   }
   __syncthreads();
   if (warp == 0) tc::tmem_dealloc(tm, 512);
@@ -477,6 +575,6 @@ extern "C" int ria_gqa_prefill(const void* q, int64_t q_stride_b, int64_t q_stri
   cudaError_t e = cudaFuncSetAttribute(gqa_prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem);
   if (e != cudaSuccess) return ria::fail(RIA_ERR_CUDA, "ria_gqa_prefill: smem attribute: %s", cudaGetErrorString(e));
   dim3 grid((seq_len + kTile - 1) / kTile, kHq, batch);
-  gqa_prefill_attn_kernel<<<grid, 128, kAttnSmem, st>>>(tmQ, tmK, tmV, tmO, ap);
+  gqa_prefill_attn_kernel<<<grid, kAttnThreads, kAttnSmem, st>>>(tmQ, tmK, tmV, tmO, ap);
   return ria::check_launch("ria_gqa_prefill (attention)");
 }
