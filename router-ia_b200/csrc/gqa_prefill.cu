@@ -67,7 +67,9 @@ struct PrepParams {
 
 // RMSNorm (1+w) and partial RoPE of one 256-dim head row held as 8 values per
 // lane (lane l has dims 8l..8l+7); dims [0,64) rotate-half inside the slice.
-__device__ __forceinline__ void norm_rope_8(float (&x)[8], const float* w, const float* inv_freq, int pos, int lane) {
+// cs_tab / sn_tab: cos / sin of position x inv_freq[f], f = 0..31.
+__device__ __forceinline__ void norm_rope_8(float (&x)[8], const float* w, const float* cs_tab, const float* sn_tab,
+                                            int lane) {
   float ss = 0.f;
 #pragma unroll
   for (int i = 0; i < 8; ++i) ss += x[i] * x[i];
@@ -86,8 +88,7 @@ __device__ __forceinline__ void norm_rope_8(float (&x)[8], const float* w, const
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int d = lane * 8 + i;
-      float sn, cs;
-      sincosf(static_cast<float>(pos) * inv_freq[d & (kRope / 2 - 1)], &sn, &cs);
+      const float cs = cs_tab[d & (kRope / 2 - 1)], sn = sn_tab[d & (kRope / 2 - 1)];
       x[i] = (d < kRope / 2) ? (x[i] * cs - partner[i] * sn) : (x[i] * cs + partner[i] * sn);
     }
   }
@@ -113,34 +114,51 @@ __device__ __forceinline__ uint4 pack8(const float (&x)[8], float s) {
   return u;
 }
 
+constexpr int kPrepTokens = 8;  // prompt tokens per prep CTA
+
+// One CTA per 8 prompt tokens: the tokens' RoPE angles once (cos / sin of
+// position x inv_freq, 32 frequencies each), then 8 x (16 q heads + 2 k
+// heads) RMSNorm + RoPE rows and 8 x 2 V rows spread over the 8 warps.
 __global__ void __launch_bounds__(256) gqa_prefill_prep_kernel(const PrepParams p) {
-  const int t = blockIdx.x, b = blockIdx.y;
+  __shared__ float cs_tab[kPrepTokens][kRope / 2], sn_tab[kPrepTokens][kRope / 2];
+  const int tb = blockIdx.x * kPrepTokens, b = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int L0 = p.seq_lens[b];
-  const int pos = p.positions[b] + t;
-  const int cidx = L0 + t;
-#pragma unroll
-  for (int hh = 0; hh < 2; ++hh) {
-    const int h = warp + 8 * hh;
-    float x[8];
-    load8(p.q + static_cast<int64_t>(b) * p.qs_b + static_cast<int64_t>(t) * p.qs_t + h * 2 * kD + lane * 8, x);
-    norm_rope_8(x, p.q_norm_w, p.inv_freq, pos, lane);
-    *reinterpret_cast<uint4*>(p.qbuf + ((static_cast<int64_t>(b) * p.T + t) * kHq + h) * kD + lane * 8) =
-        pack8(x, 0.0625f);
+  {
+    const int tt = threadIdx.x >> 5, f = threadIdx.x & 31;  // 8 tokens x 32 frequencies
+    float sn, cs;
+    sincosf(static_cast<float>(p.positions[b] + tb + tt) * p.inv_freq[f], &sn, &cs);
+    cs_tab[tt][f] = cs;
+    sn_tab[tt][f] = sn;
   }
-  if (warp < 4) {
+  __syncthreads();
+  constexpr int kTasks = kHq + 2 * kHkv;  // per token: q heads, k heads, v heads
+  for (int task = warp; task < kPrepTokens * kTasks; task += 8) {
+    const int tt = task / kTasks, kind = task % kTasks;
+    const int t = tb + tt;
+    if (t >= p.T) break;  // tasks run in token order
+    if (kind < kHq) {
+      const int h = kind;
+      float x[8];
+      load8(p.q + static_cast<int64_t>(b) * p.qs_b + static_cast<int64_t>(t) * p.qs_t + h * 2 * kD + lane * 8, x);
+      norm_rope_8(x, p.q_norm_w, cs_tab[tt], sn_tab[tt], lane);
+      *reinterpret_cast<uint4*>(p.qbuf + ((static_cast<int64_t>(b) * p.T + t) * kHq + h) * kD + lane * 8) =
+          pack8(x, 0.0625f);
+      continue;
+    }
+    const int cidx = L0 + t;
     const int lp = cidx / kBlock;
     const int phys = (lp < p.bt_stride) ? p.block_table[static_cast<int64_t>(b) * p.bt_stride + lp] : -1;
     if (phys < 0 || phys >= p.num_blocks) {
       if (lane == 0) ria_set_error(p.err, RIA_DEVERR_BAD_BLOCK);
-      return;
+      continue;
     }
-    const int kvh = warp & 1;
+    const int kvh = (kind - kHq) & 1;
     const int64_t row = static_cast<int64_t>(kvh) * p.pool_tokens + static_cast<int64_t>(phys) * kBlock + (cidx % kBlock);
-    if (warp < 2) {
+    if (kind < kHq + kHkv) {
       float x[8];
       load8(p.k + static_cast<int64_t>(b) * p.ks_b + static_cast<int64_t>(t) * p.ks_t + kvh * kD + lane * 8, x);
-      norm_rope_8(x, p.k_norm_w, p.inv_freq, pos, lane);
+      norm_rope_8(x, p.k_norm_w, cs_tab[tt], sn_tab[tt], lane);
       *reinterpret_cast<uint4*>(p.k_pool + row * kD + lane * 8) = pack8(x, 1.0f);
     } else {
       *reinterpret_cast<uint4*>(p.v_pool + row * kD + lane * 8) = *reinterpret_cast<const uint4*>(
@@ -192,7 +210,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                             const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
                             const AttnParams p) {
   extern __shared__ __align__(1024) unsigned char smem[];
-  const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int qt = gridDim.x - 1 - blockIdx.x;  // the longest (last) query tiles start first
+  const int h = blockIdx.y, b = blockIdx.z;
   const int kvh = h / kGroup;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int t0 = qt * kTile;
@@ -540,7 +559,7 @@ extern "C" int ria_gqa_prefill(const void* q, int64_t q_stride_b, int64_t q_stri
   pp.T = seq_len;
   pp.num_blocks = static_cast<int>(pool_tokens / kBlock);
   pp.err = err;
-  gqa_prefill_prep_kernel<<<dim3(seq_len, batch), 256, 0, st>>>(pp);
+  gqa_prefill_prep_kernel<<<dim3((seq_len + kPrepTokens - 1) / kPrepTokens, batch), 256, 0, st>>>(pp);
   int rc = ria::check_launch("ria_gqa_prefill (prep)");
   if (rc) return rc;
 
