@@ -432,6 +432,21 @@ def config2_prefill(device, iters=5, warmup=3):
                          "unit": "TFLOP/s", "frac": flops / (kms * 1e9) / p["bf16_tflops"], "peak_source": p["source"]}}
 
 
+def gqa_prefill_extra(device, batch=1, seq=8192, iters=5):
+    """K4 on one GQA layer: a prompt of ``seq`` tokens into an empty paged
+    cache (q/k norm + RoPE + append + causal attention + gate), timed with
+    CUDA events around the whole call.  Tensor-bound: causal FLOPs =
+    16 heads x 2 products x 2 x 256 x seq (seq + 1) / 2 per sequence."""
+    from ria_b200.profile_cases import gqa_prefill_case
+
+    r = gqa_prefill_case(batch, seq, iters, device)
+    p = peaks()
+    return {"workload": f"one GQA layer prefill, {batch} x {seq} new tokens, empty cache", "ms": r["ms"],
+            "tokens_per_s": r["tokens_per_s"],
+            "roofline": {"bound": "tensor", "achieved": r["tflops"], "peak": p["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": r["tflops"] / p["bf16_tflops"], "peak_source": p["source"]}}
+
+
 # --------------------------------------------------------------------------- CPU reference (oracle port)
 def cpu_reference(args, steps, warmup, sample):
     """router-ia's layer algorithm on the host cores, one sequence at a time
@@ -529,6 +544,7 @@ def main():
         if rank == 0 and not args.no_extras:
             line["config1_gqa_b1_l4096"] = config1_latency(device)
             line["config2_prefill"] = config2_prefill(device)
+            line["gqa_prefill_1x8192"] = gqa_prefill_extra(device)
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_reference(args, steps=2, warmup=1, sample=args.cpu_sample)
         if rank == 0:
