@@ -245,8 +245,9 @@ class BatchedAttentionState:
         self._workspace = launch.workspace
         return launch
 
-    def prepare_step(self) -> GqaLaunch:
-        """Reserve the block of each sequence's next token and plan the launch."""
+    def reserve_next(self) -> None:
+        """Reserve the page of each sequence's next token (uploading the block
+        table when one was added)."""
         grew = False
         for i, n in enumerate(self.lengths):
             if n % C.KV_BLOCK == 0 and len(self._blocks[i]) * C.KV_BLOCK <= n:
@@ -254,6 +255,10 @@ class BatchedAttentionState:
                 grew = True
         if grew:
             self.block_table.copy_(self._table_host)
+
+    def prepare_step(self) -> GqaLaunch:
+        """Reserve the page of each sequence's next token and plan the launch."""
+        self.reserve_next()
         return self.plan()
 
     def prefill(self, x: torch.Tensor) -> torch.Tensor:
@@ -284,14 +289,9 @@ class BatchedAttentionState:
         self.positions.copy_(torch.tensor(self.positions_host, dtype=torch.int32))
         return x
 
-    def step(self, x: torch.Tensor, launch: GqaLaunch | None = None, advance: bool = True) -> torch.Tensor:
-        """Run every layer once for the batch: x [B, 2048] fp32 -> [B, 2048] fp32.
-
-        This is ``run_forward_token``'s attention chain (qwen36_chat_batch.py:
-        184-187) without the MoE; ``advance`` then moves every sequence one
-        position forward on the device (the caller's ``tokens_seen += 1``)."""
-        if launch is None:
-            launch = self.prepare_step()
+    def run_layers(self, x: torch.Tensor, launch: GqaLaunch) -> torch.Tensor:
+        """The layer chain of one decode step, device work only (no host
+        bookkeeping, no synchronisation): what a CUDA graph captures."""
         for layer in sorted(self.layers):
             w = self.layers[layer]
             if isinstance(w, DeltaNetWeights):
@@ -299,8 +299,66 @@ class BatchedAttentionState:
             else:
                 x = gqa_decode(x, w, self.k_pool[layer], self.v_pool[layer], self.block_table, self.inv_freq,
                                launch, self.seq_lens, self.positions)
+        return x
+
+    def step(self, x: torch.Tensor, launch: GqaLaunch | None = None, advance: bool = True) -> torch.Tensor:
+        """Run every layer once for the batch: x [B, 2048] fp32 -> [B, 2048] fp32.
+
+        This is ``run_forward_token``'s attention chain (qwen36_chat_batch.py:
+        184-187) without the MoE; ``advance`` then moves every sequence one
+        position forward on the device (the caller's ``tokens_seen += 1``)."""
+        self.reserve_next()
+        if launch is None:
+            launch = self.plan()
+        x = self.run_layers(x, launch)
         if advance:
             _ext.advance_positions(self.seq_lens, self.positions)
             self.lengths = [n + 1 for n in self.lengths]
             self.positions_host = [p + 1 for p in self.positions_host]
         return x
+
+
+class DecodeGraph:
+    """The decode step of a ``BatchedAttentionState`` (every layer, plus the
+    device-side position advance) captured once as a CUDA graph and replayed
+    per token: the batched form of router-ia's per-token loop
+    (qwen36_chat_batch.py:181-207) without its per-layer launches and host
+    syncs.
+
+    The split-KV plan is fixed at capture for the longest sequence the block
+    table can hold (``max_blocks_per_seq`` pages), so the graph stays valid as
+    sequences grow; per-sequence lengths, positions and the block table live
+    on the device and are read by the kernels at replay.  The state must have
+    run at least one eager step (or prefill) first, so that library and cuBLAS
+    initialisation happens outside capture.
+    """
+
+    def __init__(self, state: BatchedAttentionState, split_pages: int | None = None):
+        self.state = state
+        dev = state.device
+        cap_blocks = state.max_blocks_per_seq
+        if split_pages is None:
+            total = sum(_cdiv(n + 1, C.KV_BLOCK) for n in state.lengths)
+            split_pages = _ext.gqa_split_pages(max(total, 1), C.FULL_NUM_KV_HEADS)
+        max_splits = _cdiv(cap_blocks, split_pages)
+        need = _ext.gqa_workspace_bytes(state.batch, max_splits) if max_splits > 1 else 0
+        ws = torch.empty(_cdiv(need, 16) * 4, dtype=torch.float32, device=dev) if need else None
+        self.launch = GqaLaunch(split_pages, max_splits, ws)
+        self.x = torch.zeros(state.batch, C.HIDDEN, dtype=torch.float32, device=dev)
+        self.graph = torch.cuda.CUDAGraph()
+        # Capture records work without running it: the state is untouched.
+        with torch.cuda.graph(self.graph, capture_error_mode="thread_local"):
+            self.out = state.run_layers(self.x, self.launch)
+            _ext.advance_positions(state.seq_lens, state.positions)
+
+    def step(self, x: torch.Tensor) -> torch.Tensor:
+        """x [B, 2048] fp32 on the device -> the residual stream [B, 2048] fp32
+        (a buffer owned by the graph, overwritten by the next step)."""
+        st = self.state
+        st.reserve_next()
+        self.x.copy_(x)
+        self.graph.replay()
+        st.lengths = [n + 1 for n in st.lengths]
+        st.positions_host = [p + 1 for p in st.positions_host]
+        return self.out
+
