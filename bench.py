@@ -362,9 +362,74 @@ def config1_latency(device, iters=50):
     _ext.launch_hook = None
     kms, _ = hook.mean_ms("gqa_decode")
     step_ms = s.elapsed_time(e) / iters
+    # the same layer step replayed from a CUDA graph (no per-launch host work)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, capture_error_mode="thread_local"):
+        gqa_decode(x, w, k, v, table, inv, launch, seq_len0=L, position0=L)
+    for _ in range(10):
+        graph.replay()
+    torch.cuda.synchronize(device)
+    s.record()
+    for _ in range(iters):
+        graph.replay()
+    e.record()
+    torch.cuda.synchronize(device)
+    graph_ms = s.elapsed_time(e) / iters
     kbytes = gqa_bytes([L])
-    return {"layer_step_us": step_ms * 1e3, "gqa_kernel_us": kms * 1e3, "kernel_bytes": kbytes,
-            "kernel_gbs": kbytes / (kms * 1e6), "split_pages": launch.split_pages, "splits": launch.max_splits}
+    return {"layer_step_us": step_ms * 1e3, "layer_step_graph_us": graph_ms * 1e3, "gqa_kernel_us": kms * 1e3,
+            "kernel_bytes": kbytes, "kernel_gbs": kbytes / (kms * 1e6), "split_pages": launch.split_pages,
+            "splits": launch.max_splits}
+
+
+def decode_b1_stack(device, L=4096, iters=30):
+    """One sequence through the whole 40-layer stack per token (config 1's
+    context length on every GQA layer): per-token latency of the eager step
+    and of the step replayed from a CUDA graph (DecodeGraph)."""
+    from ria_b200 import constants as C, synthetic
+    from ria_b200.engine import BatchedAttentionState, DecodeGraph
+    from ria_b200.weights import DeltaNetWeights, GqaWeights
+
+    layers = {}
+    for layer in range(C.NUM_LAYERS):
+        t = synthetic.layer_weights_on_device(layer, device, seed=0)
+        cls = GqaWeights if C.is_full_attention_layer(layer) else DeltaNetWeights
+        layers[layer] = cls.from_tensors(t, device)
+        del t
+    nb = (L + 2 * iters + 64) // C.KV_BLOCK + 2
+    eng = BatchedAttentionState(layers, batch=1, pool_blocks=nb, max_blocks_per_seq=nb, device=device)
+    g = torch.Generator(device=device)
+    g.manual_seed(7)
+    for layer in eng.rec:
+        eng.rec[layer].normal_(0.0, 0.1, generator=g)
+    for layer in eng.k_pool:
+        eng.k_pool[layer].normal_(0.0, 1.0, generator=g)
+        eng.v_pool[layer].normal_(0.0, 1.0, generator=g)
+    eng.set_length(0, L)
+    eng.sync_tables()
+    x = torch.randn(1, C.HIDDEN, device=device, generator=g)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for _ in range(3):
+        eng.step(x)
+    torch.cuda.synchronize(device)
+    s.record()
+    for _ in range(iters):
+        eng.step(x)
+    e.record()
+    torch.cuda.synchronize(device)
+    eager_ms = s.elapsed_time(e) / iters
+    graph = DecodeGraph(eng)
+    for _ in range(3):
+        graph.step(x)
+    torch.cuda.synchronize(device)
+    s.record()
+    for _ in range(iters):
+        graph.step(x)
+    e.record()
+    torch.cuda.synchronize(device)
+    graph_ms = s.elapsed_time(e) / iters
+    del graph, eng, layers
+    return {"workload": f"1 sequence, 30 DeltaNet + 10 GQA layers, {L} cached tokens", "eager_ms_per_token": eager_ms,
+            "graph_ms_per_token": graph_ms, "graph_tokens_per_s": 1e3 / graph_ms}
 
 
 PREFILL_FLOP_PER_CHUNK_HEAD = 11_534_336  # 2C^2(3d + 2d) + 6 C d^2 with C = 64, d = 128
@@ -545,6 +610,7 @@ def main():
             line["config1_gqa_b1_l4096"] = config1_latency(device)
             line["config2_prefill"] = config2_prefill(device)
             line["gqa_prefill_1x8192"] = gqa_prefill_extra(device)
+            line["decode_b1_stack_l4096"] = decode_b1_stack(device)
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_reference(args, steps=2, warmup=1, sample=args.cpu_sample)
         if rank == 0:
