@@ -381,6 +381,47 @@ def config1_latency(device, iters=50):
             "splits": launch.max_splits}
 
 
+def config0_deltanet(device, prompt=64, decode=64, reps=5):
+    """Benchmark configuration 0: one Gated DeltaNet layer, batch 1, a
+    64-token prompt through the chunked prefill (K2 + conv/gate/norm kernels)
+    then 64 decode tokens replayed from a CUDA graph (K1), from a zero state.
+    Reports tokens/s over the 128 tokens and each phase's time."""
+    from ria_b200 import constants as C, synthetic
+    from ria_b200.engine import BatchedAttentionState, DecodeGraph
+    from ria_b200.weights import DeltaNetWeights
+
+    w = {0: DeltaNetWeights.from_tensors(synthetic.layer_weights_on_device(0, device, seed=0), device)}
+    g = torch.Generator(device=device)
+    g.manual_seed(11)
+    xp = torch.randn(1, prompt, C.HIDDEN, device=device, generator=g).to(torch.bfloat16).float()
+    xd = torch.randn(decode, 1, C.HIDDEN, device=device, generator=g).to(torch.bfloat16).float()
+    s, m, e = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+    best = None
+    for _ in range(reps):
+        nb = (prompt + decode + 2) // C.KV_BLOCK + 2  # the page bookkeeping runs even without GQA layers
+        eng = BatchedAttentionState(w, batch=1, pool_blocks=nb, max_blocks_per_seq=nb, device=device)
+        eng.step(xd[0])  # warm-up step (library and cuBLAS initialisation), then reset the state
+        eng.rec[0].zero_()
+        eng.conv[0].zero_()
+        eng.lengths, eng.positions_host = [0], [0]
+        eng.sync_tables()
+        graph = DecodeGraph(eng)
+        torch.cuda.synchronize(device)
+        s.record()
+        eng.prefill(xp)
+        m.record()
+        for t in range(decode):
+            graph.step(xd[t])
+        e.record()
+        torch.cuda.synchronize(device)
+        r = (s.elapsed_time(m), m.elapsed_time(e))
+        best = r if best is None or sum(r) < sum(best) else best
+        del graph, eng
+    return {"workload": f"config0: one DeltaNet layer, batch 1, {prompt} prompt + {decode} decode tokens",
+            "tokens_per_s": (prompt + decode) / (sum(best) * 1e-3), "prefill_ms": best[0],
+            "decode_ms_per_token": best[1] / decode, "best_of": reps}
+
+
 def decode_b1_stack(device, L=4096, iters=30):
     """One sequence through the whole 40-layer stack per token (config 1's
     context length on every GQA layer): per-token latency of the eager step
@@ -611,6 +652,7 @@ def main():
             line["config2_prefill"] = config2_prefill(device)
             line["gqa_prefill_1x8192"] = gqa_prefill_extra(device)
             line["decode_b1_stack_l4096"] = decode_b1_stack(device)
+            line["config0_deltanet_b1"] = config0_deltanet(device)
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_reference(args, steps=2, warmup=1, sample=args.cpu_sample)
         if rank == 0:
