@@ -19,17 +19,17 @@
 //     maps, no multicast), gates and norms, G = [Q;K] K^T on the tensor cores,
 //     the causal score tile P and A, the 64x64 unit-lower-triangular inverse
 //     (16x16 diagonal blocks by substitution, off-diagonal blocks by tf32
-//     mma.sync), then W^T = K^T TW^T and U^T = V^T TU^T on the tensor cores.
-//     Writes one 41,600-byte record per (sequence, head, chunk) to the
-//     workspace: W^T [128 dk][64] bf16, U^T [128 dv][64] bf16, P [64][64] bf16
+//     mma.sync), then U^T = V^T TU^T and the token-major W = TW K on the
+//     tensor cores.  Writes one 41,600-byte record per (sequence, head, chunk)
+//     to the workspace: W [64][128 dk] bf16, U^T [128 dv][64] bf16, P [64][64] bf16
 //     and the chunk scalars (e^gamma_C, the per-token state-update scale
 //     s_k e^(gamma_C - gamma), the per-token output scale e^gamma s_q 128^-0.5).
 //   * gdn_chunk_recurrence_kernel: one 256-thread CTA per (sequence, value
 //     head).  The fp32 state S^T (lane = dv, column = dk) stays in TMEM for
-//     the whole prompt; per chunk: bf16 copy of S^T into TMEM, X = S^T W^T and
-//     O = S^T Qr^T with the A operand read from TMEM, V'^T = U^T - X (raw and
-//     column-scaled, both back into TMEM as bf16), S^T += V's^T K and
-//     O += V'^T P^T.  The chunk's operands (Q, K, W^T, U^T, P, scalars) arrive
+//     the whole prompt; per chunk: bf16 copy of S^T into TMEM, then
+//     [X | O] = S^T [W | Qr]^T as one N = 128 product (A read from TMEM),
+//     V'^T = U^T - X (raw and column-scaled, both back into TMEM as bf16),
+//     S^T += V's^T K and O += V'^T P^T.  The chunk's operands (Q, K, W^T, U^T, P, scalars) arrive
 //     by TMA through a three-slot ring refilled as soon as a chunk's MMAs are
 //     complete; O is double-buffered in TMEM so the output of chunk c-1 is
 //     written while chunk c's MMAs run.
@@ -55,7 +55,7 @@ constexpr uint32_t kBox = 8192;  // 64 rows x 128 bytes, 128-byte swizzled
 constexpr int kLd = 65;          // padded fp32 row of A and T (bank-conflict free)
 
 // Workspace record of one (sequence, value head, chunk).
-constexpr uint32_t kRecWT = 0;         // W^T [128 dk][64 tokens] bf16
+constexpr uint32_t kRecW = 0;          // W [64 tokens][128 dk] bf16 as two [64][64] boxes (dk 0-63, 64-127)
 constexpr uint32_t kRecUT = 16384;     // U^T [128 dv][64 tokens] bf16
 constexpr uint32_t kRecP = 32768;      // P [64 t][64 j] bf16
 constexpr uint32_t kRecScal = 40960;   // f32: [0] e^gamma_C, [4..67] state scale, [68..131] output scale
@@ -82,9 +82,11 @@ static_assert(64 * kLd * 4 <= kPT - kPA, "A region");
 static_assert(kPSmem * 3 <= 227 * 1024, "three prep CTAs per SM");
 
 // ---------------------------------------------------------------- recurrence SMEM
-constexpr uint32_t kSlQ = 0;            // Q dims 0-63 | 64-127 (scaled in place to Qr)
-constexpr uint32_t kSlK = 2 * kBox;     // K dims 0-63 | 64-127
-constexpr uint32_t kSlWT = 4 * kBox;    // W^T, two 64-row boxes
+// [W dk 0-63 | Q dk 0-63 | W dk 64-127 | Q dk 64-127]: per 64-dk half a
+// 128-row K-major operand whose rows 0-63 are W and 64-127 are Q (scaled in
+// place to Qr), the B operand of the combined [X | O] product.
+constexpr uint32_t kSlWQ = 0;
+constexpr uint32_t kSlK = 4 * kBox;     // K dims 0-63 | 64-127
 constexpr uint32_t kSlUT = 6 * kBox;    // U^T, two 64-row boxes
 constexpr uint32_t kSlP = 8 * kBox;     // P
 constexpr uint32_t kSlScal = 9 * kBox;  // chunk scalars
@@ -95,9 +97,9 @@ constexpr uint32_t kRSmem = kRBar + 128;
 constexpr uint32_t kChunkTx = 9 * kBox + kScalBytes;
 static_assert(kRSmem <= 227 * 1024, "recurrence SMEM");
 
-// Recurrence TMEM columns: S^T fp32, X, O (two buffers), bf16 S^T (two
-// buffers), bf16 V'^T, bf16 V's^T -- all 512 columns.
-constexpr uint32_t kTS = 0, kTX = 128, kTO = 192, kTSb = 320, kTV = 448, kTVs = 480;
+// Recurrence TMEM columns: S^T fp32, [X | O] (two buffers of 128), bf16 S^T,
+// bf16 V'^T, bf16 V's^T -- all 512 columns.
+constexpr uint32_t kTS = 0, kTD = 128, kTSb = 384, kTV = 448, kTVs = 480;
 
 constexpr uint32_t kBarPrep = 1;
 
@@ -332,7 +334,7 @@ __global__ void __launch_bounds__(128, 3)
   tc::fence_after_sync();
   const uint32_t tm = *tslot;
   const uint32_t my_lane = tm + (static_cast<uint32_t>(warp * 32) << 16);
-  constexpr uint32_t kTmG = 0, kTmW = 64, kTmU = 0;  // U^T reuses G's columns
+  constexpr uint32_t kTmG = 0, kTmW = 0, kTmU = 0;  // G, then U^T, then W (128 columns)
 
   // gates: inclusive scan of the chunk's log decays inside each of the two warps
   float gscan = 0.f, bv = 0.f;
@@ -444,14 +446,11 @@ __global__ void __launch_bounds__(128, 3)
   named_bar_sync(kBarPrep, 128);
   tc::fence_after_sync();
 
-  // ---- W^T = K^T TW^T, U^T = V^T TU^T (A operands MN-major from the TMA tiles)
+  // ---- U^T = V^T TU^T (A = V, MN-major over the Q boxes), into G's columns
   mbar_wait_bounded(tma_v, 0, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
   if (lt == 0) {
     tc::fence_after_sync();
     const uint32_t id = tc::idesc_bf16(128, 64, true, false);
-    for (int ks = 0; ks < 4; ++ks)
-      tc::mma_bf16(tm + kTmW, tc::sdesc_sw128(sbase + kPX + kBox + ks * 2048, kPY - kPX, 1024),
-                   tc::sdesc_sw128(sbase + kPA + ks * 32, 16, 1024), id, ks > 0);
     for (int ks = 0; ks < 4; ++ks)
       tc::mma_bf16(tm + kTmU, tc::sdesc_sw128(sbase + kPX + ks * 2048, kPY - kPX, 1024),
                    tc::sdesc_sw128(sbase + kPA + kBox + ks * 32, 16, 1024), id, ks > 0);
@@ -468,16 +467,36 @@ __global__ void __launch_bounds__(128, 3)
   }
   mbar_wait_bounded(mma, 1, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
   tc::fence_after_sync();
-  {  // W^T (row = dk) and U^T (row = dv) staged over TW|TU and T, then TMA-stored
+  {  // U^T (row = dv) staged over T (two boxes)
     float v[64];
-    tc::ld32(my_lane + kTmW, v);
-    tc::ld32(my_lane + kTmW + 32, v + 32);
-    tc::wait_ld();
-    store_row_bf16<64>(smem + kPA, lt, 0, v);
     tc::ld32(my_lane + kTmU, v);
     tc::ld32(my_lane + kTmU + 32, v + 32);
     tc::wait_ld();
     store_row_bf16<64>(smem + kPT, lt, 0, v);
+  }
+  tc::fence_before_sync();
+  named_bar_sync(kBarPrep, 128);  // U^T is read out of TMEM
+  // ---- W = TW K, token-major: A = [TW; TU] (the TU rows give unused rows
+  // 64-127), B = the K tile (MN-major, dk across the two boxes), N = 128 dk
+  if (lt == 0) {
+    tc::fence_after_sync();
+    const uint32_t id = tc::idesc_bf16(128, 128, false, true);
+    for (int ks = 0; ks < 4; ++ks)
+      tc::mma_bf16(tm + kTmW, tc::sdesc_sw128(sbase + kPA + ks * 32, 16, 1024),
+                   tc::sdesc_sw128(sbase + kPX + kBox + ks * 2048, kPY - kPX, 1024), id, ks > 0);
+    tc::commit(mma);
+  }
+  mbar_wait_bounded(mma, 0, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
+  tc::fence_after_sync();
+  if (lt < 64) {  // W rows (tokens) staged over TW|TU: dk 0-63 and dk 64-127 boxes
+    float v[64];
+#pragma unroll
+    for (int hb = 0; hb < 2; ++hb) {
+      tc::ld32(my_lane + kTmW + 64 * hb, v);
+      tc::ld32(my_lane + kTmW + 64 * hb + 32, v + 32);
+      tc::wait_ld();
+      store_row_bf16<64>(smem + kPA + hb * kBox, lt, 0, v);
+    }
   }
   fence_proxy_async_smem();
   tc::fence_before_sync();
@@ -542,12 +561,12 @@ __global__ void __launch_bounds__(256, 1)
     const int c = p.c0 + j;
     const int32_t row = static_cast<int32_t>((rec0 + j) * kRecRows);
     mbar_arrive_expect_tx(&full[s], kChunkTx);
-    tma_load_3d(slot + kSlQ, &tmQ, hk * kDK, c * kC, b, &full[s]);
-    tma_load_3d(slot + kSlQ + kBox, &tmQ, hk * kDK + 64, c * kC, b, &full[s]);
+    tma_load_3d(slot + kSlWQ + kBox, &tmQ, hk * kDK, c * kC, b, &full[s]);
+    tma_load_3d(slot + kSlWQ + 3 * kBox, &tmQ, hk * kDK + 64, c * kC, b, &full[s]);
     tma_load_3d(slot + kSlK, &tmK, hk * kDK, c * kC, b, &full[s]);
     tma_load_3d(slot + kSlK + kBox, &tmK, hk * kDK + 64, c * kC, b, &full[s]);
-    tma_load_2d(slot + kSlWT, &tmW, 0, row, &full[s]);
-    tma_load_2d(slot + kSlWT + kBox, &tmW, 0, row + 64, &full[s]);
+    tma_load_2d(slot + kSlWQ, &tmW, 0, row, &full[s]);
+    tma_load_2d(slot + kSlWQ + 2 * kBox, &tmW, 0, row + 64, &full[s]);
     tma_load_2d(slot + kSlUT, &tmW, 0, row + 128, &full[s]);
     tma_load_2d(slot + kSlUT + kBox, &tmW, 0, row + 192, &full[s]);
     tma_load_2d(slot + kSlP, &tmW, 0, row + 256, &full[s]);
@@ -598,9 +617,9 @@ __global__ void __launch_bounds__(256, 1)
     mbar_wait_bounded(bar_o, j & 1, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
     tc::fence_after_sync();
     float o[32];
-    tc::ld32(my_lane + kTO + 64 * (j & 1) + 32 * wg, o);
+    tc::ld32(my_lane + kTD + 128 * (j & 1) + 64 + 32 * wg, o);
     tc::wait_ld();
-    unsigned char* stg = smem + (j % kSlots) * kSlotBytes + kSlWT + (lt >> 6) * kBox;
+    unsigned char* stg = smem + (j % kSlots) * kSlotBytes + kSlWQ + (lt >> 6) * kBox;
     const bool odd = lane & 1;
     const int col = (lt & 63) & ~1;
 #pragma unroll
@@ -617,7 +636,7 @@ __global__ void __launch_bounds__(256, 1)
   // tile (rows past the prompt end are clipped by the tensor map); once the
   // stores have read it, the slot is refilled with chunk j + 3.
   auto store_output = [&](int j) {
-    const unsigned char* stg = smem + (j % kSlots) * kSlotBytes + kSlWT;
+    const unsigned char* stg = smem + (j % kSlots) * kSlotBytes + kSlWQ;
     const int c = p.c0 + j;
     tma_store_3d(&tmO, stg, h * kDV, c * kC, b);
     tma_store_3d(&tmO, stg + kBox, h * kDV + 64, c * kC, b);
@@ -631,7 +650,8 @@ __global__ void __launch_bounds__(256, 1)
     unsigned char* slot = smem + s * kSlotBytes;
     const uint32_t aslot = sbase + s * kSlotBytes;
     const float* scal = reinterpret_cast<const float*>(slot + kSlScal);
-    const uint32_t sb = kTSb + 64 * (j & 1);  // this chunk's bf16 S^T buffer
+    const uint32_t sb = kTSb;                  // bf16 S^T
+    const uint32_t dd = kTD + 128 * (j & 1);  // this chunk's [X | O]
     mbar_wait_bounded(&full[s], (j / kSlots) & 1, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
     const float eC = scal[0];
 
@@ -654,7 +674,7 @@ __global__ void __launch_bounds__(256, 1)
     }
     {  // Qr = diag(output scale) Q: thread -> (row, 64-dim box, half of the row)
       const int r = tid & 63;
-      unsigned char* rowp = slot + kSlQ + ((tid >> 6) & 1) * kBox + r * 128;
+      unsigned char* rowp = slot + kSlWQ + (((tid >> 6) & 1) ? 3 : 1) * kBox + r * 128;
       const float sc = scal[68 + r];
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
@@ -674,12 +694,13 @@ __global__ void __launch_bounds__(256, 1)
     tc::fence_before_sync();
     __syncthreads();
 
-    // ---- X = S^T W^T; meanwhile the previous chunk's output goes to staging
+    // ---- [X | O] = S^T [W | Qr]^T; meanwhile the previous chunk's output goes to staging
     if (tid == 0) {
       tc::fence_after_sync();
-      const uint32_t idX = tc::idesc_bf16(128, 64, false, true);
+      const uint32_t idXO = tc::idesc_bf16(128, 128, false, false);
       for (int ks = 0; ks < 8; ++ks)
-        tc::mma_bf16_ts(tm + kTX, tm + sb + ks * 8, tc::sdesc_sw128(aslot + kSlWT + ks * 2048, kBox, 1024), idX,
+        tc::mma_bf16_ts(tm + dd, tm + sb + ks * 8,
+                        tc::sdesc_sw128(aslot + kSlWQ + (ks >> 2) * (2 * kBox) + (ks & 3) * 32, 16, 1024), idXO,
                         ks > 0);
       tc::commit(bar_x);
     }
@@ -691,7 +712,7 @@ __global__ void __launch_bounds__(256, 1)
     {
       float x[32], u[32];
       uint32_t pk[16];
-      tc::ld32(my_lane + kTX + 32 * wg, x);
+      tc::ld32(my_lane + dd + 32 * wg, x);
       load_row_bf16<32>(slot + kSlUT, lt, 32 * wg, u);
       tc::wait_ld();
 #pragma unroll
@@ -707,8 +728,7 @@ __global__ void __launch_bounds__(256, 1)
     tc::fence_before_sync();
     __syncthreads();
 
-    // ---- S^T += V's^T K first (the next chunk waits only for it), then
-    // O = S^T Qr^T + V'^T P^T from the old S^T's bf16 copy
+    // ---- S^T += V's^T K first (the next chunk waits only for it), then O += V'^T P^T
     if (tid == 0) {
       tc::fence_after_sync();
       const uint32_t idS = tc::idesc_bf16(128, 128, false, true);
@@ -717,12 +737,9 @@ __global__ void __launch_bounds__(256, 1)
                         true);
       tc::commit(bar_s);
       const uint32_t idO = tc::idesc_bf16(128, 64, false, false);
-      const uint32_t od = tm + kTO + 64 * (j & 1);
-      for (int ks = 0; ks < 8; ++ks)
-        tc::mma_bf16_ts(od, tm + sb + ks * 8,
-                        tc::sdesc_sw128(aslot + kSlQ + (ks >> 2) * kBox + (ks & 3) * 32, 16, 1024), idO, ks > 0);
       for (int ks = 0; ks < 4; ++ks)
-        tc::mma_bf16_ts(od, tm + kTV + ks * 8, tc::sdesc_sw128(aslot + kSlP + ks * 32, 16, 1024), idO, true);
+        tc::mma_bf16_ts(tm + dd + 64, tm + kTV + ks * 8, tc::sdesc_sw128(aslot + kSlP + ks * 32, 16, 1024), idO,
+                        true);
       tc::commit(bar_o);
     }
     if (tid == kStoreTid && j > 0) store_output(j - 1);
