@@ -163,13 +163,17 @@ class EventHook:
 def build_engine(args, device, rank, world, headroom):
     from ria_b200 import constants as C, synthetic
     from ria_b200.engine import BatchedAttentionState
-    from ria_b200.sharding import shard_range
+    from ria_b200.sharding import balanced_assignment
     from ria_b200.weights import DeltaNetWeights, GqaWeights
 
-    # One seeded request list for the whole job; each rank decodes its shard.
-    requests = synthetic.ragged_lengths(world * args.batch, args.len_lo, args.len_hi, seed=0)
-    shard = shard_range(len(requests), world, rank)
-    lengths = requests[shard.start:shard.stop]
+    # Each rank decodes args.batch sequences whose KV lengths are a stratified
+    # sample of U[len_lo, len_hi] (the same multiset on every rank and at every
+    # GPU count: weak scaling with fixed work per GPU).  The job's request list
+    # is the ranks' lists concatenated; the cost-balanced assignment keeps
+    # each rank's list.
+    per_rank = synthetic.stratified_lengths(args.batch, args.len_lo, args.len_hi, seed=0)
+    requests = per_rank * world
+    lengths = [requests[i] for i in balanced_assignment(requests, world)[rank]]
     layers = {}
     for layer in range(C.NUM_LAYERS):
         t = synthetic.layer_weights_on_device(layer, device, seed=0)
@@ -292,7 +296,7 @@ def run_ours(args, rank, world, device):
             "kv_len_range": [args.len_lo, args.len_hi],
             "kv_tokens_per_gpu": sum(lengths),
             "kv_block_tokens": 64,
-            "parallelism": f"sequence-sharded x{world} (no collective)",
+            "parallelism": f"sequence-sharded x{world}, KV-length-balanced (no collective)",
             "l2": "inputs larger than L2 (state+KV ~%.0f GB per step)" % (step_bytes / 1e9),
         },
         "roofline": {
@@ -564,7 +568,7 @@ def cpu_reference(args, steps, warmup, sample):
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    lengths = sorted(synthetic.ragged_lengths(args.batch, args.len_lo, args.len_hi, seed=0))
+    lengths = sorted(synthetic.stratified_lengths(args.batch, args.len_lo, args.len_hi, seed=0))
     picks = [lengths[int((i + 0.5) * len(lengths) / sample)] for i in range(sample)]
     dn_w = {k: v for k, v in synthetic.layer_weights(0, 0).items()}
     gqa_w = {k: v for k, v in synthetic.layer_weights(3, 0).items()}

@@ -1,7 +1,8 @@
 """Sequence sharding across GPUs of one node (one process per GPU).
 
 The attention path has no cross-sequence dependency: each rank owns a
-contiguous slice of the requests, holds a replica of the weights and its own
+subset of the requests (a contiguous slice, or a cost-balanced assignment
+when request lengths differ), holds a replica of the weights and its own
 DeltaNet / conv / KV state, and decodes with no collective on the data path.
 The helpers here cover the host-side plumbing around that: which requests a
 rank owns, and gathering small per-rank results after the work (over
@@ -39,6 +40,33 @@ def shard_range(n: int, world: int, rank: int) -> Shard:
     start = rank * base + min(rank, extra)
     stop = start + base + (1 if rank < extra else 0)
     return Shard(rank, world, start, stop)
+
+
+def balanced_assignment(costs: list[int], world: int, per_rank: int | None = None) -> list[list[int]]:
+    """Request indices for each rank so that the ranks' summed costs (e.g. KV
+    lengths, which set a decode step's time) are near equal while every rank
+    gets the same number of requests (``per_rank``, default len/world).
+
+    Longest-first greedy: requests in decreasing cost go to the least-loaded
+    rank that still has room.  Deterministic (ties by rank, then index), so
+    every rank computes the same assignment from the same list without
+    communication.  Each rank's indices are returned in increasing order."""
+    n = len(costs)
+    if world < 1:
+        raise ValueError(f"bad world {world}")
+    if per_rank is None:
+        if n % world:
+            raise ValueError(f"{n} requests do not split evenly over {world} ranks")
+        per_rank = n // world
+    if per_rank * world < n:
+        raise ValueError(f"{n} requests exceed {world} ranks x {per_rank}")
+    load = [0] * world
+    out: list[list[int]] = [[] for _ in range(world)]
+    for i in sorted(range(n), key=lambda k: (-costs[k], k)):
+        r = min((r for r in range(world) if len(out[r]) < per_rank), key=lambda r: (load[r], r))
+        out[r].append(i)
+        load[r] += costs[i]
+    return [sorted(x) for x in out]
 
 
 def env_rank_world() -> tuple[int, int, int]:

@@ -133,6 +133,19 @@ def kv_prefix(length: int, seed: int) -> tuple[torch.Tensor, torch.Tensor]:
 
 
 def ragged_lengths(batch: int, lo: int, hi: int, seed: int) -> list[int]:
-    """Per-sequence KV lengths uniform in [lo, hi] (benchmark configuration 3)."""
+    """Per-sequence KV lengths uniform in [lo, hi] (independent draws)."""
     g = _gen(seed)
     return [int(x) for x in torch.randint(lo, hi + 1, (batch,), generator=g)]
+
+
+def stratified_lengths(batch: int, lo: int, hi: int, seed: int) -> list[int]:
+    """``batch`` KV lengths of U[lo, hi] as a stratified sample -- one length
+    from each of ``batch`` equal-probability strata, at a seeded offset inside
+    its stratum -- in seeded order.  Benchmark configuration 3 gives every GPU
+    such a set, so the work per GPU is the same at any GPU count."""
+    g = _gen(seed)
+    u = (torch.arange(batch, dtype=torch.float64) + torch.rand(batch, generator=g, dtype=torch.float64)) / batch
+    vals = [int(lo + x * (hi - lo + 1)) for x in u.tolist()]
+    vals = [min(max(v, lo), hi) for v in vals]
+    order = torch.randperm(batch, generator=g).tolist()
+    return [vals[i] for i in order]

@@ -12,7 +12,7 @@ from datetime import timedelta
 
 import pytest
 
-from ria_b200.sharding import gather_to_rank0, shard_range
+from ria_b200.sharding import balanced_assignment, gather_to_rank0, shard_range
 
 
 def test_shard_range_balanced_and_complete():
@@ -82,3 +82,22 @@ def test_failed_rank_surfaces_as_error_on_peer():
     res = _run("fail")
     assert res[1][0] == "error" and "injected" in res[1][1]
     assert res[0][0] == "error"  # the gather on rank 0 fails instead of hanging
+
+
+def test_balanced_assignment_equal_counts_and_loads():
+    import random
+
+    rng = random.Random(0)
+    for world in (1, 2, 4, 8):
+        costs = [rng.randint(512, 32768) for _ in range(world * 256)]
+        parts = balanced_assignment(costs, world)
+        assert sorted(i for p in parts for i in p) == list(range(len(costs)))  # a partition
+        assert all(len(p) == 256 for p in parts)
+        loads = [sum(costs[i] for i in p) for p in parts]
+        assert max(loads) - min(loads) <= 32768  # within one request of each other
+        assert parts == balanced_assignment(costs, world)  # deterministic
+
+
+def test_balanced_assignment_rejects_uneven_split():
+    with pytest.raises(ValueError):
+        balanced_assignment([1, 2, 3], 2)
