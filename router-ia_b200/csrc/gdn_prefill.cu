@@ -216,15 +216,36 @@ __device__ __forceinline__ void warp_mma16(float (&d)[2][4], const float* X, int
 __device__ void invert_unit_lower64(float* A, float* T, int tid) {
   const int warp = tid >> 5, lane = tid & 31;
   if (tid < 64) {
+    // column jj of diagonal block d: col[ii] = -sum_{m=jj}^{ii-1} A[ii][m] col[m]
+    // (col[m] = 0 for m < jj, so the sum may run over all m < ii).  The next
+    // row of A is loaded while this one is used, and four partial sums keep
+    // the FMA chain short.
     const int d = tid >> 4, jj = tid & 15, j = 16 * d + jj;
+    const float* Ad = A + 16 * d * kLd + 16 * d;
     float col[16];
+    float cur[16], nxt[16];
 #pragma unroll
-    for (int ii = 0; ii < 16; ++ii) {
-      float acc = 0.f;
+    for (int m = 0; m < 16; ++m) cur[m] = m < 1 ? Ad[kLd + m] : 0.f;  // row 1
 #pragma unroll
-      for (int m = 0; m < ii; ++m)
-        if (m >= jj) acc = fmaf(A[(16 * d + ii) * kLd + 16 * d + m], col[m], acc);
-      col[ii] = (ii < jj) ? 0.f : (ii == jj ? 1.f : -acc);
+    for (int ii = 0; ii < 16; ++ii) {  // cur holds row ii (ii >= 1); row ii + 1 loads meanwhile
+      if (ii >= 1 && ii + 1 < 16) {
+#pragma unroll
+        for (int m = 0; m < 16; ++m)
+          if (m <= ii) nxt[m] = Ad[(ii + 1) * kLd + m];
+      }
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      if (ii >= 1) {
+#pragma unroll
+        for (int m = 0; m < 16; ++m)
+          if (m < ii) acc[m & 3] = fmaf(cur[m], col[m], acc[m & 3]);
+      }
+      const float sum = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+      col[ii] = (ii < jj) ? 0.f : (ii == jj ? 1.f : -sum);
+      if (ii >= 1 && ii + 1 < 16) {
+#pragma unroll
+        for (int m = 0; m < 16; ++m)
+          if (m <= ii) cur[m] = nxt[m];
+      }
     }
 #pragma unroll
     for (int ii = 0; ii < 16; ++ii) T[(16 * d + ii) * kLd + j] = col[ii];
@@ -379,36 +400,37 @@ __global__ void __launch_bounds__(128, 3)
   if (lt < kC) ebk[lt] = bet[lt] * exp2f(gam[lt]) * sk[lt];
 
   // ---- P rows (lanes 0-63) staged over the Q box, A rows (lanes 64-127) to
-  // SMEM.  Rows 0-31 have no entries in columns 32-63 (causal), so warps 0
-  // and 2 skip them.
+  // SMEM, eight columns at a time (a compact loop: three CTAs per SM share
+  // the instruction cache).  Rows 0-31 have no entries in columns 32-63
+  // (causal), so warps 0 and 2 stop at column 32.
   {
-    float v[64];
-    tc::ld32(my_lane + kTmG, v);
-    tc::ld32(my_lane + kTmG + 32, v + 32);
-    tc::wait_ld();
-    const bool upper = (lt & 32) != 0;
-    if (lt < 64) {
-      const int i = lt;
-      const float gi = gam[i], si = sq[i] * kQScale;
+    const bool is_p = lt < 64;
+    const int i = lt & 63;
+    const float gi = gam[i];
+    const float si = is_p ? sq[i] * kQScale : bet[i] * sk[i];
+    const int jend = (lt & 32) ? 64 : 32;
+    float* Arow = reinterpret_cast<float*>(smem + kPA) + i * kLd;
+#pragma unroll 1
+    for (int j0 = 0; j0 < 64; j0 += 8) {
+      float v[8];
+      tc::ld8(my_lane + kTmG + j0, v);
+      tc::wait_ld();
 #pragma unroll
-      for (int j = 0; j < 64; ++j) {
-        if (j < 32 || upper) {
-          const float val = v[j] * si * sk[j] * exp2f(gi - gam[j]);
-          v[j] = (j <= i) ? val : 0.f;
-        } else {
-          v[j] = 0.f;
-        }
+      for (int e = 0; e < 8; ++e) {
+        const int j = j0 + e;
+        const bool keep = j < jend && (is_p ? j <= i : j < i);
+        v[e] = keep ? v[e] * si * sk[j] * exp2f(gi - gam[j]) : 0.f;
       }
-      store_row_bf16<64>(smem + kPX, i, 0, v);
-    } else {
-      const int i = lt - 64;
-      const float gi = gam[i], bi = bet[i] * sk[i];
-      float* A = reinterpret_cast<float*>(smem + kPA);
+      if (is_p) {
+        uint4 pk;
+        pk.x = pack_bf16x2(v[0], v[1]);
+        pk.y = pack_bf16x2(v[2], v[3]);
+        pk.z = pack_bf16x2(v[4], v[5]);
+        pk.w = pack_bf16x2(v[6], v[7]);
+        *reinterpret_cast<uint4*>(smem + kPX + tc::sw128_off(i, j0)) = pk;
+      } else {
 #pragma unroll
-      for (int j = 0; j < 64; ++j) {
-        float val = 0.f;
-        if (j < 32 || upper) val = bi * v[j] * sk[j] * exp2f(gi - gam[j]);
-        A[i * kLd + j] = (j < i) ? val : 0.f;
+        for (int e = 0; e < 8; ++e) Arow[j0 + e] = v[e];
       }
     }
   }
@@ -419,7 +441,7 @@ __global__ void __launch_bounds__(128, 3)
   // over the Q boxes (dims 0-63 over X, 64-127 over Y).  Thread 64 issues it:
   // threads 0-63 run the diagonal-block substitution meanwhile.
   if (lt == 64) {
-    tma_store_2d(&tmW, smem + kPX, 0, rec_row + 256);
+    tma_store_2d(&tmW, smem + kPX, 0, rec_row + kRecP / 128);
     bulk_commit_group();
     bulk_wait_read0();
     mbar_arrive_expect_tx(tma_v, 2 * kBox);
@@ -427,18 +449,22 @@ __global__ void __launch_bounds__(128, 3)
     tma_load_3d(smem + kPY, &tmV, h * kDV + 64, c * kC, b, tma_v);
   }
   invert_unit_lower64(reinterpret_cast<float*>(smem + kPA), reinterpret_cast<float*>(smem + kPT), lt);
-  {
+  {  // TW = T diag(beta e^gamma s_k) (lanes 0-63), TU = T diag(beta) (lanes 64-127), bf16
     const int i = lt & 63;
-    const float* T = reinterpret_cast<const float*>(smem + kPT);
-    float v[64];
-    if (lt < 64) {
+    const float* Trow = reinterpret_cast<const float*>(smem + kPT) + i * kLd;
+    const float* cs = lt < 64 ? ebk : bet;
+    unsigned char* dst = smem + kPA + (lt < 64 ? 0 : kBox);
+#pragma unroll 1
+    for (int j0 = 0; j0 < 64; j0 += 8) {
+      float v[8];
 #pragma unroll
-      for (int j = 0; j < 64; ++j) v[j] = T[i * kLd + j] * ebk[j];
-      store_row_bf16<64>(smem + kPA, i, 0, v);  // TW
-    } else {
-#pragma unroll
-      for (int j = 0; j < 64; ++j) v[j] = T[i * kLd + j] * bet[j];
-      store_row_bf16<64>(smem + kPA + kBox, i, 0, v);  // TU
+      for (int e = 0; e < 8; ++e) v[e] = Trow[j0 + e] * cs[j0 + e];
+      uint4 pk;
+      pk.x = pack_bf16x2(v[0], v[1]);
+      pk.y = pack_bf16x2(v[2], v[3]);
+      pk.z = pack_bf16x2(v[4], v[5]);
+      pk.w = pack_bf16x2(v[6], v[7]);
+      *reinterpret_cast<uint4*>(dst + tc::sw128_off(i, j0)) = pk;
     }
   }
   fence_proxy_async_smem();
@@ -502,10 +528,10 @@ __global__ void __launch_bounds__(128, 3)
   tc::fence_before_sync();
   __syncthreads();
   if (lt == 0) {
-    tma_store_2d(&tmW, smem + kPA, 0, rec_row);
-    tma_store_2d(&tmW, smem + kPA + kBox, 0, rec_row + 64);
-    tma_store_2d(&tmW, smem + kPT, 0, rec_row + 128);
-    tma_store_2d(&tmW, smem + kPT + kBox, 0, rec_row + 192);
+    tma_store_2d(&tmW, smem + kPA, 0, rec_row + kRecW / 128);
+    tma_store_2d(&tmW, smem + kPA + kBox, 0, rec_row + kRecW / 128 + 64);
+    tma_store_2d(&tmW, smem + kPT, 0, rec_row + kRecUT / 128);
+    tma_store_2d(&tmW, smem + kPT + kBox, 0, rec_row + kRecUT / 128 + 64);
     bulk_commit_group();
     bulk_wait_all0();
   }
@@ -565,11 +591,11 @@ __global__ void __launch_bounds__(256, 1)
     tma_load_3d(slot + kSlWQ + 3 * kBox, &tmQ, hk * kDK + 64, c * kC, b, &full[s]);
     tma_load_3d(slot + kSlK, &tmK, hk * kDK, c * kC, b, &full[s]);
     tma_load_3d(slot + kSlK + kBox, &tmK, hk * kDK + 64, c * kC, b, &full[s]);
-    tma_load_2d(slot + kSlWQ, &tmW, 0, row, &full[s]);
-    tma_load_2d(slot + kSlWQ + 2 * kBox, &tmW, 0, row + 64, &full[s]);
-    tma_load_2d(slot + kSlUT, &tmW, 0, row + 128, &full[s]);
-    tma_load_2d(slot + kSlUT + kBox, &tmW, 0, row + 192, &full[s]);
-    tma_load_2d(slot + kSlP, &tmW, 0, row + 256, &full[s]);
+    tma_load_2d(slot + kSlWQ, &tmW, 0, row + kRecW / 128, &full[s]);
+    tma_load_2d(slot + kSlWQ + 2 * kBox, &tmW, 0, row + kRecW / 128 + 64, &full[s]);
+    tma_load_2d(slot + kSlUT, &tmW, 0, row + kRecUT / 128, &full[s]);
+    tma_load_2d(slot + kSlUT + kBox, &tmW, 0, row + kRecUT / 128 + 64, &full[s]);
+    tma_load_2d(slot + kSlP, &tmW, 0, row + kRecP / 128, &full[s]);
     bulk_g2s(slot + kSlScal, p.ws + (rec0 + j) * static_cast<int64_t>(kRecBytes) + kRecScal, kScalBytes, &full[s]);
   };
 

@@ -102,6 +102,14 @@ __device__ __forceinline__ void st32(uint32_t taddr, const float* v) {
       : "memory");
 }
 
+// 8 consecutive fp32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void ld8(uint32_t taddr, float* v) {
+  uint32_t* r = reinterpret_cast<uint32_t*>(v);
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+
 // 16 consecutive 32-bit columns of this thread's TMEM lane.
 __device__ __forceinline__ void st16(uint32_t taddr, const uint32_t* r) {
   asm volatile(
