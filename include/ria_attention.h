@@ -245,6 +245,24 @@ RIA_API int ria_umma_selftest(int32_t a_mn_major, int32_t b_mn_major, int32_t n,
 RIA_API int ria_rmsnorm_rows(const float* x, int64_t x_stride, const float* weight, void* out, int64_t out_stride, int32_t rows,
                      int32_t n, ria_stream_t stream);
 
+/* Small-batch projections (batch <= 8), weight-streaming GEMVs with the
+ * neighbouring row ops fused (the "projection fusion" of the layer steps):
+ *
+ * ria_rmsnorm_gemv: out[b, n] (bf16) = W[n, :] . bf16(rmsnorm(x[b]) * (1 + norm_w)),
+ *   the layer's input RMSNorm (qwen36_op_probe.py:55-67) and its fused
+ *   in-projection (qwen36_attention_cache.py:228-240 DeltaNet, :289-297 GQA);
+ *   x [batch, k] f32, W [n, k] bf16 (row stride w_stride), out bf16.
+ * ria_gemv_residual: out[b, n] (f32) = x0[b, n] + bf16(W[n, :] . a[b]), the
+ *   out-projection and the residual add that end the layer (:272-277, :318-321);
+ *   a [batch, k] bf16, x0 / out f32.
+ * k a multiple of 8 with 16-byte aligned rows; batch * k * 2 <= 96 KiB. */
+RIA_API int ria_rmsnorm_gemv(const float* x, int64_t x_stride, const float* norm_weight, const void* w,
+                             int64_t w_stride, void* out, int64_t out_stride, int32_t batch, int32_t n, int32_t k,
+                             ria_stream_t stream);
+RIA_API int ria_gemv_residual(const void* a, int64_t a_stride, const void* w, int64_t w_stride, const float* x0,
+                              int64_t x0_stride, float* out, int64_t out_stride, int32_t batch, int32_t n, int32_t k,
+                              ria_stream_t stream);
+
 /* out[B, n] f32 = x0[B, n] f32 + proj[B, n] bf16: the residual add that ends
  * _linear_stateful / _full_stateful (qwen36_attention_cache.py:276-277, 320-321). */
 RIA_API int ria_residual_add(const float* x0, int64_t x0_stride, const void* proj, int64_t proj_stride, float* out,

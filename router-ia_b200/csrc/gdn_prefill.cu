@@ -153,23 +153,6 @@ __device__ __forceinline__ float sumsq_row(const unsigned char* box0, const unsi
   return ss;
 }
 
-// Multiply the 64 bf16 of row r of a 128-byte-swizzled box by s in place.
-__device__ __forceinline__ void scale_row_bf16(unsigned char* box, int r, float s) {
-  unsigned char* rowp = box + r * 128;
-#pragma unroll
-  for (int c = 0; c < 8; ++c) {
-    const int ch = c ^ (r & 7);  // bank-spread visiting order
-    uint4 u = *reinterpret_cast<uint4*>(rowp + ch * 16);
-    __nv_bfloat162* h2 = reinterpret_cast<__nv_bfloat162*>(&u);
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float2 f = __bfloat1622float2(h2[e]);
-      h2[e] = __floats2bfloat162_rn(f.x * s, f.y * s);
-    }
-    *reinterpret_cast<uint4*>(rowp + ch * 16) = u;
-  }
-}
-
 // D (+)= A(16x8 tf32, row) * B(8x8 tf32, col), fp32 accumulate.
 __device__ __forceinline__ void mma_tf32_1688(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                               uint32_t b0, uint32_t b1) {

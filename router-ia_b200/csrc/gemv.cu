@@ -1,0 +1,240 @@
+// Small-batch projections (B <= 8) as weight-streaming GEMVs, with the layer
+// input RMSNorm fused into the in-projection and the residual add fused into
+// the out-projection (router-ia qwen36_attention_cache.py:228-240 and
+// :272-277 for DeltaNet, :289-297 and :318-321 for GQA).  At batch 1 the
+// projections read 67 MB of bf16 weights per DeltaNet layer, so the step is
+// bound by that stream; a library GEMM at M = 1 runs well below it, and the
+// separate norm / add launches cost as much as a GEMV.
+//
+// One warp per output row at a time: every lane streams 16-byte chunks of the
+// weight row (coalesced, read once), multiplies them with the B input rows
+// staged in shared memory, and the warp reduces.  The in-projection CTA first
+// recomputes the RMSNorm of its B input rows with the same reduction order as
+// ria_rmsnorm_rows, so both paths produce the same bf16 activations.
+#include <algorithm>
+
+#include "ria_capi_internal.h"
+#include "ria_common.cuh"
+
+namespace {
+
+constexpr int kMaxBatch = 8;
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+
+// One warp per output row at a time, rows strided over all warps of the grid.
+// A lane holds KC 16-byte chunks of the row (the whole row is in flight at
+// once) and prefetches the next row's chunks while it reduces the current.
+// pro() runs once the first row's loads are issued (it stages the inputs, so
+// the two overlap); f(row, acc[B]) consumes each finished row (lane 0's
+// values are the sums).
+template <int B, int KC, class P, class F>
+__device__ __forceinline__ void gemv_rows(const __nv_bfloat16* __restrict__ w, int64_t ws,
+                                          const __nv_bfloat16* xs, int n, P&& pro, F&& f) {
+  constexpr int k = KC * 256;
+  const int lane = threadIdx.x & 31;
+  const int warps = gridDim.x * kWarps;
+  int row = blockIdx.x * kWarps + (threadIdx.x >> 5);
+  uint4 cur[KC], nxt[KC];
+  if (row < n) {
+#pragma unroll
+    for (int c = 0; c < KC; ++c)
+      cur[c] = __ldg(reinterpret_cast<const uint4*>(w + static_cast<int64_t>(row) * ws + c * 256 + lane * 8));
+  }
+  pro();
+  for (; row < n; row += warps) {
+    const int next = row + warps;
+    if (next < n) {
+#pragma unroll
+      for (int c = 0; c < KC; ++c)
+        nxt[c] = __ldg(reinterpret_cast<const uint4*>(w + static_cast<int64_t>(next) * ws + c * 256 + lane * 8));
+    }
+    float acc[B];
+#pragma unroll
+    for (int b = 0; b < B; ++b) acc[b] = 0.f;
+#pragma unroll
+    for (int c = 0; c < KC; ++c) {
+      const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&cur[c]);
+#pragma unroll
+      for (int b = 0; b < B; ++b) {
+        const uint4 u = *reinterpret_cast<const uint4*>(xs + b * k + c * 256 + lane * 8);
+        const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 wf = __bfloat1622float2(w2[e]);
+          const float2 xf = __bfloat1622float2(x2[e]);
+          acc[b] = fmaf(wf.x, xf.x, acc[b]);
+          acc[b] = fmaf(wf.y, xf.y, acc[b]);
+        }
+      }
+    }
+#pragma unroll
+    for (int b = 0; b < B; ++b) acc[b] = warp_sum(acc[b]);
+    f(row, acc);
+#pragma unroll
+    for (int c = 0; c < KC; ++c) cur[c] = nxt[c];
+  }
+}
+
+// out[b, :] = bf16(W . bf16(rmsnorm(x[b]) * (1 + norm_w)))
+template <int B, int KC>
+__global__ void __launch_bounds__(kThreads) rmsnorm_gemv_kernel(const float* __restrict__ x, int64_t xs,
+                                                                const float* __restrict__ norm_w,
+                                                                const __nv_bfloat16* __restrict__ w, int64_t ws,
+                                                                __nv_bfloat16* __restrict__ out, int64_t os, int n) {
+  constexpr int k = KC * 256;
+  extern __shared__ __align__(16) unsigned char smem[];
+  __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(smem);  // [B][k]
+  __shared__ float red[kWarps];
+  auto norm = [&]() {
+    for (int b = 0; b < B; ++b) {  // the reduction order of rmsnorm_rows_kernel
+      const float* xr = x + b * xs;
+      float ss = 0.f;
+      for (int i = threadIdx.x * 4; i < k; i += kThreads * 4) {
+        const float4 v = *reinterpret_cast<const float4*>(xr + i);
+        ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+      }
+      ss = warp_sum(ss);
+      if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+      __syncthreads();
+      float tot = 0.f;
+      for (int i = 0; i < kWarps; ++i) tot += red[i];
+      const float r = rsqrtf(tot / static_cast<float>(k) + 1e-6f);
+      for (int i = threadIdx.x * 4; i < k; i += kThreads * 4) {
+        const float4 v = *reinterpret_cast<const float4*>(xr + i);
+        const float4 ww = *reinterpret_cast<const float4*>(norm_w + i);
+        uint2 pk;
+        pk.x = pack_bf16x2(v.x * r * (1.f + ww.x), v.y * r * (1.f + ww.y));
+        pk.y = pack_bf16x2(v.z * r * (1.f + ww.z), v.w * r * (1.f + ww.w));
+        *reinterpret_cast<uint2*>(h + b * k + i) = pk;
+      }
+      __syncthreads();  // red is reused by the next row; h is complete
+    }
+  };
+  gemv_rows<B, KC>(w, ws, h, n, norm, [&](int row, const float (&acc)[B]) {
+    if ((threadIdx.x & 31) == 0)
+#pragma unroll
+      for (int b = 0; b < B; ++b) out[b * os + row] = __float2bfloat16_rn(acc[b]);
+  });
+}
+
+// out[b, :] = x0[b, :] + bf16(W . a[b])  (the projection rounded to bf16 as
+// the library GEMM's output would be, then added in fp32)
+template <int B, int KC>
+__global__ void __launch_bounds__(kThreads) gemv_residual_kernel(const __nv_bfloat16* __restrict__ a, int64_t as,
+                                                                 const __nv_bfloat16* __restrict__ w, int64_t ws,
+                                                                 const float* __restrict__ x0, int64_t x0s,
+                                                                 float* __restrict__ out, int64_t os, int n) {
+  constexpr int k = KC * 256;
+  extern __shared__ __align__(16) unsigned char smem[];
+  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem);  // [B][k]
+  auto stage = [&]() {
+    for (int b = 0; b < B; ++b)
+      for (int i = threadIdx.x * 8; i < k; i += kThreads * 8)
+        *reinterpret_cast<uint4*>(xs + b * k + i) = *reinterpret_cast<const uint4*>(a + b * as + i);
+    __syncthreads();
+  };
+  gemv_rows<B, KC>(w, ws, xs, n, stage, [&](int row, const float (&acc)[B]) {
+    if ((threadIdx.x & 31) == 0)
+#pragma unroll
+      for (int b = 0; b < B; ++b) out[b * os + row] = x0[b * x0s + row] + bf16_round(acc[b]);
+  });
+}
+
+int check_common(const char* what, const void* w, int64_t w_stride, int32_t batch, int32_t n, int32_t k) {
+  if (batch < 0 || batch > kMaxBatch || n <= 0)
+    return ria::fail(RIA_ERR_INVALID, "%s: batch %d (max %d), n %d", what, batch, kMaxBatch, n);
+  if (k != 2048 && k != 4096)
+    return ria::fail(RIA_ERR_INVALID, "%s: k %d (the layer widths 2048 and 4096 are compiled)", what, k);
+  if (w_stride < k || w_stride % 8 || !ria::aligned(w, 16))
+    return ria::fail(RIA_ERR_INVALID, "%s: weight rows must be 16-byte aligned", what);
+  return RIA_OK;
+}
+
+// CTAs per SM that fit beside each other (a lane keeps 2 x KC chunks in
+// registers): two for 2048-wide rows, one for 4096; the row loop covers the rest.
+int grid_for(int n, int kc) {
+  const int per_sm = kc <= 8 ? 2 : 1;
+  return std::max(1, std::min(per_sm * ria::num_sms(), (n + kWarps - 1) / kWarps));
+}
+
+
+template <int B, int KC>
+cudaError_t launch_rg(const float* x, int64_t xs, const float* nw, const __nv_bfloat16* w, int64_t ws,
+                      __nv_bfloat16* out, int64_t os, int n, cudaStream_t st) {
+  const int smem = B * KC * 256 * 2;
+  cudaError_t e = cudaFuncSetAttribute(rmsnorm_gemv_kernel<B, KC>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e == cudaSuccess) rmsnorm_gemv_kernel<B, KC><<<grid_for(n, KC), kThreads, smem, st>>>(x, xs, nw, w, ws, out, os, n);
+  return e;
+}
+
+template <int B, int KC>
+cudaError_t launch_gr(const __nv_bfloat16* a, int64_t as, const __nv_bfloat16* w, int64_t ws, const float* x0,
+                      int64_t x0s, float* out, int64_t os, int n, cudaStream_t st) {
+  const int smem = B * KC * 256 * 2;
+  cudaError_t e = cudaFuncSetAttribute(gemv_residual_kernel<B, KC>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e == cudaSuccess) gemv_residual_kernel<B, KC><<<grid_for(n, KC), kThreads, smem, st>>>(a, as, w, ws, x0, x0s, out, os, n);
+  return e;
+}
+
+template <int KC, class L>
+cudaError_t by_batch(int batch, L&& launch) {
+  switch (batch) {
+    case 1: return launch(std::integral_constant<int, 1>{});
+    case 2: return launch(std::integral_constant<int, 2>{});
+    case 3: return launch(std::integral_constant<int, 3>{});
+    case 4: return launch(std::integral_constant<int, 4>{});
+    case 5: return launch(std::integral_constant<int, 5>{});
+    case 6: return launch(std::integral_constant<int, 6>{});
+    case 7: return launch(std::integral_constant<int, 7>{});
+    default: return launch(std::integral_constant<int, 8>{});
+  }
+}
+
+}  // namespace
+
+extern "C" int ria_rmsnorm_gemv(const float* x, int64_t x_stride, const float* norm_weight, const void* w,
+                                int64_t w_stride, void* out, int64_t out_stride, int32_t batch, int32_t n, int32_t k,
+                                ria_stream_t stream) {
+  int rc = check_common("ria_rmsnorm_gemv", w, w_stride, batch, n, k);
+  if (rc) return rc;
+  if (batch == 0) return RIA_OK;
+  if (!x || !norm_weight || !out) return ria::fail(RIA_ERR_INVALID, "ria_rmsnorm_gemv: null pointer");
+  if (x_stride % 4 || !ria::aligned(x, 16) || !ria::aligned(norm_weight, 16))
+    return ria::fail(RIA_ERR_INVALID, "ria_rmsnorm_gemv: x rows must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const __nv_bfloat16* wb = static_cast<const __nv_bfloat16*>(w);
+  __nv_bfloat16* ob = static_cast<__nv_bfloat16*>(out);
+  auto go = [&](auto kc) {
+    constexpr int KC = decltype(kc)::value;
+    return by_batch<KC>(batch, [&](auto bb) {
+      return launch_rg<decltype(bb)::value, KC>(x, x_stride, norm_weight, wb, w_stride, ob, out_stride, n, st);
+    });
+  };
+  const cudaError_t e = k == 2048 ? go(std::integral_constant<int, 8>{}) : go(std::integral_constant<int, 16>{});
+  if (e != cudaSuccess) return ria::fail(RIA_ERR_CUDA, "ria_rmsnorm_gemv: %s", cudaGetErrorString(e));
+  return ria::check_launch("ria_rmsnorm_gemv");
+}
+
+extern "C" int ria_gemv_residual(const void* a, int64_t a_stride, const void* w, int64_t w_stride, const float* x0,
+                                 int64_t x0_stride, float* out, int64_t out_stride, int32_t batch, int32_t n, int32_t k,
+                                 ria_stream_t stream) {
+  int rc = check_common("ria_gemv_residual", w, w_stride, batch, n, k);
+  if (rc) return rc;
+  if (batch == 0) return RIA_OK;
+  if (!a || !x0 || !out) return ria::fail(RIA_ERR_INVALID, "ria_gemv_residual: null pointer");
+  if (a_stride % 8 || !ria::aligned(a, 16))
+    return ria::fail(RIA_ERR_INVALID, "ria_gemv_residual: input rows must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const __nv_bfloat16* ab = static_cast<const __nv_bfloat16*>(a);
+  const __nv_bfloat16* wb = static_cast<const __nv_bfloat16*>(w);
+  auto go = [&](auto kc) {
+    constexpr int KC = decltype(kc)::value;
+    return by_batch<KC>(batch, [&](auto bb) {
+      return launch_gr<decltype(bb)::value, KC>(ab, a_stride, wb, w_stride, x0, x0_stride, out, out_stride, n, st);
+    });
+  };
+  const cudaError_t e = k == 2048 ? go(std::integral_constant<int, 8>{}) : go(std::integral_constant<int, 16>{});
+  if (e != cudaSuccess) return ria::fail(RIA_ERR_CUDA, "ria_gemv_residual: %s", cudaGetErrorString(e));
+  return ria::check_launch("ria_gemv_residual");
+}

@@ -414,14 +414,39 @@ __global__ void __launch_bounds__(kD) gqa_combine_kernel(const GqaParams p) {
   const int nsplit = min(cdiv(npages, p.split_pages), p.max_splits);
   if (nsplit <= 1) return;
   const float* lse = p.part_lse + static_cast<int64_t>(b) * p.max_splits * kHq + hq;
+  // Per-split weights 2^(lse - max) once, in chunks of kD splits in shared
+  // memory; then each thread sums its dimension over the chunk with 16
+  // partial loads in flight.
+  __shared__ float wts[kD];
+  __shared__ float red[kD / 32];
   float M = -INFINITY;
-  for (int s = 0; s < nsplit; ++s) M = fmaxf(M, lse[s * kHq]);
+  for (int s = d; s < nsplit; s += kD) M = fmaxf(M, lse[s * kHq]);
+  M = warp_max(M);
+  if ((d & 31) == 0) red[d >> 5] = M;
+  __syncthreads();
+  M = red[0];
+#pragma unroll
+  for (int i = 1; i < kD / 32; ++i) M = fmaxf(M, red[i]);
   float acc = 0.f, wsum = 0.f;
   const float* po = p.part_o + (static_cast<int64_t>(b) * p.max_splits * kHq + hq) * kD + d;
-  for (int s = 0; s < nsplit; ++s) {
-    const float w = exp2f(lse[s * kHq] - M);
-    wsum += w;
-    acc = fmaf(w, po[static_cast<int64_t>(s) * kHq * kD], acc);
+  for (int c0 = 0; c0 < nsplit; c0 += kD) {
+    const int cn = min(kD, nsplit - c0);
+    __syncthreads();  // the previous chunk's weights are consumed
+    if (d < cn) wts[d] = exp2f(lse[(c0 + d) * kHq] - M);
+    __syncthreads();
+    constexpr int kInFlight = 16;
+    for (int s0 = 0; s0 < cn; s0 += kInFlight) {
+      float o[kInFlight];
+#pragma unroll
+      for (int i = 0; i < kInFlight; ++i)
+        o[i] = s0 + i < cn ? po[static_cast<int64_t>(c0 + s0 + i) * kHq * kD] : 0.f;
+#pragma unroll
+      for (int i = 0; i < kInFlight; ++i) {
+        const float w = s0 + i < cn ? wts[s0 + i] : 0.f;
+        wsum += w;
+        acc = fmaf(w, o[i], acc);
+      }
+    }
   }
   const float gz = __bfloat162float(p.q[static_cast<int64_t>(b) * p.q_stride + hq * 2 * kD + kD + d]);
   p.out[static_cast<int64_t>(b) * p.out_stride + hq * kD + d] =

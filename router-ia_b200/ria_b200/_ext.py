@@ -66,6 +66,11 @@ _SIGNATURES: dict[str, tuple[object, list]] = {
          c_int64, c_void_p, c_int32, c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_int64, c_int32, c_int32,
          c_int32, c_void_p],
     ),
+    "ria_rmsnorm_gemv": (
+        c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_void_p, c_int64, c_int32, c_int32, c_int32, c_void_p]),
+    "ria_gemv_residual": (
+        c_int, [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_int32, c_int32, c_int32,
+                c_void_p]),
     "ria_gdn_chunk_prefill_workspace_bytes": (c_int64, [c_int32, c_int32, c_int32]),
     "ria_gdn_chunk_prefill": (
         c_int,
@@ -326,6 +331,27 @@ def advance_positions(seq_lens, positions):
     with _Hooked("advance"):
         rc = lib().ria_advance_positions(seq_lens.data_ptr(), positions.data_ptr(), seq_lens.shape[0], _stream(seq_lens))
     _check(rc, "ria_advance_positions")
+
+
+GEMV_MAX_BATCH = 8
+
+
+def rmsnorm_gemv(x, norm_w, w, out):
+    """out [B, n] bf16 = w [n, k] . bf16(rmsnorm(x [B, k] f32) * (1 + norm_w)), B <= 8."""
+    _require_cuda(x, norm_w, w, out)
+    with _Hooked("rmsnorm_gemv"):
+        rc = lib().ria_rmsnorm_gemv(x.data_ptr(), x.stride(0), norm_w.data_ptr(), w.data_ptr(), w.stride(0),
+                                    out.data_ptr(), out.stride(0), x.shape[0], w.shape[0], w.shape[1], _stream(x))
+    _check(rc, "ria_rmsnorm_gemv")
+
+
+def gemv_residual(a, w, x0, out):
+    """out [B, n] f32 = x0 + bf16(w [n, k] . a [B, k] bf16), B <= 8."""
+    _require_cuda(a, w, x0, out)
+    with _Hooked("gemv_residual"):
+        rc = lib().ria_gemv_residual(a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), x0.data_ptr(), x0.stride(0),
+                                     out.data_ptr(), out.stride(0), a.shape[0], w.shape[0], w.shape[1], _stream(a))
+    _check(rc, "ria_gemv_residual")
 
 
 def rmsnorm_rows(x, weight, out):

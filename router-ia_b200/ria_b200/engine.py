@@ -34,22 +34,44 @@ def _cdiv(a: int, b: int) -> int:
     return (a + b - 1) // b
 
 
+def _in_projection(x: torch.Tensor, w: DeltaNetWeights | GqaWeights) -> torch.Tensor:
+    """bf16(rmsnorm(x) * (1 + w)) through the layer's fused in-projection: one
+    weight-streaming GEMV kernel with the norm fused for small batches, the
+    norm kernel plus a library GEMM otherwise."""
+    batch = x.shape[0]
+    if batch <= _ext.GEMV_MAX_BATCH:
+        proj = torch.empty(batch, w.w_in.shape[0], dtype=torch.bfloat16, device=x.device)
+        _ext.rmsnorm_gemv(x, w.in_norm, w.w_in, proj)
+        return proj
+    h = torch.empty(batch, C.HIDDEN, dtype=torch.bfloat16, device=x.device)
+    _ext.rmsnorm_rows(x, w.in_norm, h)
+    return F.linear(h, w.w_in)
+
+
+def _out_projection(a: torch.Tensor, w: DeltaNetWeights | GqaWeights, x: torch.Tensor) -> torch.Tensor:
+    """x + bf16(a . w_out^T): the out-projection and the residual add, fused
+    into one GEMV kernel for small batches."""
+    batch = a.shape[0]
+    out = torch.empty(batch, C.HIDDEN, dtype=torch.float32, device=x.device)
+    if batch <= _ext.GEMV_MAX_BATCH:
+        _ext.gemv_residual(a, w.w_out, x, out)
+        return out
+    o = F.linear(a, w.w_out)
+    _ext.residual_add(x, o, out)
+    return out
+
+
 def deltanet_decode(x: torch.Tensor, w: DeltaNetWeights, rec: torch.Tensor, conv: torch.Tensor,
                     slots: torch.Tensor | None = None) -> torch.Tensor:
     """One DeltaNet layer step for ``x`` [B, 2048] fp32; returns the residual."""
     batch = x.shape[0]
-    h = torch.empty(batch, C.HIDDEN, dtype=torch.bfloat16, device=x.device)
-    _ext.rmsnorm_rows(x, w.in_norm, h)
-    proj = F.linear(h, w.w_in)
+    proj = _in_projection(x, w)
     gated = torch.empty(batch, C.LINEAR_VALUE_DIM, dtype=torch.bfloat16, device=x.device)
     _ext.gdn_decode_step(
         proj[:, C.DN_PROJ_QKV[0]:C.DN_PROJ_QKV[1]], proj[:, C.DN_PROJ_Z[0]:C.DN_PROJ_Z[1]],
         proj[:, C.DN_PROJ_B[0]:C.DN_PROJ_B[1]], proj[:, C.DN_PROJ_A[0]:C.DN_PROJ_A[1]],
         w.conv_w, w.a_log, w.dt_bias, w.norm_w, conv, rec, slots, gated)
-    o = F.linear(gated, w.w_out)
-    out = torch.empty(batch, C.HIDDEN, dtype=torch.float32, device=x.device)
-    _ext.residual_add(x, o, out)
-    return out
+    return _out_projection(gated, w, x)
 
 
 @dataclass
@@ -81,19 +103,14 @@ def gqa_decode(x: torch.Tensor, w: GqaWeights, k_pool: torch.Tensor, v_pool: tor
     """One GQA layer step for ``x`` [B, 2048] fp32; returns the residual.  The
     new token of sequence i is appended to the pool at index seq_lens[i]."""
     batch = x.shape[0]
-    h = torch.empty(batch, C.HIDDEN, dtype=torch.bfloat16, device=x.device)
-    _ext.rmsnorm_rows(x, w.in_norm, h)
-    proj = F.linear(h, w.w_in)
+    proj = _in_projection(x, w)
     attn = torch.empty(batch, C.FULL_Q_DIM, dtype=torch.bfloat16, device=x.device)
     _ext.gqa_decode_paged(
         proj[:, C.GQA_PROJ_Q[0]:C.GQA_PROJ_Q[1]], proj[:, C.GQA_PROJ_K[0]:C.GQA_PROJ_K[1]],
         proj[:, C.GQA_PROJ_V[0]:C.GQA_PROJ_V[1]], w.q_norm, w.k_norm, inv_freq, k_pool, v_pool, block_table,
         seq_lens, positions, attn, launch.workspace, launch.split_pages, launch.max_splits,
         seq_len0=seq_len0, position0=position0)
-    o = F.linear(attn, w.w_out)
-    out = torch.empty(batch, C.HIDDEN, dtype=torch.float32, device=x.device)
-    _ext.residual_add(x, o, out)
-    return out
+    return _out_projection(attn, w, x)
 
 
 def deltanet_prefill(x: torch.Tensor, w: DeltaNetWeights, rec: torch.Tensor, conv: torch.Tensor) -> torch.Tensor:
