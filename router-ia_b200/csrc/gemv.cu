@@ -23,38 +23,37 @@ constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 
 // One warp per output row at a time, rows strided over all warps of the grid.
-// A lane holds KC 16-byte chunks of the row (the whole row is in flight at
-// once) and prefetches the next row's chunks while it reduces the current.
-// pro() runs once the first row's loads are issued (it stages the inputs, so
-// the two overlap); f(row, acc[B]) consumes each finished row (lane 0's
-// values are the sums).
-template <int B, int KC, class P, class F>
+// A lane holds KC 16-byte chunks of a row (the whole row is in flight at
+// once) in a ring of D rows: rows r + warps .. r + (D-1) warps are loading
+// while row r is reduced.  pro() runs once the first rows' loads are issued
+// (it stages the inputs, so the two overlap); f(row, acc[B]) consumes each
+// finished row (lane 0's values are the sums).
+template <int B, int KC, int D, class P, class F>
 __device__ __forceinline__ void gemv_rows(const __nv_bfloat16* __restrict__ w, int64_t ws,
                                           const __nv_bfloat16* xs, int n, P&& pro, F&& f) {
   constexpr int k = KC * 256;
   const int lane = threadIdx.x & 31;
   const int warps = gridDim.x * kWarps;
-  int row = blockIdx.x * kWarps + (threadIdx.x >> 5);
-  uint4 cur[KC], nxt[KC];
-  if (row < n) {
-#pragma unroll
-    for (int c = 0; c < KC; ++c)
-      cur[c] = __ldg(reinterpret_cast<const uint4*>(w + static_cast<int64_t>(row) * ws + c * 256 + lane * 8));
-  }
-  pro();
-  for (; row < n; row += warps) {
-    const int next = row + warps;
-    if (next < n) {
+  const int row0 = blockIdx.x * kWarps + (threadIdx.x >> 5);
+  uint4 ring[D][KC];
+  auto load = [&](int slot, int row) {
+    if (row < n) {
 #pragma unroll
       for (int c = 0; c < KC; ++c)
-        nxt[c] = __ldg(reinterpret_cast<const uint4*>(w + static_cast<int64_t>(next) * ws + c * 256 + lane * 8));
+        ring[slot][c] =
+            __ldg(reinterpret_cast<const uint4*>(w + static_cast<int64_t>(row) * ws + c * 256 + lane * 8));
     }
+  };
+#pragma unroll
+  for (int d = 0; d < D; ++d) load(d, row0 + d * warps);
+  pro();
+  for (int row = row0; row < n; row += warps) {
     float acc[B];
 #pragma unroll
     for (int b = 0; b < B; ++b) acc[b] = 0.f;
 #pragma unroll
     for (int c = 0; c < KC; ++c) {
-      const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&cur[c]);
+      const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&ring[0][c]);
 #pragma unroll
       for (int b = 0; b < B; ++b) {
         const uint4 u = *reinterpret_cast<const uint4*>(xs + b * k + c * 256 + lane * 8);
@@ -69,15 +68,19 @@ __device__ __forceinline__ void gemv_rows(const __nv_bfloat16* __restrict__ w, i
       }
     }
 #pragma unroll
+    for (int d = 0; d + 1 < D; ++d)
+#pragma unroll
+      for (int c = 0; c < KC; ++c) ring[d][c] = ring[d + 1][c];
+    if (D > 1) load(D - 1, row + D * warps);
+#pragma unroll
     for (int b = 0; b < B; ++b) acc[b] = warp_sum(acc[b]);
     f(row, acc);
-#pragma unroll
-    for (int c = 0; c < KC; ++c) cur[c] = nxt[c];
+    if (D == 1) load(0, row + warps);
   }
 }
 
 // out[b, :] = bf16(W . bf16(rmsnorm(x[b]) * (1 + norm_w)))
-template <int B, int KC>
+template <int B, int KC, int D>
 __global__ void __launch_bounds__(kThreads) rmsnorm_gemv_kernel(const float* __restrict__ x, int64_t xs,
                                                                 const float* __restrict__ norm_w,
                                                                 const __nv_bfloat16* __restrict__ w, int64_t ws,
@@ -111,7 +114,7 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_gemv_kernel(const float* __r
       __syncthreads();  // red is reused by the next row; h is complete
     }
   };
-  gemv_rows<B, KC>(w, ws, h, n, norm, [&](int row, const float (&acc)[B]) {
+  gemv_rows<B, KC, D>(w, ws, h, n, norm, [&](int row, const float (&acc)[B]) {
     if ((threadIdx.x & 31) == 0)
 #pragma unroll
       for (int b = 0; b < B; ++b) out[b * os + row] = __float2bfloat16_rn(acc[b]);
@@ -120,7 +123,7 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_gemv_kernel(const float* __r
 
 // out[b, :] = x0[b, :] + bf16(W . a[b])  (the projection rounded to bf16 as
 // the library GEMM's output would be, then added in fp32)
-template <int B, int KC>
+template <int B, int KC, int D>
 __global__ void __launch_bounds__(kThreads) gemv_residual_kernel(const __nv_bfloat16* __restrict__ a, int64_t as,
                                                                  const __nv_bfloat16* __restrict__ w, int64_t ws,
                                                                  const float* __restrict__ x0, int64_t x0s,
@@ -134,7 +137,7 @@ __global__ void __launch_bounds__(kThreads) gemv_residual_kernel(const __nv_bflo
         *reinterpret_cast<uint4*>(xs + b * k + i) = *reinterpret_cast<const uint4*>(a + b * as + i);
     __syncthreads();
   };
-  gemv_rows<B, KC>(w, ws, xs, n, stage, [&](int row, const float (&acc)[B]) {
+  gemv_rows<B, KC, D>(w, ws, xs, n, stage, [&](int row, const float (&acc)[B]) {
     if ((threadIdx.x & 31) == 0)
 #pragma unroll
       for (int b = 0; b < B; ++b) out[b * os + row] = x0[b * x0s + row] + bf16_round(acc[b]);
@@ -151,29 +154,38 @@ int check_common(const char* what, const void* w, int64_t w_stride, int32_t batc
   return RIA_OK;
 }
 
-// CTAs per SM that fit beside each other (a lane keeps 2 x KC chunks in
-// registers): two for 2048-wide rows, one for 4096; the row loop covers the rest.
-int grid_for(int n, int kc) {
-  const int per_sm = kc <= 8 ? 2 : 1;
-  return std::max(1, std::min(per_sm * ria::num_sms(), (n + kWarps - 1) / kWarps));
+// Launch shape: rows that fit one per warp at two CTAs per SM need no
+// prefetch ring (D = 1); otherwise one row ahead (D = 2), two CTAs per SM for
+// 2048-wide rows and one for 4096-wide rows (register budget).  A ring two
+// rows deep measured slower than one for the 2048-wide rows.
+struct Shape {
+  int grid, depth;
+};
+Shape shape_for(int n, int kc) {
+  const int sms = ria::num_sms();
+  const int ctas_for_rows = (n + kWarps - 1) / kWarps;
+  if (ctas_for_rows <= 2 * sms) return {ctas_for_rows, 1};
+  return kc <= 8 ? Shape{2 * sms, 2} : Shape{sms, 2};
 }
 
-
-template <int B, int KC>
+template <int B, int KC, int D>
 cudaError_t launch_rg(const float* x, int64_t xs, const float* nw, const __nv_bfloat16* w, int64_t ws,
-                      __nv_bfloat16* out, int64_t os, int n, cudaStream_t st) {
+                      __nv_bfloat16* out, int64_t os, int n, int grid, cudaStream_t st) {
   const int smem = B * KC * 256 * 2;
-  cudaError_t e = cudaFuncSetAttribute(rmsnorm_gemv_kernel<B, KC>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e == cudaSuccess) rmsnorm_gemv_kernel<B, KC><<<grid_for(n, KC), kThreads, smem, st>>>(x, xs, nw, w, ws, out, os, n);
+  cudaError_t e =
+      cudaFuncSetAttribute(rmsnorm_gemv_kernel<B, KC, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e == cudaSuccess) rmsnorm_gemv_kernel<B, KC, D><<<grid, kThreads, smem, st>>>(x, xs, nw, w, ws, out, os, n);
   return e;
 }
 
-template <int B, int KC>
+template <int B, int KC, int D>
 cudaError_t launch_gr(const __nv_bfloat16* a, int64_t as, const __nv_bfloat16* w, int64_t ws, const float* x0,
-                      int64_t x0s, float* out, int64_t os, int n, cudaStream_t st) {
+                      int64_t x0s, float* out, int64_t os, int n, int grid, cudaStream_t st) {
   const int smem = B * KC * 256 * 2;
-  cudaError_t e = cudaFuncSetAttribute(gemv_residual_kernel<B, KC>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e == cudaSuccess) gemv_residual_kernel<B, KC><<<grid_for(n, KC), kThreads, smem, st>>>(a, as, w, ws, x0, x0s, out, os, n);
+  cudaError_t e =
+      cudaFuncSetAttribute(gemv_residual_kernel<B, KC, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e == cudaSuccess)
+    gemv_residual_kernel<B, KC, D><<<grid, kThreads, smem, st>>>(a, as, w, ws, x0, x0s, out, os, n);
   return e;
 }
 
@@ -205,13 +217,21 @@ extern "C" int ria_rmsnorm_gemv(const float* x, int64_t x_stride, const float* n
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const __nv_bfloat16* wb = static_cast<const __nv_bfloat16*>(w);
   __nv_bfloat16* ob = static_cast<__nv_bfloat16*>(out);
-  auto go = [&](auto kc) {
-    constexpr int KC = decltype(kc)::value;
+  const int kc = k / 256;
+  const Shape sh = shape_for(n, kc);
+  auto go = [&](auto kcc, auto dd) {
+    constexpr int KC = decltype(kcc)::value, D = decltype(dd)::value;
     return by_batch<KC>(batch, [&](auto bb) {
-      return launch_rg<decltype(bb)::value, KC>(x, x_stride, norm_weight, wb, w_stride, ob, out_stride, n, st);
+      return launch_rg<decltype(bb)::value, KC, D>(x, x_stride, norm_weight, wb, w_stride, ob, out_stride, n,
+                                                   sh.grid, st);
     });
   };
-  const cudaError_t e = k == 2048 ? go(std::integral_constant<int, 8>{}) : go(std::integral_constant<int, 16>{});
+  using I8 = std::integral_constant<int, 8>;
+  using I16 = std::integral_constant<int, 16>;
+  using D1 = std::integral_constant<int, 1>;
+  using D2 = std::integral_constant<int, 2>;
+  const cudaError_t e = kc == 8 ? (sh.depth == 1 ? go(I8{}, D1{}) : go(I8{}, D2{}))
+                                : (sh.depth == 1 ? go(I16{}, D1{}) : go(I16{}, D2{}));
   if (e != cudaSuccess) return ria::fail(RIA_ERR_CUDA, "ria_rmsnorm_gemv: %s", cudaGetErrorString(e));
   return ria::check_launch("ria_rmsnorm_gemv");
 }
@@ -228,13 +248,21 @@ extern "C" int ria_gemv_residual(const void* a, int64_t a_stride, const void* w,
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const __nv_bfloat16* ab = static_cast<const __nv_bfloat16*>(a);
   const __nv_bfloat16* wb = static_cast<const __nv_bfloat16*>(w);
-  auto go = [&](auto kc) {
-    constexpr int KC = decltype(kc)::value;
+  const int kc = k / 256;
+  const Shape sh = shape_for(n, kc);
+  auto go = [&](auto kcc, auto dd) {
+    constexpr int KC = decltype(kcc)::value, D = decltype(dd)::value;
     return by_batch<KC>(batch, [&](auto bb) {
-      return launch_gr<decltype(bb)::value, KC>(ab, a_stride, wb, w_stride, x0, x0_stride, out, out_stride, n, st);
+      return launch_gr<decltype(bb)::value, KC, D>(ab, a_stride, wb, w_stride, x0, x0_stride, out, out_stride, n,
+                                                   sh.grid, st);
     });
   };
-  const cudaError_t e = k == 2048 ? go(std::integral_constant<int, 8>{}) : go(std::integral_constant<int, 16>{});
+  using I8 = std::integral_constant<int, 8>;
+  using I16 = std::integral_constant<int, 16>;
+  using D1 = std::integral_constant<int, 1>;
+  using D2 = std::integral_constant<int, 2>;
+  const cudaError_t e = kc == 8 ? (sh.depth == 1 ? go(I8{}, D1{}) : go(I8{}, D2{}))
+                                : (sh.depth == 1 ? go(I16{}, D1{}) : go(I16{}, D2{}));
   if (e != cudaSuccess) return ria::fail(RIA_ERR_CUDA, "ria_gemv_residual: %s", cudaGetErrorString(e));
   return ria::check_launch("ria_gemv_residual");
 }
