@@ -12,6 +12,9 @@ it, as the checker.  It restates, in plain torch CPU code, the arithmetic of:
 * ``_linear_stateful``     qwen36_attention_cache.py:224-282 (CPU path: fp32
   projections, conv in the conv weight dtype)
 * ``_full_stateful``       qwen36_attention_cache.py:285-324 (CPU path: fp32)
+* ``route``                v2/src/router_ia/qwen36_router.py:96-133 and the
+  MoE block ``batched_moe_step`` qwen36_chat_batch.py:127-178 (CPU path: fp32
+  router, experts, shared expert and its sigmoid gate)
 * the gated delta rule, recurrent and chunked (C=64, WY/UT), as in
   transformers 5.5.0 ``models/qwen3_5_moe/modeling_qwen3_5_moe.py``
   ``torch_recurrent_gated_delta_rule`` (:315-354) and
@@ -310,6 +313,45 @@ def chunk_gated_delta_rule(q, k, v, g, beta, chunk_size=64, initial_state=None, 
             ki * (g_last[..., None] - g[:, :, i]).exp()[..., None]).transpose(-1, -2) @ v_new
     out = out.reshape(B, H, n * C, Dv)[:, :, :T]
     return out.transpose(1, 2).contiguous(), state
+
+
+def route(hidden: torch.Tensor, gate_weight: torch.Tensor, top_k: int):
+    """Router (qwen36_router.py:96-133): logits = hidden @ W^T in the gate
+    weight's dtype (fp32 here), the top_k largest, softmax over them.
+    hidden [T, H]; returns (ids [T, k] int64, weights [T, k] fp32)."""
+    x = hidden.to(gate_weight.dtype)
+    logits = torch.matmul(x, gate_weight.transpose(0, 1))
+    values, ids = torch.topk(logits, k=top_k, dim=-1)
+    return ids, torch.softmax(values, dim=-1).float()
+
+
+def moe_step(w: dict, residual: torch.Tensor, top_k: int = 8):
+    """One MoE block for T tokens, each as the reference's CPU path runs one
+    token (qwen36_chat_batch.py:127-178): post-attention RMSNorm (1 + w),
+    router, the top_k experts' SwiGLU FFNs weighted by the router weights, the
+    shared expert times sigmoid(shared gate), and the residual add.  Weights
+    are the checkpoint's (bf16) tensors, used in fp32 as the CPU path loads
+    them.  residual [T, H] fp32; returns (out [T, H], ids [T, k], weights
+    [T, k], shared_gate [T])."""
+    moe_in = rmsnorm(residual.float(), w["post_attention_layernorm.weight"])
+    ids, wts = route(moe_in, w["mlp.gate.weight"].float(), top_k)
+    routed = torch.zeros_like(moe_in)
+    for t in range(moe_in.shape[0]):
+        x = moe_in[t]
+        acc = torch.zeros_like(x)
+        outs = []
+        for j in range(top_k):
+            e = int(ids[t, j])
+            gate = w[f"mlp.experts.{e}.gate_proj.weight"].float() @ x
+            up = w[f"mlp.experts.{e}.up_proj.weight"].float() @ x
+            outs.append(w[f"mlp.experts.{e}.down_proj.weight"].float() @ (F.silu(gate) * up))
+        acc = (torch.stack(outs) * wts[t].reshape(-1, 1)).sum(dim=0)
+        routed[t] = acc
+    sg = torch.sigmoid(F.linear(moe_in, w["mlp.shared_expert_gate.weight"].float()))  # [T, 1]
+    sh = F.silu(F.linear(moe_in, w["mlp.shared_expert.gate_proj.weight"].float())) * F.linear(
+        moe_in, w["mlp.shared_expert.up_proj.weight"].float())
+    shared = F.linear(sh, w["mlp.shared_expert.down_proj.weight"].float()) * sg
+    return residual.float() + (routed + shared), ids, wts, sg[:, 0]
 
 
 def rel_rms(a: torch.Tensor, b: torch.Tensor) -> float:

@@ -70,6 +70,39 @@ def gqa_weights(seed: int) -> dict[str, torch.Tensor]:
     }
 
 
+MOE_EXPERTS = 256
+MOE_TOP_K = 8
+MOE_INTERMEDIATE = 512
+SHARED_INTERMEDIATE = 512
+
+
+def moe_weights(seed: int, num_experts: int = MOE_EXPERTS, device="cpu") -> dict[str, torch.Tensor]:
+    """The MoE block of one decoder layer (router, routed experts, shared
+    expert and its gate, post-attention norm) in checkpoint dtypes, keyed by
+    the tensor-name suffixes the reference reads (qwen36_chat_batch.py:127-178):
+    projections N(0, 0.02) bf16, norm weight N(0, 0.1) bf16 (the (1 + w) form)."""
+    g = torch.Generator(device=device)
+    g.manual_seed(int(seed))
+    bf = torch.bfloat16
+
+    def nrm(shape, std):
+        return (torch.randn(*shape, generator=g, device=device) * std).to(bf)
+
+    out = {
+        "post_attention_layernorm.weight": nrm((C.HIDDEN,), 0.1),
+        "mlp.gate.weight": nrm((num_experts, C.HIDDEN), 0.02),
+        "mlp.shared_expert_gate.weight": nrm((1, C.HIDDEN), 0.02),
+        "mlp.shared_expert.gate_proj.weight": nrm((SHARED_INTERMEDIATE, C.HIDDEN), 0.02),
+        "mlp.shared_expert.up_proj.weight": nrm((SHARED_INTERMEDIATE, C.HIDDEN), 0.02),
+        "mlp.shared_expert.down_proj.weight": nrm((C.HIDDEN, SHARED_INTERMEDIATE), 0.02),
+    }
+    for e in range(num_experts):
+        out[f"mlp.experts.{e}.gate_proj.weight"] = nrm((MOE_INTERMEDIATE, C.HIDDEN), 0.02)
+        out[f"mlp.experts.{e}.up_proj.weight"] = nrm((MOE_INTERMEDIATE, C.HIDDEN), 0.02)
+        out[f"mlp.experts.{e}.down_proj.weight"] = nrm((C.HIDDEN, MOE_INTERMEDIATE), 0.02)
+    return out
+
+
 def layer_weights(layer: int, seed: int = 0) -> dict[str, torch.Tensor]:
     """Weights of decoder layer ``layer`` of the 3:1 hybrid stack."""
     s = seed * 1000 + layer

@@ -65,3 +65,25 @@ def test_kernel_boundary_oracle_equals_layer_oracle():
     gated, conv2, rec2 = O.deltanet_kernel_ref(mixed, z, b, a, w, conv0, rec0)
     assert torch.equal(conv1, conv2)
     assert O.rel_rms(rec2, rec1) < 1e-6
+
+
+def test_moe_step_matches_reference():
+    """The MoE block (router, routed experts, shared expert) against
+    router-ia's own batched_moe_step (tests/golden/make_golden_moe.py)."""
+    import json
+    from pathlib import Path
+
+    import numpy as np
+
+    g = np.load(Path(__file__).resolve().parent / "golden" / "reference_moe.npz")
+    meta = json.loads(str(g["meta"]))
+    w = synthetic.moe_weights(meta["weight_seed"], num_experts=meta["num_experts"])
+    xs = synthetic.hidden_stream(meta["tokens"], meta["input_seed"])
+    out, ids, wts, sg = O.moe_step(w, xs.reshape(meta["tokens"], -1).float(), meta["top_k"])
+    assert torch.equal(ids, torch.from_numpy(g["ids"]))
+    assert O.max_abs(wts, torch.from_numpy(g["weights"])) < 1e-6
+    assert O.max_abs(sg, torch.from_numpy(g["shared_gate"])) < 1e-6
+    ref = torch.from_numpy(g["out"])
+    x0 = xs.reshape(meta["tokens"], -1).float()
+    assert O.rel_rms(out - x0, ref - x0) < 1e-5  # the MoE contribution
+    assert O.max_abs(out, ref) < 1e-5
