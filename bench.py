@@ -557,6 +557,70 @@ def gqa_prefill_extra(device, batch=1, seq=8192, iters=5):
                          "frac": r["tflops"] / p["bf16_tflops"], "peak_source": p["source"]}}
 
 
+MOE_EXPERT_BYTES = 3 * 512 * 2048 * 2  # gate, up, down of one expert (or the shared expert), bf16
+
+
+def moe_extra(device, batches=(1, 8, 64), iters=20, warmup=3):
+    """K5, the MoE block of one decode step (256 experts top-8 + shared
+    expert, bf16 weights), at config 4's 64 tokens per GPU and at small
+    batches.  Two layers' weights (3.2 GB) alternate between iterations so
+    that no iteration finds its experts in L2.  HBM-bound: algorithmic bytes
+    = the distinct experts the batch chose + the shared expert + the router
+    rows + activations."""
+    from ria_b200 import synthetic
+    from ria_b200.engine import MoePlan, moe_decode
+    from ria_b200.weights import MoeWeights
+
+    ws = []
+    for seed in (41, 42):
+        t = synthetic.moe_weights(seed, device=device)
+        ws.append(MoeWeights.from_tensors(t, device))
+        del t
+    torch.cuda.empty_cache()
+    p = peaks()
+    out = {"workload": "MoE block of one layer: 256 experts top-8 + 1 shared expert, hidden 2048, "
+                       "intermediate 512, bf16 weights, fp32 activations; two layers' weights alternate; "
+                       "CUDA-graph replay"}
+    g = torch.Generator(device=device)
+    g.manual_seed(5)
+    for batch in batches:
+        x = torch.randn(batch, 2048, device=device, generator=g) * 2.0
+        y = torch.empty_like(x)
+        plans = [MoePlan.create(batch, w.num_experts, device) for w in ws]
+        # the two layers' blocks captured as one graph, as a decode step replays them
+        side = torch.cuda.Stream(device)
+        side.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(side):
+            for i in range(warmup):
+                moe_decode(x, ws[i % 2], plans[i % 2], out=y)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=side):
+                for i in range(2):
+                    moe_decode(x, ws[i], plans[i], out=y)
+        torch.cuda.current_stream(device).wait_stream(side)
+        for _ in range(warmup):
+            graph.replay()
+        torch.cuda.synchronize(device)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(iters // 2):
+            graph.replay()
+        e.record()
+        torch.cuda.synchronize(device)
+        us = s.elapsed_time(e) * 1e3 / (2 * (iters // 2))
+        del graph
+        active = [len(set(pl.expert_ids.flatten().tolist())) for pl in plans]
+        nbytes = (sum(active) / 2 + 1) * MOE_EXPERT_BYTES + 257 * 2048 * 2 + batch * 2048 * 8
+        gbs = nbytes / (us * 1e-6) / 1e9
+        out[f"b{batch}"] = {"us_per_layer": us, "active_experts": sum(active) / 2, "bytes_per_layer": nbytes,
+                            "tokens_per_s_per_layer": batch / (us * 1e-6),
+                            "roofline": {"bound": "hbm", "achieved": gbs, "peak": p["hbm_gbs"], "unit": "GB/s",
+                                         "frac": gbs / p["hbm_gbs"], "peak_source": p["source"]}}
+    del ws
+    torch.cuda.empty_cache()
+    return out
+
+
 # --------------------------------------------------------------------------- CPU reference (oracle port)
 def cpu_reference(args, steps, warmup, sample):
     """router-ia's layer algorithm on the host cores, one sequence at a time
@@ -657,6 +721,7 @@ def main():
             line["gqa_prefill_1x8192"] = gqa_prefill_extra(device)
             line["decode_b1_stack_l4096"] = decode_b1_stack(device)
             line["config0_deltanet_b1"] = config0_deltanet(device)
+            line["moe_block"] = moe_extra(device)
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_reference(args, steps=2, warmup=1, sample=args.cpu_sample)
         if rank == 0:

@@ -268,6 +268,39 @@ RIA_API int ria_gemv_residual(const void* a, int64_t a_stride, const void* w, in
 RIA_API int ria_residual_add(const float* x0, int64_t x0_stride, const void* proj, int64_t proj_stride, float* out,
                      int64_t out_stride, int32_t rows, int32_t n, ria_stream_t stream);
 
+/* ------------------------------------------------------------------------
+ * MoE block of a decode step (hidden 2048, expert and shared-expert
+ * intermediate 512), for a batch of tokens: batched_moe_step
+ * (qwen36_chat_batch.py:127-178) with route (qwen36_router.py:96-133):
+ *
+ *   moe_in = rmsnorm(residual) * (1 + post_norm_weight)       (eps 1e-6)
+ *   logits = moe_in . router_weight^T  (fp32); top_k largest; softmax over them
+ *   out    = residual + sum_j w_j * down_j(silu(gate_j moe_in) * up_j moe_in)
+ *                     + sigmoid(moe_in . shared_gate_weight)
+ *                       * shared_down(silu(shared_gate_proj moe_in) * shared_up_proj moe_in)
+ *
+ * residual / out [batch, 2048] f32 (row strides in elements, multiples of 4;
+ * out may alias residual); weights bf16 as in the checkpoint:
+ * post_norm_weight [2048], router_weight [E, 2048], shared_gate_weight
+ * [2048], experts_gate / experts_up [E, 512, 2048] and experts_down
+ * [E, 2048, 512] (each expert's tensors stacked), shared_gate_proj /
+ * shared_up_proj [512, 2048], shared_down_proj [2048, 512].  Also written:
+ * expert_ids [batch, top_k] int32 and expert_weights [batch, top_k] f32 (the
+ * routing, largest logit first; equal logits pick the lower expert id) and
+ * shared_gate [batch] f32.  batch * top_k <= 2048, E <= 1024, top_k <= 16;
+ * workspace (16-byte aligned, device) of ria_moe_workspace_bytes bytes,
+ * zero-filled before its first use (it holds hand-off counters that every
+ * call returns to zero; one workspace serves one stream at a time).
+ * Experts no token chose are not read.  Deterministic: fixed-order sums. */
+RIA_API int64_t ria_moe_workspace_bytes(int32_t batch, int32_t num_experts, int32_t top_k);
+RIA_API int ria_moe_decode(const float* residual, int64_t residual_stride, const void* post_norm_weight,
+                           const void* router_weight, const void* shared_gate_weight, const void* experts_gate,
+                           const void* experts_up, const void* experts_down, const void* shared_gate_proj,
+                           const void* shared_up_proj, const void* shared_down_proj, float* out, int64_t out_stride,
+                           int32_t* expert_ids, float* expert_weights, float* shared_gate, void* workspace,
+                           int64_t workspace_bytes, int32_t batch, int32_t num_experts, int32_t top_k,
+                           ria_stream_t stream);
+
 /* One-token causal depthwise conv (kernel 4) + SiLU for B rows of `channels`
  * channels, in bf16 like the reference's conv weight dtype:
  * _causal_conv1d_step (qwen36_attention_cache.py:176-221).

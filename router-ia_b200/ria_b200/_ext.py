@@ -71,6 +71,12 @@ _SIGNATURES: dict[str, tuple[object, list]] = {
     "ria_gemv_residual": (
         c_int, [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_int32, c_int32, c_int32,
                 c_void_p]),
+    "ria_moe_workspace_bytes": (c_int64, [c_int32, c_int32, c_int32]),
+    "ria_moe_decode": (
+        c_int,
+        [c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+         c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int32, c_int32, c_int32, c_void_p],
+    ),
     "ria_gdn_chunk_prefill_workspace_bytes": (c_int64, [c_int32, c_int32, c_int32]),
     "ria_gdn_chunk_prefill": (
         c_int,
@@ -352,6 +358,28 @@ def gemv_residual(a, w, x0, out):
         rc = lib().ria_gemv_residual(a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), x0.data_ptr(), x0.stride(0),
                                      out.data_ptr(), out.stride(0), a.shape[0], w.shape[0], w.shape[1], _stream(a))
     _check(rc, "ria_gemv_residual")
+
+
+def moe_workspace_bytes(batch: int, num_experts: int, top_k: int) -> int:
+    return int(lib().ria_moe_workspace_bytes(batch, num_experts, top_k))
+
+
+def moe_decode(residual, w, out, expert_ids, expert_weights, shared_gate, workspace, top_k: int):
+    """One MoE block for residual [B, 2048] f32 into out (may alias residual).
+    ``w`` holds the stacked bf16 weights (keys of ``engine.stack_moe_weights``);
+    expert_ids [B, k] int32, expert_weights [B, k] f32, shared_gate [B] f32
+    receive the routing; workspace a uint8 device buffer."""
+    _require_cuda(residual, out, expert_ids, expert_weights, shared_gate, workspace)
+    num_experts = w["router"].shape[0]
+    with _Hooked("moe", kernels=5):
+        rc = lib().ria_moe_decode(
+            residual.data_ptr(), residual.stride(0), w["post_norm"].data_ptr(), w["router"].data_ptr(),
+            w["shared_gate"].data_ptr(), w["experts_gate"].data_ptr(), w["experts_up"].data_ptr(),
+            w["experts_down"].data_ptr(), w["shared_gate_proj"].data_ptr(), w["shared_up_proj"].data_ptr(),
+            w["shared_down_proj"].data_ptr(), out.data_ptr(), out.stride(0), expert_ids.data_ptr(),
+            expert_weights.data_ptr(), shared_gate.data_ptr(), workspace.data_ptr(), workspace.numel(),
+            residual.shape[0], num_experts, top_k, _stream(residual))
+    _check(rc, "ria_moe_decode")
 
 
 def rmsnorm_rows(x, weight, out):

@@ -27,7 +27,7 @@ import torch.nn.functional as F
 
 from . import _ext
 from . import constants as C
-from .weights import DeltaNetWeights, GqaWeights, rope_inv_freq
+from .weights import DeltaNetWeights, GqaWeights, MoeWeights, rope_inv_freq
 
 
 def _cdiv(a: int, b: int) -> int:
@@ -163,6 +163,47 @@ def gqa_prefill(x: torch.Tensor, w: GqaWeights, k_pool: torch.Tensor, v_pool: to
     out = torch.empty(B * T, C.HIDDEN, dtype=torch.float32, device=x.device)
     _ext.residual_add(xf, o, out)
     return out.view(B, T, C.HIDDEN), workspace
+
+
+@dataclass
+class MoePlan:
+    """Buffers of one MoE launch for a fixed batch: the routing it writes
+    (expert ids, router weights, shared gate) and the kernels' workspace
+    (zero-filled once: its hand-off counters start at zero and every call
+    leaves them there).  Allocated once so that a captured decode step
+    reuses them."""
+
+    batch: int
+    top_k: int
+    expert_ids: torch.Tensor  # [B, k] int32
+    expert_weights: torch.Tensor  # [B, k] f32
+    shared_gate: torch.Tensor  # [B] f32
+    workspace: torch.Tensor  # uint8
+
+    @classmethod
+    def create(cls, batch: int, num_experts: int, device, top_k: int = 8) -> "MoePlan":
+        ws = _ext.moe_workspace_bytes(batch, num_experts, top_k)
+        return cls(batch, top_k,
+                   torch.empty(batch, top_k, dtype=torch.int32, device=device),
+                   torch.empty(batch, top_k, dtype=torch.float32, device=device),
+                   torch.empty(batch, dtype=torch.float32, device=device),
+                   torch.zeros(max(ws, 1), dtype=torch.uint8, device=device))
+
+
+def moe_decode(x: torch.Tensor, w: MoeWeights, plan: MoePlan | None = None,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+    """The MoE block after a layer's attention (K5): x [B, 2048] fp32 residual
+    -> x + routed experts + gated shared expert, as batched_moe_step
+    (qwen36_chat_batch.py:127-178) computes it token by token.  ``out`` may
+    be ``x`` (in place).  The routing lands in ``plan``."""
+    if plan is None:
+        plan = MoePlan.create(x.shape[0], w.num_experts, x.device)
+    if plan.batch != x.shape[0]:
+        raise ValueError(f"MoE plan is for batch {plan.batch}, got {x.shape[0]} tokens")
+    if out is None:
+        out = torch.empty_like(x)
+    _ext.moe_decode(x, w, out, plan.expert_ids, plan.expert_weights, plan.shared_gate, plan.workspace, plan.top_k)
+    return out
 
 
 class BlockAllocator:

@@ -89,6 +89,57 @@ class GqaWeights:
         )
 
 
+@dataclass
+class MoeWeights:
+    """The MoE block of one layer (qwen36_chat_batch.py:127-178), bf16 as in
+    the checkpoint, with each expert's three projections stacked so that the
+    kernels index an expert by offset."""
+
+    post_norm: torch.Tensor  # [2048] bf16, the (1+w) RMSNorm weight
+    router: torch.Tensor  # [E, 2048] bf16
+    shared_gate: torch.Tensor  # [2048] bf16
+    experts_gate: torch.Tensor  # [E, 512, 2048] bf16
+    experts_up: torch.Tensor  # [E, 512, 2048] bf16
+    experts_down: torch.Tensor  # [E, 2048, 512] bf16
+    shared_gate_proj: torch.Tensor  # [512, 2048] bf16
+    shared_up_proj: torch.Tensor  # [512, 2048] bf16
+    shared_down_proj: torch.Tensor  # [2048, 512] bf16
+
+    @property
+    def num_experts(self) -> int:
+        return self.router.shape[0]
+
+    def __getitem__(self, key: str) -> torch.Tensor:
+        return getattr(self, key)
+
+    @classmethod
+    def from_tensors(cls, t: dict[str, torch.Tensor], device) -> "MoeWeights":
+        bf = torch.bfloat16
+        num_experts = t["mlp.gate.weight"].shape[0]
+
+        def stack(proj: str) -> torch.Tensor:
+            first = t[f"mlp.experts.0.{proj}.weight"]
+            out = torch.empty((num_experts, *first.shape), dtype=bf, device=device)
+            for e in range(num_experts):
+                out[e].copy_(t[f"mlp.experts.{e}.{proj}.weight"].to(bf))
+            return out
+
+        def dev(name: str) -> torch.Tensor:
+            return t[name].to(bf).contiguous().to(device)
+
+        return cls(
+            post_norm=dev("post_attention_layernorm.weight"),
+            router=dev("mlp.gate.weight"),
+            shared_gate=dev("mlp.shared_expert_gate.weight").reshape(C.HIDDEN),
+            experts_gate=stack("gate_proj"),
+            experts_up=stack("up_proj"),
+            experts_down=stack("down_proj"),
+            shared_gate_proj=dev("mlp.shared_expert.gate_proj.weight"),
+            shared_up_proj=dev("mlp.shared_expert.up_proj.weight"),
+            shared_down_proj=dev("mlp.shared_expert.down_proj.weight"),
+        )
+
+
 def rope_inv_freq(device) -> torch.Tensor:
     """Inverse RoPE frequencies exactly as the reference computes them
     (qwen36_attention_cache.py:140-143): fp32 on the CPU, then moved."""
