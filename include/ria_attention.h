@@ -301,6 +301,34 @@ RIA_API int ria_moe_decode(const float* residual, int64_t residual_stride, const
                            int64_t workspace_bytes, int32_t batch, int32_t num_experts, int32_t top_k,
                            ria_stream_t stream);
 
+/* ------------------------------------------------------------------------
+ * Greedy head of a decode step: the end of run_forward_token
+ * (qwen36_chat_batch.py:194-199) and sample_next with temperature <= 0
+ * (qwen36_mini_chat.py:75-78):
+ *   h = fp16(rmsnorm(x) * (1 + norm_weight))   (fp32 norm, eps 1e-6, then the
+ *                                               fp16 autocast rounding)
+ *   logits = fp16(h . lm_head^T)               (fp32 accumulation)
+ *   next_id = argmax(logits)                   (first index among equal maxima)
+ *
+ * ria_lm_head_greedy: batch <= 8; x [batch, 2048] f32, norm_weight [2048]
+ * f32, lm_head [vocab, 2048] fp16 (row stride w_stride), next_ids [batch]
+ * int32; logits [batch, vocab] fp16 (row stride logits_stride) is written
+ * when not NULL.  workspace: ria_lm_head_workspace_bytes(batch) bytes,
+ * 16-byte aligned, zero-filled before its first use (it holds a hand-off
+ * counter that every call returns to zero; one workspace serves one stream
+ * at a time).
+ * Larger batches: ria_final_norm_f16 (out [rows, n] fp16), a library GEMM
+ * for the fp16 logits, then ria_argmax_f16_rows (one index per row). */
+RIA_API int64_t ria_lm_head_workspace_bytes(int32_t batch);
+RIA_API int ria_lm_head_greedy(const float* x, int64_t x_stride, const float* norm_weight, const void* lm_head,
+                               int64_t w_stride, int32_t vocab, void* logits, int64_t logits_stride,
+                               int32_t* next_ids, void* workspace, int64_t workspace_bytes, int32_t batch,
+                               ria_stream_t stream);
+RIA_API int ria_final_norm_f16(const float* x, int64_t x_stride, const float* weight, void* out, int64_t out_stride,
+                               int32_t rows, int32_t n, ria_stream_t stream);
+RIA_API int ria_argmax_f16_rows(const void* logits, int64_t stride, int32_t vocab, int32_t rows, int32_t* out,
+                                ria_stream_t stream);
+
 /* One-token causal depthwise conv (kernel 4) + SiLU for B rows of `channels`
  * channels, in bf16 like the reference's conv weight dtype:
  * _causal_conv1d_step (qwen36_attention_cache.py:176-221).

@@ -15,6 +15,9 @@ it, as the checker.  It restates, in plain torch CPU code, the arithmetic of:
 * ``route``                v2/src/router_ia/qwen36_router.py:96-133 and the
   MoE block ``batched_moe_step`` qwen36_chat_batch.py:127-178 (CPU path: fp32
   router, experts, shared expert and its sigmoid gate)
+* the greedy head: final ``rmsnorm``, ``F.linear(x, lm_head)`` and
+  ``sample_next`` at temperature <= 0, qwen36_chat_batch.py:194-199 and
+  qwen36_mini_chat.py:75-78 (CPU path fp32; CUDA path fp16 autocast)
 * the gated delta rule, recurrent and chunked (C=64, WY/UT), as in
   transformers 5.5.0 ``models/qwen3_5_moe/modeling_qwen3_5_moe.py``
   ``torch_recurrent_gated_delta_rule`` (:315-354) and
@@ -352,6 +355,22 @@ def moe_step(w: dict, residual: torch.Tensor, top_k: int = 8):
         moe_in, w["mlp.shared_expert.up_proj.weight"].float())
     shared = F.linear(sh, w["mlp.shared_expert.down_proj.weight"].float()) * sg
     return residual.float() + (routed + shared), ids, wts, sg[:, 0]
+
+
+def lm_head_greedy(x: torch.Tensor, final_norm: torch.Tensor, lm_head: torch.Tensor, fp16: bool = True):
+    """The end of run_forward_token (qwen36_chat_batch.py:194-199) and
+    sample_next with temperature <= 0 (qwen36_mini_chat.py:75-78): fp32
+    RMSNorm with the (1 + w) weight, then logits = x . lm_head^T and the
+    argmax (first index among equal maxima).  fp16=True is the CUDA path
+    (fp16 autocast: both operands rounded to fp16, fp32 sums, fp16 logits);
+    fp16=False the CPU path (fp32 throughout).  x [T, H]; returns (logits
+    [T, V] fp32 holding the path's values, ids [T] int64)."""
+    h = rmsnorm(x.float(), final_norm.float())
+    if fp16:
+        logits = (h.half().float() @ lm_head.half().float().T).half().float()
+    else:
+        logits = h @ lm_head.float().T
+    return logits, torch.argmax(logits, dim=-1)
 
 
 def rel_rms(a: torch.Tensor, b: torch.Tensor) -> float:

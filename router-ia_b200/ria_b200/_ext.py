@@ -77,6 +77,12 @@ _SIGNATURES: dict[str, tuple[object, list]] = {
         [c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
          c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int32, c_int32, c_int32, c_void_p],
     ),
+    "ria_lm_head_workspace_bytes": (c_int64, [c_int32]),
+    "ria_lm_head_greedy": (
+        c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int32, c_void_p, c_int64, c_void_p, c_void_p,
+                c_int64, c_int32, c_void_p]),
+    "ria_final_norm_f16": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int32, c_int32, c_void_p]),
+    "ria_argmax_f16_rows": (c_int, [c_void_p, c_int64, c_int32, c_int32, c_void_p, c_void_p]),
     "ria_gdn_chunk_prefill_workspace_bytes": (c_int64, [c_int32, c_int32, c_int32]),
     "ria_gdn_chunk_prefill": (
         c_int,
@@ -366,12 +372,12 @@ def moe_workspace_bytes(batch: int, num_experts: int, top_k: int) -> int:
 
 def moe_decode(residual, w, out, expert_ids, expert_weights, shared_gate, workspace, top_k: int):
     """One MoE block for residual [B, 2048] f32 into out (may alias residual).
-    ``w`` holds the stacked bf16 weights (keys of ``engine.stack_moe_weights``);
+    ``w`` holds the stacked bf16 weights (a ``weights.MoeWeights``);
     expert_ids [B, k] int32, expert_weights [B, k] f32, shared_gate [B] f32
     receive the routing; workspace a uint8 device buffer."""
     _require_cuda(residual, out, expert_ids, expert_weights, shared_gate, workspace)
     num_experts = w["router"].shape[0]
-    with _Hooked("moe", kernels=5):
+    with _Hooked("moe", kernels=3):
         rc = lib().ria_moe_decode(
             residual.data_ptr(), residual.stride(0), w["post_norm"].data_ptr(), w["router"].data_ptr(),
             w["shared_gate"].data_ptr(), w["experts_gate"].data_ptr(), w["experts_up"].data_ptr(),
@@ -380,6 +386,45 @@ def moe_decode(residual, w, out, expert_ids, expert_weights, shared_gate, worksp
             expert_weights.data_ptr(), shared_gate.data_ptr(), workspace.data_ptr(), workspace.numel(),
             residual.shape[0], num_experts, top_k, _stream(residual))
     _check(rc, "ria_moe_decode")
+
+
+LM_HEAD_MAX_BATCH = 8
+
+
+def lm_head_workspace_bytes(batch: int) -> int:
+    return int(lib().ria_lm_head_workspace_bytes(batch))
+
+
+def lm_head_greedy(x, norm_w, lm_head, next_ids, workspace, logits=None):
+    """next_ids [B] int32 = argmax(fp16(rmsnorm(x) * (1 + norm_w)) . lm_head^T)
+    for x [B, 2048] f32, B <= 8; lm_head [V, 2048] fp16; logits [B, V] fp16
+    (optional) receives the fp16 logits; workspace a zero-filled uint8 buffer."""
+    _require_cuda(x, norm_w, lm_head, next_ids, workspace)
+    lp = logits.data_ptr() if logits is not None else None
+    ls = logits.stride(0) if logits is not None else 0
+    with _Hooked("lm_head", kernels=2):
+        rc = lib().ria_lm_head_greedy(x.data_ptr(), x.stride(0), norm_w.data_ptr(), lm_head.data_ptr(),
+                                      lm_head.stride(0), lm_head.shape[0], lp, ls, next_ids.data_ptr(),
+                                      workspace.data_ptr(), workspace.numel(), x.shape[0], _stream(x))
+    _check(rc, "ria_lm_head_greedy")
+
+
+def final_norm_f16(x, weight, out):
+    """out [B, n] fp16 = fp16(rmsnorm(x [B, n] f32) * (1 + weight))."""
+    _require_cuda(x, weight, out)
+    with _Hooked("final_norm"):
+        rc = lib().ria_final_norm_f16(x.data_ptr(), x.stride(0), weight.data_ptr(), out.data_ptr(), out.stride(0),
+                                      x.shape[0], x.shape[1], _stream(x))
+    _check(rc, "ria_final_norm_f16")
+
+
+def argmax_f16_rows(logits, out):
+    """out [B] int32 = first index of each row's largest value; logits [B, V] fp16."""
+    _require_cuda(logits, out)
+    with _Hooked("argmax"):
+        rc = lib().ria_argmax_f16_rows(logits.data_ptr(), logits.stride(0), logits.shape[1], logits.shape[0],
+                                       out.data_ptr(), _stream(logits))
+    _check(rc, "ria_argmax_f16_rows")
 
 
 def rmsnorm_rows(x, weight, out):

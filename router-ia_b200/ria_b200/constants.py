@@ -4,6 +4,7 @@ v2/src/router_ia/qwen36_40layer_loop.py:36-50, qwen36_attention_cache.py:17-24).
 HIDDEN = 2048
 NUM_LAYERS = 40
 EPS = 1e-6
+VOCAB = 151936  # embedding rows and lm_head rows
 
 # Gated DeltaNet ("linear attention") layers
 LINEAR_NUM_K_HEADS = 16

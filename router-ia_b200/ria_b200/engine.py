@@ -347,9 +347,11 @@ class BatchedAttentionState:
         self.positions.copy_(torch.tensor(self.positions_host, dtype=torch.int32))
         return x
 
-    def run_layers(self, x: torch.Tensor, launch: GqaLaunch) -> torch.Tensor:
+    def run_layers(self, x: torch.Tensor, launch: GqaLaunch, after_layer=None) -> torch.Tensor:
         """The layer chain of one decode step, device work only (no host
-        bookkeeping, no synchronisation): what a CUDA graph captures."""
+        bookkeeping, no synchronisation): what a CUDA graph captures.
+        ``after_layer(layer, x) -> x`` runs after each layer's attention (the
+        full model's MoE block)."""
         for layer in sorted(self.layers):
             w = self.layers[layer]
             if isinstance(w, DeltaNetWeights):
@@ -357,6 +359,8 @@ class BatchedAttentionState:
             else:
                 x = gqa_decode(x, w, self.k_pool[layer], self.v_pool[layer], self.block_table, self.inv_freq,
                                launch, self.seq_lens, self.positions)
+            if after_layer is not None:
+                x = after_layer(layer, x)
         return x
 
     def step(self, x: torch.Tensor, launch: GqaLaunch | None = None, advance: bool = True) -> torch.Tensor:

@@ -150,6 +150,22 @@ def layer_weights_on_device(layer: int, device, seed: int = 0) -> dict[str, torc
     return out
 
 
+def head_weights(seed: int, vocab: int = C.VOCAB, device="cpu") -> dict[str, torch.Tensor]:
+    """Embedding, final norm and lm_head in checkpoint dtypes (bf16), keyed
+    by the names the reference looks up (qwen36_mini_chat.py:52-61,
+    qwen36_op_probe.py:46-52): embedding and lm_head N(0, 0.02), final norm
+    weight N(0, 0.1) (the (1 + w) form)."""
+    g = torch.Generator(device=device)
+    g.manual_seed(int(seed))
+    bf = torch.bfloat16
+    return {
+        "model.language_model.embed_tokens.weight": (torch.randn(vocab, C.HIDDEN, generator=g, device=device)
+                                                     * 0.02).to(bf),
+        "model.language_model.norm.weight": (torch.randn(C.HIDDEN, generator=g, device=device) * 0.1).to(bf),
+        "lm_head.weight": (torch.randn(vocab, C.HIDDEN, generator=g, device=device) * 0.02).to(bf),
+    }
+
+
 def hidden_stream(n: int, seed: int, rows: int = 1) -> torch.Tensor:
     """``n`` steps of layer inputs, (n, rows, 2048) fp32 holding bf16 values."""
     g = _gen(seed)

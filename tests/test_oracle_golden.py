@@ -87,3 +87,23 @@ def test_moe_step_matches_reference():
     x0 = xs.reshape(meta["tokens"], -1).float()
     assert O.rel_rms(out - x0, ref - x0) < 1e-5  # the MoE contribution
     assert O.max_abs(out, ref) < 1e-5
+
+
+def test_greedy_head_matches_reference():
+    """Final norm, lm_head and greedy pick against router-ia's own functions
+    (tests/golden/make_golden_head.py)."""
+    import json
+    from pathlib import Path
+
+    import numpy as np
+
+    g = np.load(Path(__file__).resolve().parent / "golden" / "reference_head.npz")
+    meta = json.loads(str(g["meta"]))
+    w = synthetic.head_weights(meta["weight_seed"], vocab=meta["vocab"])
+    xs = synthetic.hidden_stream(meta["tokens"], meta["input_seed"]).reshape(meta["tokens"], -1) * meta["input_scale"]
+    logits, ids = O.lm_head_greedy(xs, w["model.language_model.norm.weight"], w["lm_head.weight"], fp16=False)
+    assert torch.equal(ids, torch.from_numpy(g["ids"]))
+    assert O.rel_rms(logits, torch.from_numpy(g["logits"])) < 1e-6
+    # the CUDA path's fp16 rounding moves logits by at most a few fp16 steps
+    l16, ids16 = O.lm_head_greedy(xs, w["model.language_model.norm.weight"], w["lm_head.weight"], fp16=True)
+    assert O.max_abs(l16, torch.from_numpy(g["logits"])) < 1e-2
