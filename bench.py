@@ -621,6 +621,90 @@ def moe_extra(device, batches=(1, 8, 64), iters=20, warmup=3):
     return out
 
 
+def config4_decode(device, batch=64, prompt=2048, steps=10, warmup=3):
+    """Benchmark configuration 4's decode phase on one GPU: 64 sequences (the
+    per-GPU share of 512 requests on 8 GPUs) of the random-init 40-layer
+    35B-A3B stack, each holding a 2048-token prompt (random KV, DeltaNet and
+    conv states ~ N(0, 0.1)), greedy decode: embedding gather, 40 x
+    (attention layer + 256-expert top-8 MoE with shared expert), final norm,
+    lm_head and argmax, the ids fed back on the device; the step is replayed
+    from one CUDA graph.  All 40 layers have their own weights (~63 GB), far
+    larger than L2.  Algorithmic bytes per step: attention and head weights,
+    DeltaNet state read + write, KV read, and the weights of the experts each
+    layer's batch chose (counted on an eager step)."""
+    from ria_b200 import constants as C, synthetic
+    from ria_b200.model import DecodeModel, HeadWeights, ModelGraph
+    from ria_b200.weights import DeltaNetWeights, GqaWeights
+
+    torch.cuda.empty_cache()
+    attn, moe = {}, {}
+    for layer in range(C.NUM_LAYERS):
+        t = synthetic.layer_weights_on_device(layer, device, seed=4)
+        attn[layer] = (GqaWeights if C.is_full_attention_layer(layer) else DeltaNetWeights).from_tensors(t, device)
+        del t
+        moe[layer] = synthetic.moe_layer_on_device(4000 + layer, device)
+    head = HeadWeights.from_tensors(synthetic.head_weights(4, device=device), device)
+    per_seq = (prompt + warmup + steps + 8 + C.KV_BLOCK - 1) // C.KV_BLOCK + 1
+    model = DecodeModel(attn, moe, head, batch, pool_blocks=batch * per_seq, max_blocks_per_seq=per_seq,
+                        device=device)
+    st = model.state
+    g = torch.Generator(device=device)
+    g.manual_seed(44)
+    for layer in st.rec:
+        st.rec[layer].normal_(0.0, 0.1, generator=g)
+        st.conv[layer].normal_(0.0, 0.1, generator=g)
+    for layer in st.k_pool:
+        st.k_pool[layer].normal_(0.0, 1.0, generator=g)
+        st.v_pool[layer].normal_(0.0, 1.0, generator=g)
+    for i in range(batch):
+        st.set_length(i, prompt)
+    st.sync_tables()
+    model.ids.copy_(torch.randint(0, head.vocab, (batch,), device=device, generator=g, dtype=torch.int32))
+    # one eager step that counts the experts each layer's batch chose
+    active = []
+    plain = model._moe
+
+    def counting(layer, x):
+        y = plain(layer, x)
+        active.append(int(torch.unique(model.plan.expert_ids).numel()))
+        return y
+
+    model._moe = counting
+    model.step()
+    model._moe = plain
+    graph = ModelGraph(model)
+    for _ in range(warmup):
+        graph.step()
+    torch.cuda.synchronize(device)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    lens = sum(st.lengths) / batch
+    s.record()
+    for _ in range(steps):
+        graph.step()
+    e.record()
+    torch.cuda.synchronize(device)
+    ms = s.elapsed_time(e) / steps
+    n_dn = sum(1 for w in attn.values() if isinstance(w, DeltaNetWeights))
+    n_gqa = C.NUM_LAYERS - n_dn
+    weights = sum(w.w_in.numel() * 2 + w.w_out.numel() * 2 for w in attn.values())
+    moe_bytes = sum((a + 1) * MOE_EXPERT_BYTES + 257 * 2048 * 2 for a in active)
+    state = n_dn * batch * 2 * 32 * 128 * 128 * 4
+    kv = n_gqa * batch * (lens + steps / 2) * 2 * 2 * 256 * 2
+    head_bytes = head.lm_head.numel() * 2
+    nbytes = weights + moe_bytes + state + kv + head_bytes
+    p = peaks()
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    del graph, model, attn, moe, head
+    torch.cuda.empty_cache()
+    return {"workload": f"config 4 decode phase: {batch} sequences x {prompt}-token prompts, 40 layers with "
+                        "256-expert top-8 MoE + shared expert, greedy lm_head; CUDA-graph replay",
+            "ms_per_step": ms, "tokens_per_s": batch / (ms * 1e-3),
+            "active_experts_per_layer": sum(active) / len(active), "bytes_per_step": nbytes,
+            "moe_bytes_share": moe_bytes / nbytes,
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": p["hbm_gbs"], "unit": "GB/s",
+                         "frac": gbs / p["hbm_gbs"], "peak_source": p["source"]}}
+
+
 # --------------------------------------------------------------------------- CPU reference (oracle port)
 def cpu_reference(args, steps, warmup, sample):
     """router-ia's layer algorithm on the host cores, one sequence at a time
@@ -722,6 +806,7 @@ def main():
             line["decode_b1_stack_l4096"] = decode_b1_stack(device)
             line["config0_deltanet_b1"] = config0_deltanet(device)
             line["moe_block"] = moe_extra(device)
+            line["config4_decode_b64"] = config4_decode(device)
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_reference(args, steps=2, warmup=1, sample=args.cpu_sample)
         if rank == 0:

@@ -216,15 +216,28 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
 }
 
-// One CTA per row: the first index of the largest fp16 logit.
-__global__ void __launch_bounds__(256) argmax_f16_rows_kernel(const __half* __restrict__ logits, int64_t ls, int vocab,
-                                                              int* __restrict__ out) {
-  __shared__ Best wb[8];
+// One 1024-thread CTA per row: the first index of the largest fp16 logit.
+// 16-byte loads when the row start and length allow (8 logits per load),
+// indices rising per thread so the first maximum is kept.
+__global__ void __launch_bounds__(1024) argmax_f16_rows_kernel(const __half* __restrict__ logits, int64_t ls,
+                                                               int vocab, int* __restrict__ out) {
+  __shared__ Best wb[32];
   const __half* row = logits + blockIdx.x * ls;
   Best bb = {-INFINITY, 0x7fffffff};
-  for (int i = threadIdx.x; i < vocab; i += blockDim.x) {  // indices rise per thread
+  const bool vec = (reinterpret_cast<uintptr_t>(row) & 15) == 0;
+  const int nvec = vec ? vocab / 8 : 0;
+  for (int c = threadIdx.x; c < nvec; c += blockDim.x) {
+    const uint4 u = *reinterpret_cast<const uint4*>(row + c * 8);
+    const __half* h = reinterpret_cast<const __half*>(&u);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float v = __half2float(h[e]);
+      if (v > bb.v || bb.i == 0x7fffffff) bb = {v, c * 8 + e};
+    }
+  }
+  for (int i = nvec * 8 + threadIdx.x; i < vocab; i += blockDim.x) {
     const float v = __half2float(row[i]);
-    if (v > bb.v || bb.i == 0x7fffffff) bb = {v, i};
+    if (better(v, i, bb.v, bb.i) || bb.i == 0x7fffffff) bb = {v, i};
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
@@ -234,11 +247,15 @@ __global__ void __launch_bounds__(256) argmax_f16_rows_kernel(const __half* __re
   }
   if ((threadIdx.x & 31) == 0) wb[threadIdx.x >> 5] = bb;
   __syncthreads();
-  if (threadIdx.x == 0) {
-    Best r = wb[0];
-    for (int w = 1; w < 8; ++w)
-      if (better(wb[w].v, wb[w].i, r.v, r.i)) r = wb[w];
-    out[blockIdx.x] = r.i;
+  if (threadIdx.x < 32) {
+    bb = wb[threadIdx.x];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bb.v, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bb.i, o);
+      if (better(ov, oi, bb.v, bb.i)) bb = {ov, oi};
+    }
+    if (threadIdx.x == 0) out[blockIdx.x] = bb.i;
   }
 }
 
@@ -307,7 +324,7 @@ extern "C" int ria_argmax_f16_rows(const void* logits, int64_t stride, int32_t v
     return ria::fail(RIA_ERR_INVALID, "ria_argmax_f16_rows: bad rows/vocab/stride");
   if (rows == 0) return RIA_OK;
   if (!logits || !out) return ria::fail(RIA_ERR_INVALID, "ria_argmax_f16_rows: null pointer");
-  argmax_f16_rows_kernel<<<rows, 256, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<const __half*>(logits),
-                                                                               stride, vocab, out);
+  argmax_f16_rows_kernel<<<rows, 1024, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<const __half*>(logits),
+                                                                                stride, vocab, out);
   return ria::check_launch("ria_argmax_f16_rows");
 }

@@ -25,16 +25,17 @@
 //     expert some token chose, units of up to 8 of its (token, slot) pairs in
 //     token order, then the shared expert's units of 8 tokens.  Experts
 //     nobody chose get no unit; their weights are never read.
-//   * moe_gate_up_kernel, a CTA per (unit, tpc 16-row tiles): finds its pairs
+//   * moe_gate_up_kernel, persistent, over 16-row tiles: finds a unit's pairs
 //     in the routing table, stages their activations in SMEM as bf16 hi + lo
 //     parts; warps stream gate / up rows through mma.sync m16n8k16 (weight
 //     rows = M, activations = N, fp32 accumulation) with the next stage's
 //     loads in flight, and write h = silu(gate) * up per (token, slot).
-//   * moe_down_kernel, the same over 64-row tiles of the down rows:
-//     y[token][slot] = scale * down . h, scale = the slot's router weight
-//     (the shared gate for the shared slot).  The CTA that finishes the last
-//     of a (token, 64-row tile)'s k + 1 slots writes that piece of the output:
-//     x + (routed slots summed in slot order + shared slot).
+//   * moe_down_kernel, the same over 128-row tiles of the down rows (a warp
+//     per 16 rows, all 512 columns): y[token][slot] = scale * down . h,
+//     scale = the slot's router weight (the shared gate for the shared
+//     slot).  The CTA that finishes the last of a (token, tile)'s k + 1
+//     slots writes that piece of the output: x + (routed slots summed in slot
+//     order + shared slot).
 // "Last CTA" hand-offs use a fence and an atomic counter (no waiting); the
 // last arrival resets the counter, so the workspace counters stay zero
 // between calls.  Every sum runs in a fixed order: results are deterministic
@@ -65,7 +66,8 @@ constexpr int kTokens = 8;        // tokens per unit and per route CTA
 constexpr int kLogitRows = 16;    // router rows per route CTA (2 per warp)
 constexpr int kLogitSmem = kTokens * kH * 4;
 constexpr int kGuTiles = kI / 16;  // 16-row gate/up tiles per unit
-constexpr int kDnTiles = kH / 64;  // 64-row down tiles per unit
+constexpr int kDnRows = 16 * kWarps;  // down rows per tile: 16 per warp
+constexpr int kDnTiles = kH / kDnRows;  // down tiles per unit
 constexpr int kXStride = kH + 32;  // staged activation row (bf16): 64 bytes past a multiple of 128
 constexpr int kHStride = kI + 32;
 constexpr int kMaxGroups = kMaxPairs / kTokens;
@@ -96,7 +98,7 @@ struct MoeParams {
   unsigned* cnt_group;  // [kMaxGroups] route CTAs done per token group
   unsigned* cnt_plan;   // token groups done
   unsigned* cnt_out;    // [B][kDnTiles] slots done per (token, down row tile)
-  int B, E, k, tpc_gu, tpc_dn;
+  int B, E, k;
 };
 
 __device__ __forceinline__ void bf16x8(const uint4& u, float* f) {
@@ -439,170 +441,199 @@ __device__ __forceinline__ void unit_pairs(const MoeParams& p, int e, int start,
   }
 }
 
-// gate/up: a CTA per (unit, group of tpc_gu 16-row tiles).  Warps 0-3 stream
-// the gate rows, warps 4-7 the up rows, each over a quarter of the 2048
-// columns; the quarters are summed in a fixed order and h = silu(gate) * up
-// is written per (token, slot) for the down kernel.
+// The expert kernels run a persistent grid over the flattened list of
+// (unit, tile) pairs: CTA c takes the contiguous range [c T / G, (c + 1) T / G)
+// of the T = units x tiles pairs, so every CTA streams the same number of
+// weight bytes (within one tile) and no partial last wave idles the machine.
+// A range crosses into a new unit a few times; each crossing re-stages the
+// activations.  seg(tt) gives the segment that starts at flattened index tt.
+struct Segment {
+  int unit, ta, tb;  // tiles [ta, tb) of unit
+};
+
+__device__ __forceinline__ Segment segment_at(int64_t tt, int64_t t_end, int tiles) {
+  Segment sg;
+  sg.unit = static_cast<int>(tt / tiles);
+  sg.ta = static_cast<int>(tt % tiles);
+  const int64_t end = sg.ta + (t_end - tt);
+  sg.tb = static_cast<int>(end < tiles ? end : tiles);
+  return sg;
+}
+
+// gate/up: tiles of 16 rows.  Warps 0-3 stream the gate rows, warps 4-7 the
+// up rows, each over a quarter of the 2048 columns; at each tile's end the
+// quarters are summed in a fixed order and h = silu(gate) * up is written per
+// (token, slot) for the down kernel.
 __global__ void __launch_bounds__(kThreads, 2) moe_gate_up_kernel(const MoeParams p) {
   extern __shared__ __align__(16) unsigned char smem[];
   __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem);  // rows 0-7 hi, 8-15 lo
-  float* red = reinterpret_cast<float*>(xs + 2 * kTokens * kXStride);  // [tpc][8 warps][16][8]
-  int* ids_s = reinterpret_cast<int*>(red + p.tpc_gu * kWarps * 16 * kTokens);  // [B * k]
+  float* red = reinterpret_cast<float*>(xs + 2 * kTokens * kXStride);  // [2][8 warps][16][8]
+  int* ids_s = reinterpret_cast<int*>(red + 2 * kWarps * 16 * kTokens);  // [B * k]
   __shared__ int pr_s[kTokens];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
-  const int groups = kGuTiles / p.tpc_gu;
-  const int unit = blockIdx.x / groups;
-  // the unit, the unit count and the routing table in one round trip
-  const int n_units = *p.n_units;
-  const int4 ui = p.units[min(unit, static_cast<int>(gridDim.x / groups) - 1)];
+  const int64_t total = static_cast<int64_t>(*p.n_units) * kGuTiles;
+  const int64_t t_begin = total * blockIdx.x / gridDim.x, t_end = total * (blockIdx.x + 1) / gridDim.x;
   for (int i = tid; i < p.B * p.k; i += kThreads) ids_s[i] = p.ids[i];
-  if (unit >= n_units) return;
-  const int e = ui.x, start = ui.y, ntok = ui.z;
-  const bool shared = e == p.E, packed = ntok <= 4;
-  const int tile0 = (blockIdx.x % groups) * p.tpc_gu;
-  const __nv_bfloat16* wm = warp < 4 ? (shared ? p.sgp : p.eg + static_cast<int64_t>(e) * kI * kH)
-                                     : (shared ? p.sup : p.eu + static_cast<int64_t>(e) * kI * kH);
   const int kq = (warp & 3) * (kH / 4);
-  auto addr = [&](int idx) {  // idx = tile * 4 + stage
-    return wm + static_cast<int64_t>((tile0 + (idx >> 2)) * 16 + g) * kH + kq + (idx & 3) * 128 + 8 * t;
-  };
-  const int nst = p.tpc_gu * 4;
-  // the activations first (L2 hits that would otherwise queue behind the
-  // weight misses), then the first two weight stages
-  __syncthreads();
-  unit_pairs(p, e, start, ntok, ids_s, pr_s);
-  __syncthreads();
-  for (int j = 0; j < ntok; ++j)
-    stage_split(p.xin + static_cast<int64_t>(pr_s[j] / kMaxTopK) * kH, kH, xs + j * kXStride,
-                xs + (kTokens + j) * kXStride);
-  uint4 ra[8], rb[8];
-  load_stage(ra, addr(0), kH);
-  load_stage(rb, addr(1), kH);
-  __syncthreads();
-  auto xcol = [&](int idx) { return kq + (idx & 3) * 128; };
-  auto done = [&](int idx, float (&acc)[4]) {
-    if ((idx & 3) == 3) {
-      store_partial(red + ((idx >> 2) * kWarps + warp) * 16 * kTokens, acc, g, t);
+  for (int64_t tt = t_begin; tt < t_end;) {
+    const Segment sg = segment_at(tt, t_end, kGuTiles);
+    tt += sg.tb - sg.ta;
+    const int4 ui = p.units[sg.unit];
+    const int e = ui.x, start = ui.y, ntok = ui.z;
+    const bool shared = e == p.E, packed = ntok <= 4;
+    const __nv_bfloat16* wm = warp < 4 ? (shared ? p.sgp : p.eg + static_cast<int64_t>(e) * kI * kH)
+                                       : (shared ? p.sup : p.eu + static_cast<int64_t>(e) * kI * kH);
+    auto addr = [&](int idx) {  // idx = (tile - ta) * 4 + stage
+      return wm + static_cast<int64_t>((sg.ta + (idx >> 2)) * 16 + g) * kH + kq + (idx & 3) * 128 + 8 * t;
+    };
+    const int nst = (sg.tb - sg.ta) * 4;
+    // the activations first (L2 hits that would otherwise queue behind the
+    // weight misses), then the first two weight stages
+    __syncthreads();  // the previous segment is done with pr_s, xs and red; ids_s is complete
+    unit_pairs(p, e, start, ntok, ids_s, pr_s);
+    __syncthreads();
+    for (int j = 0; j < ntok; ++j)
+      stage_split(p.xin + static_cast<int64_t>(pr_s[j] / kMaxTopK) * kH, kH, xs + j * kXStride,
+                  xs + (kTokens + j) * kXStride);
+    uint4 ra[8], rb[8];
+    load_stage(ra, addr(0), kH);
+    load_stage(rb, addr(1), kH);
+    __syncthreads();
+    auto xcol = [&](int idx) { return kq + (idx & 3) * 128; };
+    auto done = [&](int idx, float (&acc)[4]) {
+      if ((idx & 3) != 3) return;
+      const int j = idx >> 2;
+      float* rb_tile = red + (j & 1) * kWarps * 16 * kTokens;  // double-buffered by tile parity
+      store_partial(rb_tile + warp * 16 * kTokens, acc, g, t);
       acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
-    }
-  };
-  if (packed)
-    stream_stages<true>(nst, kH, xs + (g < 4 ? g : g + 4) * kXStride + 8 * t, nullptr, addr, xcol, done, ra, rb);
-  else
-    stream_stages<false>(nst, kH, xs + g * kXStride + 8 * t, xs + (kTokens + g) * kXStride + 8 * t, addr, xcol, done,
-                         ra, rb);
-  __syncthreads();
-  for (int i = tid; i < p.tpc_gu * 16 * kTokens; i += kThreads) {
-    const int n = i % kTokens, r = (i / kTokens) % 16, j = i / (16 * kTokens);
-    if (n < ntok) {
-      const float* rj = red + j * kWarps * 16 * kTokens + r * kTokens;
-      constexpr int W = 16 * kTokens;  // one warp's partials
-      const float gs = ((partial(rj, n, packed) + partial(rj + W, n, packed)) + partial(rj + 2 * W, n, packed)) +
-                       partial(rj + 3 * W, n, packed);
-      const float us = ((partial(rj + 4 * W, n, packed) + partial(rj + 5 * W, n, packed)) +
-                        partial(rj + 6 * W, n, packed)) +
-                       partial(rj + 7 * W, n, packed);
-      p.hbuf[pair_row(p, pr_s[n]) * kI + (tile0 + j) * 16 + r] = silu_mul(gs, us);
-    }
+      __syncthreads();
+      if (tid < 16 * kTokens) {
+        const int n = tid % kTokens, r = tid / kTokens;
+        if (n < ntok) {
+          const float* rj = rb_tile + r * kTokens;
+          constexpr int W = 16 * kTokens;  // one warp's partials
+          const float gs = ((partial(rj, n, packed) + partial(rj + W, n, packed)) + partial(rj + 2 * W, n, packed)) +
+                           partial(rj + 3 * W, n, packed);
+          const float us = ((partial(rj + 4 * W, n, packed) + partial(rj + 5 * W, n, packed)) +
+                            partial(rj + 6 * W, n, packed)) +
+                           partial(rj + 7 * W, n, packed);
+          p.hbuf[pair_row(p, pr_s[n]) * kI + (sg.ta + j) * 16 + r] = silu_mul(gs, us);
+        }
+      }
+    };
+    if (packed)
+      stream_stages<true>(nst, kH, xs + (g < 4 ? g : g + 4) * kXStride + 8 * t, nullptr, addr, xcol, done, ra, rb);
+    else
+      stream_stages<false>(nst, kH, xs + g * kXStride + 8 * t, xs + (kTokens + g) * kXStride + 8 * t, addr, xcol,
+                           done, ra, rb);
   }
 }
 
-// down: a CTA per (unit, group of tpc_dn 64-row tiles).  Warp w streams rows
-// 16 (w & 3) .. +16 of the tile over column half w >> 2 of the 512; the halves
-// are summed, scaled by the slot's router weight (or the shared gate) and
-// written per (token, slot).  Each (token, tile) counts its k + 1 slots; the
-// CTA that brings the count to k + 1 writes that token's tile of the output:
-// x + (routed slots in slot order + shared slot).
+// down: tiles of 128 rows; warp w streams rows 16 w .. 16 w + 15 of each tile
+// over all 512 columns (no cross-warp sum) and writes them per (token, slot)
+// scaled by the slot's router weight (or the shared gate).  Each (token,
+// tile) counts its k + 1 slots; the CTA that brings the count to k + 1
+// writes that token's tile of the output: x + (routed slots in slot order +
+// shared slot).
 __global__ void __launch_bounds__(kThreads, 2) moe_down_kernel(const MoeParams p) {
   extern __shared__ __align__(16) unsigned char smem[];
   __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem);  // rows 0-7 hi, 8-15 lo
-  float* red = reinterpret_cast<float*>(xs + 2 * kTokens * kHStride);  // [tpc][8 warps][16][8]
-  int* ids_s = reinterpret_cast<int*>(red + p.tpc_dn * kWarps * 16 * kTokens);  // [B * k]
+  int* ids_s = reinterpret_cast<int*>(xs + 2 * kTokens * kHStride);  // [B * k]
   __shared__ int pr_s[kTokens];
   __shared__ float sc_s[kTokens];
   __shared__ int fin_s[kTokens * kDnTiles];
   __shared__ int n_fin;
+  constexpr int kSt = kI / 128;  // stages per tile
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
-  const int groups = kDnTiles / p.tpc_dn;
-  const int unit = blockIdx.x / groups;
-  const int n_units = *p.n_units;
-  const int4 ui = p.units[min(unit, static_cast<int>(gridDim.x / groups) - 1)];
+  const int64_t total = static_cast<int64_t>(*p.n_units) * kDnTiles;
+  const int64_t t_begin = total * blockIdx.x / gridDim.x, t_end = total * (blockIdx.x + 1) / gridDim.x;
   for (int i = tid; i < p.B * p.k; i += kThreads) ids_s[i] = p.ids[i];
-  if (tid == 0) n_fin = 0;
-  if (unit >= n_units) return;
-  const int e = ui.x, start = ui.y, ntok = ui.z;
-  const bool shared = e == p.E, packed = ntok <= 4;
-  const int tile0 = (blockIdx.x % groups) * p.tpc_dn;
-  const __nv_bfloat16* wd = shared ? p.sdp : p.ed + static_cast<int64_t>(e) * kH * kI;
-  const int rsub = (warp & 3) * 16, kh = (warp >> 2) * (kI / 2);
-  auto addr = [&](int idx) {  // idx = tile * 2 + stage
-    return wd + static_cast<int64_t>((tile0 + (idx >> 1)) * 64 + rsub + g) * kI + kh + (idx & 1) * 128 + 8 * t;
-  };
-  const int nst = p.tpc_dn * 2;
-  __syncthreads();
-  unit_pairs(p, e, start, ntok, ids_s, pr_s);
-  __syncthreads();
-  if (tid < ntok) {
-    const int tok = pr_s[tid] / kMaxTopK, slot = pr_s[tid] % kMaxTopK;
-    sc_s[tid] = slot < p.k ? p.wts[tok * p.k + slot] : p.sgate[tok];
-  }
-  for (int j = 0; j < ntok; ++j)
-    stage_split(p.hbuf + pair_row(p, pr_s[j]) * kI, kI, xs + j * kHStride, xs + (kTokens + j) * kHStride);
-  uint4 ra[8], rb[8];
-  load_stage(ra, addr(0), kI);
-  load_stage(rb, addr(1), kI);
-  __syncthreads();
-  auto xcol = [&](int idx) { return kh + (idx & 1) * 128; };
-  auto done = [&](int idx, float (&acc)[4]) {
-    if (idx & 1) {
-      store_partial(red + ((idx >> 1) * kWarps + warp) * 16 * kTokens, acc, g, t);
-      acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+  for (int64_t tt = t_begin; tt < t_end;) {
+    const Segment sg = segment_at(tt, t_end, kDnTiles);
+    tt += sg.tb - sg.ta;
+    const int4 ui = p.units[sg.unit];
+    const int e = ui.x, start = ui.y, ntok = ui.z;
+    const bool shared = e == p.E, packed = ntok <= 4;
+    const __nv_bfloat16* wd = shared ? p.sdp : p.ed + static_cast<int64_t>(e) * kH * kI;
+    auto row_of = [&](int idx) { return (sg.ta + idx / kSt) * kDnRows + warp * 16; };
+    auto addr = [&](int idx) {  // idx = (tile - ta) * kSt + stage
+      return wd + static_cast<int64_t>(row_of(idx) + g) * kI + (idx % kSt) * 128 + 8 * t;
+    };
+    const int nst = (sg.tb - sg.ta) * kSt;
+    __syncthreads();  // the previous segment is done with pr_s, sc_s, xs and fin_s; ids_s is complete
+    if (tid == 0) n_fin = 0;
+    unit_pairs(p, e, start, ntok, ids_s, pr_s);
+    __syncthreads();
+    if (tid < ntok) {
+      const int tok = pr_s[tid] / kMaxTopK, slot = pr_s[tid] % kMaxTopK;
+      sc_s[tid] = slot < p.k ? p.wts[tok * p.k + slot] : p.sgate[tok];
     }
-  };
-  if (packed)
-    stream_stages<true>(nst, kI, xs + (g < 4 ? g : g + 4) * kHStride + 8 * t, nullptr, addr, xcol, done, ra, rb);
-  else
-    stream_stages<false>(nst, kI, xs + g * kHStride + 8 * t, xs + (kTokens + g) * kHStride + 8 * t, addr, xcol, done,
-                         ra, rb);
-  __syncthreads();
-  for (int i = tid; i < p.tpc_dn * 64 * kTokens; i += kThreads) {
-    const int n = i % kTokens, r = (i / kTokens) % 64, j = i / (64 * kTokens);
-    if (n < ntok) {
-      const float* rj = red + (j * kWarps + (r >> 4)) * 16 * kTokens + (r & 15) * kTokens;
-      const float s = partial(rj, n, packed) + partial(rj + 4 * 16 * kTokens, n, packed);
-      p.ybuf[pair_row(p, pr_s[n]) * kH + (tile0 + j) * 64 + r] = s * sc_s[n];
+    for (int j = 0; j < ntok; ++j)
+      stage_split(p.hbuf + pair_row(p, pr_s[j]) * kI, kI, xs + j * kHStride, xs + (kTokens + j) * kHStride);
+    uint4 ra[8], rb[8];
+    load_stage(ra, addr(0), kI);
+    load_stage(rb, addr(1), kI);
+    __syncthreads();
+    auto xcol = [&](int idx) { return (idx % kSt) * 128; };
+    // a finished tile straight from the accumulators: lane (g, t) holds rows
+    // g, g + 8 of the warp's 16 and columns 2t, 2t + 1 (packed: columns n and
+    // n + 4 are token n's hi and lo parts, held by lanes t and t + 2)
+    auto done = [&](int idx, float (&acc)[4]) {
+      if (idx % kSt != kSt - 1) return;
+      float v[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float other = __shfl_xor_sync(0xffffffffu, acc[j], 2);
+        v[j] = packed ? acc[j] + other : acc[j];
+        acc[j] = 0.f;
+      }
+      if (!packed || t < 2) {
+        const int r0 = row_of(idx) + g;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int n = 2 * t + (j & 1);
+          if (n < ntok) p.ybuf[pair_row(p, pr_s[n]) * kH + r0 + (j >> 1) * 8] = v[j] * sc_s[n];
+        }
+      }
+    };
+    if (packed)
+      stream_stages<true>(nst, kI, xs + (g < 4 ? g : g + 4) * kHStride + 8 * t, nullptr, addr, xcol, done, ra, rb);
+    else
+      stream_stages<false>(nst, kI, xs + g * kHStride + 8 * t, xs + (kTokens + g) * kHStride + 8 * t, addr, xcol,
+                           done, ra, rb);
+    // hand-off: the last of a (token, tile)'s k + 1 slots to finish combines it
+    __threadfence();
+    __syncthreads();
+    const int ntiles = sg.tb - sg.ta;
+    if (tid < ntok * ntiles) {
+      const int n = tid % ntok, tile = sg.ta + tid / ntok;
+      unsigned* c = p.cnt_out + (pr_s[n] / kMaxTopK) * kDnTiles + tile;
+      if (atomicAdd(c, 1u) == static_cast<unsigned>(p.k)) {
+        *c = 0u;
+        fin_s[atomicAdd(&n_fin, 1)] = (pr_s[n] / kMaxTopK) * kDnTiles + tile;
+      }
     }
-  }
-  // hand-off: the last of a (token, tile)'s k + 1 slots to finish combines it
-  __threadfence();
-  __syncthreads();
-  if (tid < ntok * p.tpc_dn) {
-    const int n = tid % ntok, j = tid / ntok;
-    unsigned* c = p.cnt_out + (pr_s[n] / kMaxTopK) * kDnTiles + tile0 + j;
-    if (atomicAdd(c, 1u) == static_cast<unsigned>(p.k)) {
-      *c = 0u;
-      fin_s[atomicAdd(&n_fin, 1)] = (pr_s[n] / kMaxTopK) * kDnTiles + tile0 + j;
+    __syncthreads();
+    if (n_fin > 0) {
+      __threadfence();
+      for (int i = tid; i < n_fin * (kDnRows / 4); i += kThreads) {
+        const int item = fin_s[i / (kDnRows / 4)];
+        const int b = item / kDnTiles, d = (item % kDnTiles) * kDnRows + (i % (kDnRows / 4)) * 4;
+        const float* y = p.ybuf + static_cast<int64_t>(b) * (p.k + 1) * kH + d;
+        float4 routed = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int s = 0; s < p.k; ++s) {
+          const float4 v = __ldcg(reinterpret_cast<const float4*>(y + static_cast<int64_t>(s) * kH));
+          routed.x += v.x;
+          routed.y += v.y;
+          routed.z += v.z;
+          routed.w += v.w;
+        }
+        const float4 sh = __ldcg(reinterpret_cast<const float4*>(y + static_cast<int64_t>(p.k) * kH));
+        const float4 x = *reinterpret_cast<const float4*>(p.residual + static_cast<int64_t>(b) * p.rs + d);
+        *reinterpret_cast<float4*>(p.out + static_cast<int64_t>(b) * p.os + d) = make_float4(
+            x.x + (routed.x + sh.x), x.y + (routed.y + sh.y), x.z + (routed.z + sh.z), x.w + (routed.w + sh.w));
+      }
     }
-  }
-  __syncthreads();
-  if (n_fin == 0) return;
-  __threadfence();
-  for (int i = tid; i < n_fin * 16; i += kThreads) {
-    const int item = fin_s[i / 16];
-    const int b = item / kDnTiles, d = (item % kDnTiles) * 64 + (i % 16) * 4;
-    const float* y = p.ybuf + static_cast<int64_t>(b) * (p.k + 1) * kH + d;
-    float4 routed = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int s = 0; s < p.k; ++s) {
-      const float4 v = __ldcg(reinterpret_cast<const float4*>(y + static_cast<int64_t>(s) * kH));
-      routed.x += v.x;
-      routed.y += v.y;
-      routed.z += v.z;
-      routed.w += v.w;
-    }
-    const float4 sh = __ldcg(reinterpret_cast<const float4*>(y + static_cast<int64_t>(p.k) * kH));
-    const float4 x = *reinterpret_cast<const float4*>(p.residual + static_cast<int64_t>(b) * p.rs + d);
-    *reinterpret_cast<float4*>(p.out + static_cast<int64_t>(b) * p.os + d) = make_float4(
-        x.x + (routed.x + sh.x), x.y + (routed.y + sh.y), x.z + (routed.z + sh.z), x.w + (routed.w + sh.w));
   }
 }
 
@@ -636,22 +667,6 @@ Layout layout(int64_t b, int64_t e, int64_t k) {
   off += round_up(max_units(b, e, k) * 16);
   l.total = off;
   return l;
-}
-
-// Tiles per expert CTA (gate/up: 128 KB of weights per tile, down: 64 KB):
-// longer weight streams per CTA amortise its prologue (routing lookup and
-// activation staging), so the largest count that still gives about five CTAs
-// per SM -- two and a half waves at two resident -- for the units a batch of
-// this size is expected to touch: E (1 - (1 - k/E)^B) distinct experts plus
-// the shared expert's units.  (Measured on B200, 64 tokens: 4 tiles per
-// gate/up CTA 277 us per layer, 2 tiles 301 us; 1 token: 1 tile 31.5 us,
-// 2 tiles 33 us.)
-int tiles_per_cta(int b, int e, int k, int max_tpc, int tiles) {
-  const double active = e * (1.0 - std::pow(1.0 - static_cast<double>(k) / e, b)) + (b + kTokens - 1) / kTokens;
-  const double want = 5.0 * ria::num_sms();
-  for (int tpc = max_tpc; tpc > 1; tpc /= 2)
-    if (active * (tiles / tpc) >= want) return tpc;
-  return 1;
 }
 
 }  // namespace
@@ -692,11 +707,9 @@ extern "C" int ria_moe_decode(const float* residual, int64_t residual_stride, co
       return ria::fail(RIA_ERR_INVALID, "ria_moe_decode: activations, weights and workspace must be 16-byte aligned");
   if (!ria::aligned(post_norm_weight, 4))
     return ria::fail(RIA_ERR_INVALID, "ria_moe_decode: post_norm_weight must be 4-byte aligned");
-  const int tpc_gu = tiles_per_cta(batch, num_experts, top_k, 4, kGuTiles);
-  const int tpc_dn = tiles_per_cta(batch, num_experts, top_k, 8, kDnTiles);
   const int ids_bytes = batch * top_k * 4;
-  const int gu_smem = 2 * kTokens * kXStride * 2 + tpc_gu * kWarps * 16 * kTokens * 4 + ids_bytes;
-  const int dn_smem = 2 * kTokens * kHStride * 2 + tpc_dn * kWarps * 16 * kTokens * 4 + ids_bytes;
+  const int gu_smem = 2 * kTokens * kXStride * 2 + 2 * kWarps * 16 * kTokens * 4 + ids_bytes;
+  const int dn_smem = 2 * kTokens * kHStride * 2 + ids_bytes;
   static bool attr_set = false;
   if (!attr_set) {
     const int max_ids = kMaxPairs * 4;
@@ -706,10 +719,10 @@ extern "C" int ria_moe_decode(const float* residual, int64_t residual_stride, co
                                kLogitSmem);
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(moe_gate_up_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               2 * kTokens * kXStride * 2 + 4 * kWarps * 16 * kTokens * 4 + max_ids);
+                               2 * kTokens * kXStride * 2 + 2 * kWarps * 16 * kTokens * 4 + max_ids);
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(moe_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               2 * kTokens * kHStride * 2 + 8 * kWarps * 16 * kTokens * 4 + max_ids);
+                               2 * kTokens * kHStride * 2 + max_ids);
     if (e != cudaSuccess)
       return ria::fail(RIA_ERR_CUDA, "ria_moe_decode: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     attr_set = true;
@@ -744,8 +757,6 @@ extern "C" int ria_moe_decode(const float* residual, int64_t residual_stride, co
   p.B = batch;
   p.E = num_experts;
   p.k = top_k;
-  p.tpc_gu = tpc_gu;
-  p.tpc_dn = tpc_dn;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const dim3 route_grid((num_experts + 1 + kLogitRows - 1) / kLogitRows, (batch + kTokens - 1) / kTokens);
   if (num_experts <= 256)
@@ -755,9 +766,11 @@ extern "C" int ria_moe_decode(const float* residual, int64_t residual_stride, co
   int rc = ria::check_launch("ria_moe_decode (route and plan)");
   if (rc) return rc;
   const int64_t units = max_units(batch, num_experts, top_k);
-  moe_gate_up_kernel<<<static_cast<unsigned>(units * (kGuTiles / tpc_gu)), kThreads, gu_smem, st>>>(p);
+  // persistent grids: two CTAs per SM, or fewer when there are fewer tiles
+  const int resident = 2 * ria::num_sms();
+  moe_gate_up_kernel<<<static_cast<unsigned>(std::min<int64_t>(resident, units * kGuTiles)), kThreads, gu_smem, st>>>(p);
   rc = ria::check_launch("ria_moe_decode (gate/up)");
   if (rc) return rc;
-  moe_down_kernel<<<static_cast<unsigned>(units * (kDnTiles / tpc_dn)), kThreads, dn_smem, st>>>(p);
+  moe_down_kernel<<<static_cast<unsigned>(std::min<int64_t>(resident, units * kDnTiles)), kThreads, dn_smem, st>>>(p);
   return ria::check_launch("ria_moe_decode (down and combine)");
 }

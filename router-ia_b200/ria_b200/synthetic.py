@@ -150,6 +150,30 @@ def layer_weights_on_device(layer: int, device, seed: int = 0) -> dict[str, torc
     return out
 
 
+def moe_layer_on_device(seed: int, device, num_experts: int = MOE_EXPERTS):
+    """A ``MoeWeights`` with ``moe_weights``' shapes and distributions, drawn
+    stacked directly on ``device`` (fast, for benchmarks; values differ from
+    the per-expert CPU stream)."""
+    from .weights import MoeWeights
+
+    g = torch.Generator(device=device)
+    g.manual_seed(int(seed))
+    bf = torch.bfloat16
+
+    def nrm(shape, std):
+        return (torch.randn(*shape, generator=g, device=device) * std).to(bf)
+
+    return MoeWeights(
+        post_norm=nrm((C.HIDDEN,), 0.1), router=nrm((num_experts, C.HIDDEN), 0.02),
+        shared_gate=nrm((C.HIDDEN,), 0.02),
+        experts_gate=nrm((num_experts, MOE_INTERMEDIATE, C.HIDDEN), 0.02),
+        experts_up=nrm((num_experts, MOE_INTERMEDIATE, C.HIDDEN), 0.02),
+        experts_down=nrm((num_experts, C.HIDDEN, MOE_INTERMEDIATE), 0.02),
+        shared_gate_proj=nrm((SHARED_INTERMEDIATE, C.HIDDEN), 0.02),
+        shared_up_proj=nrm((SHARED_INTERMEDIATE, C.HIDDEN), 0.02),
+        shared_down_proj=nrm((C.HIDDEN, SHARED_INTERMEDIATE), 0.02))
+
+
 def head_weights(seed: int, vocab: int = C.VOCAB, device="cpu") -> dict[str, torch.Tensor]:
     """Embedding, final norm and lm_head in checkpoint dtypes (bf16), keyed
     by the names the reference looks up (qwen36_mini_chat.py:52-61,
