@@ -633,33 +633,12 @@ def config4_decode(device, batch=64, prompt=2048, steps=10, warmup=3):
     DeltaNet state read + write, KV read, and the weights of the experts each
     layer's batch chose (counted on an eager step)."""
     from ria_b200 import constants as C, synthetic
-    from ria_b200.model import DecodeModel, HeadWeights, ModelGraph
-    from ria_b200.weights import DeltaNetWeights, GqaWeights
+    from ria_b200.model import ModelGraph
+    from ria_b200.weights import DeltaNetWeights
 
     torch.cuda.empty_cache()
-    attn, moe = {}, {}
-    for layer in range(C.NUM_LAYERS):
-        t = synthetic.layer_weights_on_device(layer, device, seed=4)
-        attn[layer] = (GqaWeights if C.is_full_attention_layer(layer) else DeltaNetWeights).from_tensors(t, device)
-        del t
-        moe[layer] = synthetic.moe_layer_on_device(4000 + layer, device)
-    head = HeadWeights.from_tensors(synthetic.head_weights(4, device=device), device)
-    per_seq = (prompt + warmup + steps + 8 + C.KV_BLOCK - 1) // C.KV_BLOCK + 1
-    model = DecodeModel(attn, moe, head, batch, pool_blocks=batch * per_seq, max_blocks_per_seq=per_seq,
-                        device=device)
-    st = model.state
-    g = torch.Generator(device=device)
-    g.manual_seed(44)
-    for layer in st.rec:
-        st.rec[layer].normal_(0.0, 0.1, generator=g)
-        st.conv[layer].normal_(0.0, 0.1, generator=g)
-    for layer in st.k_pool:
-        st.k_pool[layer].normal_(0.0, 1.0, generator=g)
-        st.v_pool[layer].normal_(0.0, 1.0, generator=g)
-    for i in range(batch):
-        st.set_length(i, prompt)
-    st.sync_tables()
-    model.ids.copy_(torch.randint(0, head.vocab, (batch,), device=device, generator=g, dtype=torch.int32))
+    model = synthetic.config4_decode_model(device, batch, prompt, extra_tokens=warmup + steps + 8)
+    st, attn, head = model.state, model.state.layers, model.head
     # one eager step that counts the experts each layer's batch chose
     active = []
     plain = model._moe
@@ -694,7 +673,7 @@ def config4_decode(device, batch=64, prompt=2048, steps=10, warmup=3):
     nbytes = weights + moe_bytes + state + kv + head_bytes
     p = peaks()
     gbs = nbytes / (ms * 1e-3) / 1e9
-    del graph, model, attn, moe, head
+    del graph, model, st, attn, head
     torch.cuda.empty_cache()
     return {"workload": f"config 4 decode phase: {batch} sequences x {prompt}-token prompts, 40 layers with "
                         "256-expert top-8 MoE + shared expert, greedy lm_head; CUDA-graph replay",

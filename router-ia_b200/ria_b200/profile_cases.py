@@ -2,6 +2,9 @@
 
     python router-ia_b200/ria_b200/profile_cases.py --kernel gdn --batch 64 --iters 20
     python router-ia_b200/ria_b200/profile_cases.py --kernel gqa --batch 32 --len 4096 --iters 20
+    python router-ia_b200/ria_b200/profile_cases.py --kernel moe --batch 64 --iters 3
+    python router-ia_b200/ria_b200/profile_cases.py --kernel head --batch 8 --iters 3
+    python router-ia_b200/ria_b200/profile_cases.py --kernel model_step --batch 64
 
 Each case allocates only one layer's state (about 1 GB), so a multi-pass
 ``ncu`` capture of one launch stays small, while one launch still moves more
@@ -131,6 +134,50 @@ def gqa_prefill_case(batch: int, seq: int, iters: int, device) -> dict:
             "tflops": flops / (ms * 1e9)}
 
 
+def moe_case(batch: int, iters: int, device) -> dict:
+    """One layer's MoE block (256 experts top-8 + shared, 1.6 GB of weights)
+    for ``batch`` tokens."""
+    from ria_b200.engine import MoePlan, moe_decode
+
+    w = synthetic.moe_layer_on_device(41, device)
+    g = torch.Generator(device=device)
+    g.manual_seed(5)
+    x = torch.randn(batch, C.HIDDEN, device=device, generator=g) * 2.0
+    plan = MoePlan.create(batch, w.num_experts, device)
+    y = torch.empty_like(x)
+    ms = _time(lambda: moe_decode(x, w, plan, out=y), iters, device)
+    active = len(set(plan.expert_ids.flatten().tolist()))
+    return {"kernel": "moe", "batch": batch, "ms": ms, "active_experts": active}
+
+
+def head_case(batch: int, iters: int, device) -> dict:
+    """The greedy head over the fp16 lm_head (151936 x 2048) for ``batch`` rows."""
+    from ria_b200.model import HeadWeights, greedy_head
+
+    head = HeadWeights.from_tensors(synthetic.head_weights(1, device=device), device)
+    x = torch.randn(batch, C.HIDDEN, device=device)
+    ids = torch.empty(batch, dtype=torch.int32, device=device)
+    ws = (torch.zeros(_ext.lm_head_workspace_bytes(batch), dtype=torch.uint8, device=device)
+          if batch <= _ext.LM_HEAD_MAX_BATCH else None)
+    ms = _time(lambda: greedy_head(x, head, ids, ws), iters, device)
+    return {"kernel": "head", "batch": batch, "ms": ms, "gb_per_s": head.lm_head.numel() * 2 / (ms * 1e6)}
+
+
+def model_step_case(batch: int, device) -> dict:
+    """Configuration 4's decode step (``batch`` sequences with 2048-token
+    prompts, 40 layers with MoE, greedy head): two eager steps, then one in
+    the NVTX range ``decode_step`` (for ``ncu --nvtx --nvtx-include``)."""
+    model = synthetic.config4_decode_model(device, batch, 2048)
+    for _ in range(2):
+        model.step()
+    torch.cuda.synchronize(device)
+    torch.cuda.nvtx.range_push("decode_step")
+    model.step()
+    torch.cuda.synchronize(device)
+    torch.cuda.nvtx.range_pop()
+    return {"kernel": "model_step", "batch": batch, "ids": model.ids[:4].tolist()}
+
+
 def _time(fn, iters, device):
     for _ in range(3):
         fn()
@@ -146,7 +193,8 @@ def _time(fn, iters, device):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--kernel", choices=("gdn", "gqa", "prefill", "gqa_prefill", "all"), default="all")
+    ap.add_argument("--kernel", choices=("gdn", "gqa", "prefill", "gqa_prefill", "moe", "head", "model_step", "all"),
+                    default="all")
     ap.add_argument("--seq", type=int, default=8192)
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--len", type=int, default=4096)
@@ -163,6 +211,12 @@ def main():
         print(gqa_prefill_case(args.batch, args.seq, args.iters, dev), flush=True)
     if args.kernel == "prefill":
         print(prefill_case(args.batch, args.seq, args.iters, dev), flush=True)
+    if args.kernel == "moe":
+        print(moe_case(args.batch, args.iters, dev), flush=True)
+    if args.kernel == "head":
+        print(head_case(args.batch, args.iters, dev), flush=True)
+    if args.kernel == "model_step":
+        print(model_step_case(args.batch, dev), flush=True)
     if _ext.device_error():
         raise SystemExit("device error word set")
 

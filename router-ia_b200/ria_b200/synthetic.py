@@ -222,3 +222,40 @@ def stratified_lengths(batch: int, lo: int, hi: int, seed: int) -> list[int]:
     vals = [min(max(v, lo), hi) for v in vals]
     order = torch.randperm(batch, generator=g).tolist()
     return [vals[i] for i in order]
+
+
+def config4_decode_model(device, batch: int = 64, prompt: int = 2048, extra_tokens: int = 32, seed: int = 4):
+    """Benchmark configuration 4's decode-phase state on one GPU: a
+    ``model.DecodeModel`` of the random-init 40-layer stack (every layer with
+    its own attention and 256-expert MoE weights, ~63 GB), ``batch``
+    sequences each holding a ``prompt``-token cache (KV ~ N(0, 1), DeltaNet
+    and conv states ~ N(0, 0.1)), page room for ``extra_tokens`` more, and
+    random current token ids."""
+    from .model import DecodeModel, HeadWeights
+    from .weights import DeltaNetWeights, GqaWeights
+
+    attn, moe = {}, {}
+    for layer in range(C.NUM_LAYERS):
+        t = layer_weights_on_device(layer, device, seed=seed)
+        attn[layer] = (GqaWeights if C.is_full_attention_layer(layer) else DeltaNetWeights).from_tensors(t, device)
+        del t
+        moe[layer] = moe_layer_on_device(seed * 1000 + layer, device)
+    head = HeadWeights.from_tensors(head_weights(seed, device=device), device)
+    per_seq = (prompt + extra_tokens + C.KV_BLOCK - 1) // C.KV_BLOCK + 1
+    model = DecodeModel(attn, moe, head, batch, pool_blocks=batch * per_seq, max_blocks_per_seq=per_seq,
+                        device=device)
+    st = model.state
+    g = torch.Generator(device=device)
+    g.manual_seed(seed * 11)
+    for layer in st.rec:
+        st.rec[layer].normal_(0.0, 0.1, generator=g)
+        st.conv[layer].normal_(0.0, 0.1, generator=g)
+    for layer in st.k_pool:
+        st.k_pool[layer].normal_(0.0, 1.0, generator=g)
+        st.v_pool[layer].normal_(0.0, 1.0, generator=g)
+    for i in range(batch):
+        st.set_length(i, prompt)
+    st.sync_tables()
+    model.ids.copy_(torch.randint(0, head.vocab, (batch,), device=device, generator=g, dtype=torch.int32))
+    return model
+
