@@ -621,25 +621,40 @@ def moe_extra(device, batches=(1, 8, 64), iters=20, warmup=3):
     return out
 
 
-def config4_decode(device, batch=64, prompt=2048, steps=10, warmup=3):
-    """Benchmark configuration 4's decode phase on one GPU: 64 sequences (the
-    per-GPU share of 512 requests on 8 GPUs) of the random-init 40-layer
-    35B-A3B stack, each holding a 2048-token prompt (random KV, DeltaNet and
-    conv states ~ N(0, 0.1)), greedy decode: embedding gather, 40 x
-    (attention layer + 256-expert top-8 MoE with shared expert), final norm,
-    lm_head and argmax, the ids fed back on the device; the step is replayed
-    from one CUDA graph.  All 40 layers have their own weights (~63 GB), far
-    larger than L2.  Algorithmic bytes per step: attention and head weights,
-    DeltaNet state read + write, KV read, and the weights of the experts each
-    layer's batch chose (counted on an eager step)."""
+def config4_e2e(device, batch=64, prompt=2048, gen=256):
+    """Benchmark configuration 4 on one GPU: its per-GPU share of the 512
+    requests (64 sequences) of the random-init 40-layer 35B-A3B stack, each a
+    2048-token random-id prompt, then 256 greedily generated tokens.  Prefill:
+    the whole prompt in one pass per layer (chunked DeltaNet K2, GQA prefill
+    K4, the prompt MoE as grouped library GEMMs) and the greedy head on the
+    last position.  Decode: embedding, 40 x (attention step + MoE block K5),
+    greedy head K6, the ids fed back on the device, one CUDA graph per step
+    (captured after the first generated step, untimed capture).  All 40
+    layers have their own weights (~63 GB).  Reported: prefill time, decode
+    time per step with its algorithmic bytes (attention and head weights,
+    DeltaNet state read + write, KV read, the weights of the experts each
+    layer's batch chose, counted on the first step) and HBM fraction, and the
+    whole job's generated tokens/s (prefill + every decode step)."""
     from ria_b200 import constants as C, synthetic
     from ria_b200.model import ModelGraph
     from ria_b200.weights import DeltaNetWeights
 
     torch.cuda.empty_cache()
-    model = synthetic.config4_decode_model(device, batch, prompt, extra_tokens=warmup + steps + 8)
+    model = synthetic.config4_decode_model(device, batch, prompt, extra_tokens=gen + 8, empty=True)
     st, attn, head = model.state, model.state.layers, model.head
-    # one eager step that counts the experts each layer's batch chose
+    g = torch.Generator(device=device)
+    g.manual_seed(404)
+    # library set-up on a short prompt, then a fresh state
+    model.prefill(torch.randint(0, head.vocab, (batch, 64), device=device, generator=g, dtype=torch.int32))
+    torch.cuda.synchronize(device)
+    st.reset()
+    ids = torch.randint(0, head.vocab, (batch, prompt), device=device, generator=g, dtype=torch.int32)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    torch.cuda.synchronize(device)
+    ev[0].record()
+    model.prefill(ids)  # -> the first generated token
+    ev[1].record()
+    # the second generated token, eager, counting the experts each layer's batch chose
     active = []
     plain = model._moe
 
@@ -651,37 +666,41 @@ def config4_decode(device, batch=64, prompt=2048, steps=10, warmup=3):
     model._moe = counting
     model.step()
     model._moe = plain
-    graph = ModelGraph(model)
-    for _ in range(warmup):
-        graph.step()
+    ev[2].record()
     torch.cuda.synchronize(device)
+    graph = ModelGraph(model)
+    steps = gen - 2
+    lens0 = sum(st.lengths) / batch
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    lens = sum(st.lengths) / batch
     s.record()
     for _ in range(steps):
         graph.step()
     e.record()
     torch.cuda.synchronize(device)
-    ms = s.elapsed_time(e) / steps
+    prefill_ms = ev[0].elapsed_time(ev[1])
+    eager_ms = ev[1].elapsed_time(ev[2])
+    step_ms = s.elapsed_time(e) / steps
+    total_s = (prefill_ms + eager_ms + steps * step_ms) / 1e3
     n_dn = sum(1 for w in attn.values() if isinstance(w, DeltaNetWeights))
     n_gqa = C.NUM_LAYERS - n_dn
     weights = sum(w.w_in.numel() * 2 + w.w_out.numel() * 2 for w in attn.values())
     moe_bytes = sum((a + 1) * MOE_EXPERT_BYTES + 257 * 2048 * 2 for a in active)
     state = n_dn * batch * 2 * 32 * 128 * 128 * 4
-    kv = n_gqa * batch * (lens + steps / 2) * 2 * 2 * 256 * 2
-    head_bytes = head.lm_head.numel() * 2
-    nbytes = weights + moe_bytes + state + kv + head_bytes
+    kv = n_gqa * batch * (lens0 + steps / 2) * 2 * 2 * 256 * 2
+    nbytes = weights + moe_bytes + state + kv + head.lm_head.numel() * 2
     p = peaks()
-    gbs = nbytes / (ms * 1e-3) / 1e9
+    gbs = nbytes / (step_ms * 1e-3) / 1e9
     del graph, model, st, attn, head
     torch.cuda.empty_cache()
-    return {"workload": f"config 4 decode phase: {batch} sequences x {prompt}-token prompts, 40 layers with "
-                        "256-expert top-8 MoE + shared expert, greedy lm_head; CUDA-graph replay",
-            "ms_per_step": ms, "tokens_per_s": batch / (ms * 1e-3),
-            "active_experts_per_layer": sum(active) / len(active), "bytes_per_step": nbytes,
-            "moe_bytes_share": moe_bytes / nbytes,
-            "roofline": {"bound": "hbm", "achieved": gbs, "peak": p["hbm_gbs"], "unit": "GB/s",
-                         "frac": gbs / p["hbm_gbs"], "peak_source": p["source"]}}
+    return {"workload": f"config 4 on one GPU: {batch} sequences x ({prompt}-token random-id prompt + {gen} greedy "
+                        "tokens), 40 layers with 256-expert top-8 MoE + shared expert",
+            "prefill_ms": prefill_ms, "prefill_tokens_per_s": batch * prompt / (prefill_ms * 1e-3),
+            "decode_ms_per_step": step_ms, "decode_tokens_per_s": batch / (step_ms * 1e-3),
+            "e2e_generated_tokens_per_s": batch * gen / total_s, "e2e_s": total_s,
+            "active_experts_per_layer": sum(active) / len(active), "decode_bytes_per_step": nbytes,
+            "decode_moe_bytes_share": moe_bytes / nbytes,
+            "decode_roofline": {"bound": "hbm", "achieved": gbs, "peak": p["hbm_gbs"], "unit": "GB/s",
+                                "frac": gbs / p["hbm_gbs"], "peak_source": p["source"]}}
 
 
 # --------------------------------------------------------------------------- CPU reference (oracle port)
@@ -785,7 +804,7 @@ def main():
             line["decode_b1_stack_l4096"] = decode_b1_stack(device)
             line["config0_deltanet_b1"] = config0_deltanet(device)
             line["moe_block"] = moe_extra(device)
-            line["config4_decode_b64"] = config4_decode(device)
+            line["config4_e2e_b64"] = config4_e2e(device)
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_reference(args, steps=2, warmup=1, sample=args.cpu_sample)
         if rank == 0:

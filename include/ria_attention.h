@@ -301,6 +301,26 @@ RIA_API int ria_moe_decode(const float* residual, int64_t residual_stride, const
                            int64_t workspace_bytes, int32_t batch, int32_t num_experts, int32_t top_k,
                            ria_stream_t stream);
 
+/* Element kernels of the prompt-prefill MoE path, whose expert projections
+ * run as grouped library GEMMs over the (token, slot) pairs sorted by expert
+ * (batched_moe_step, qwen36_chat_batch.py:127-178, for many tokens at once):
+ * ria_moe_prompt_norm: h [rows, 2048] f32 and h_bf16 = x rsqrt(mean(x^2) +
+ *   1e-6) (1 + post_norm_weight) (bf16 weight), x [rows, 2048] f32.
+ * ria_silu_mul_bf16: out[i] = bf16(silu(gate[i]) * up[i]), n bf16 elements
+ *   (a multiple of 8, 16-byte aligned buffers).
+ * ria_moe_prompt_combine: out[t] = x[t] + (sum_{j < top_k} weights[t, j] *
+ *   expert_out[sorted_position[t, j]] + shared_gate[t] * shared_out[t]), the
+ *   slots summed in order; expert_out [pairs, 2048] and shared_out [rows,
+ *   2048] bf16, weights [rows, top_k] f32, sorted_position [rows, top_k]
+ *   int32 (where pair (t, j) sits in the expert-sorted order). */
+RIA_API int ria_moe_prompt_norm(const float* x, int64_t x_stride, const void* post_norm_weight, float* h, void* h_bf16,
+                                int32_t rows, ria_stream_t stream);
+RIA_API int ria_silu_mul_bf16(const void* gate, const void* up, void* out, int64_t n, ria_stream_t stream);
+RIA_API int ria_moe_prompt_combine(const float* x, int64_t x_stride, const void* expert_out,
+                                   const int32_t* sorted_position, const float* weights, const void* shared_out,
+                                   const float* shared_gate, float* out, int64_t out_stride, int32_t rows,
+                                   int32_t top_k, ria_stream_t stream);
+
 /* ------------------------------------------------------------------------
  * Greedy head of a decode step: the end of run_forward_token
  * (qwen36_chat_batch.py:194-199) and sample_next with temperature <= 0

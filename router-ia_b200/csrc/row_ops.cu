@@ -37,8 +37,8 @@ __global__ void __launch_bounds__(256) rmsnorm_rows_kernel(const float* __restri
 
 __global__ void residual_add_kernel(const float* __restrict__ x0, int64_t xs, const __nv_bfloat16* __restrict__ proj,
                                     int64_t ps, float* __restrict__ out, int64_t os, int n) {
-  const int row = blockIdx.y;
-  const int i = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  const int64_t row = blockIdx.x;  // rows on x: up to 2^31 - 1 of them
+  const int i = (blockIdx.y * blockDim.x + threadIdx.x) * 4;
   if (i >= n) return;
   const float4 a = *reinterpret_cast<const float4*>(x0 + row * xs + i);
   const uint2 raw = *reinterpret_cast<const uint2*>(proj + row * ps + i);
@@ -125,7 +125,7 @@ extern "C" int ria_residual_add(const float* x0, int64_t x0_stride, const void* 
   if (!ria::aligned(x0, 16) || !ria::aligned(out, 16) || !ria::aligned(proj, 8) || x0_stride % 4 || out_stride % 4 ||
       proj_stride % 4)
     return ria::fail(RIA_ERR_INVALID, "ria_residual_add: misaligned rows");
-  dim3 grid((n / 4 + 255) / 256, rows);
+  dim3 grid(rows, (n / 4 + 255) / 256);
   residual_add_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       x0, x0_stride, static_cast<const __nv_bfloat16*>(proj), proj_stride, out, out_stride, n);
   return ria::check_launch("ria_residual_add");

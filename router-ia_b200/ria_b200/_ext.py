@@ -77,6 +77,11 @@ _SIGNATURES: dict[str, tuple[object, list]] = {
         [c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
          c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int32, c_int32, c_int32, c_void_p],
     ),
+    "ria_moe_prompt_norm": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int32, c_void_p]),
+    "ria_silu_mul_bf16": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
+    "ria_moe_prompt_combine": (
+        c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int32,
+                c_int32, c_void_p]),
     "ria_lm_head_workspace_bytes": (c_int64, [c_int32]),
     "ria_lm_head_greedy": (
         c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int32, c_void_p, c_int64, c_void_p, c_void_p,
@@ -386,6 +391,33 @@ def moe_decode(residual, w, out, expert_ids, expert_weights, shared_gate, worksp
             expert_weights.data_ptr(), shared_gate.data_ptr(), workspace.data_ptr(), workspace.numel(),
             residual.shape[0], num_experts, top_k, _stream(residual))
     _check(rc, "ria_moe_decode")
+
+
+def moe_prompt_norm(x, post_norm, h, h_bf16):
+    """h [N, 2048] f32, h_bf16 [N, 2048] bf16 <- rmsnorm(x) * (1 + post_norm)."""
+    _require_cuda(x, post_norm, h, h_bf16)
+    with _Hooked("moe_prompt_norm"):
+        rc = lib().ria_moe_prompt_norm(x.data_ptr(), x.stride(0), post_norm.data_ptr(), h.data_ptr(), h_bf16.data_ptr(),
+                                       x.shape[0], _stream(x))
+    _check(rc, "ria_moe_prompt_norm")
+
+
+def silu_mul_bf16(gate, up, out):
+    """out = bf16(silu(gate) * up), contiguous bf16 tensors of one shape."""
+    _require_cuda(gate, up, out)
+    with _Hooked("silu_mul"):
+        rc = lib().ria_silu_mul_bf16(gate.data_ptr(), up.data_ptr(), out.data_ptr(), out.numel(), _stream(out))
+    _check(rc, "ria_silu_mul_bf16")
+
+
+def moe_prompt_combine(x, expert_out, sorted_position, weights, shared_out, shared_gate, out):
+    """out [N, 2048] f32 = x + sum_j weights[:, j] expert_out[sorted_position[:, j]] + shared_gate shared_out."""
+    _require_cuda(x, expert_out, sorted_position, weights, shared_out, shared_gate, out)
+    with _Hooked("moe_prompt_combine"):
+        rc = lib().ria_moe_prompt_combine(x.data_ptr(), x.stride(0), expert_out.data_ptr(), sorted_position.data_ptr(),
+                                          weights.data_ptr(), shared_out.data_ptr(), shared_gate.data_ptr(),
+                                          out.data_ptr(), out.stride(0), x.shape[0], weights.shape[1], _stream(x))
+    _check(rc, "ria_moe_prompt_combine")
 
 
 LM_HEAD_MAX_BATCH = 8

@@ -206,6 +206,55 @@ def moe_decode(x: torch.Tensor, w: MoeWeights, plan: MoePlan | None = None,
     return out
 
 
+def moe_prefill(x: torch.Tensor, w: MoeWeights, top_k: int = 8, chunk: int = 16384) -> torch.Tensor:
+    """The MoE block for many tokens at once (a prompt prefill): x [N, 2048]
+    fp32 -> x + routed experts + gated shared expert, batched_moe_step's
+    arithmetic (qwen36_chat_batch.py:127-178) for every token.
+
+    With thousands of tokens per expert the block is a grouped GEMM, compute-
+    rather than weight-bound, so this path runs its projections on library
+    GEMMs instead of the decode kernels: the post-attention norm (one kernel,
+    fp32 and bf16 copies), fp32 router logits (fp32 GEMM), top-k and softmax
+    as in the decode path; the (token, slot) pairs sorted by expert (stable),
+    their bf16 activations gathered and the expert projections run as grouped
+    bf16 GEMMs over the sorted pairs (``torch._grouped_mm``, fp32
+    accumulation) with silu(gate) * up in one kernel; the shared expert as
+    plain GEMMs; one kernel then sums each token's k weighted expert rows (in
+    slot order, read from their sorted positions), the gated shared row and
+    the residual.  bf16 activations put the result within about 1e-3
+    relative of the fp32-grade decode kernels.  Tokens go through in chunks
+    of ``chunk`` to bound the temporaries (~1.5 GB at 16384)."""
+    bf = torch.bfloat16
+    n, hidden = x.shape
+    out = torch.empty_like(x)
+    router = w.router.float()
+    sgw = w.shared_gate.float()
+    for s in range(0, n, chunk):
+        xc = x[s:s + chunk]
+        c = xc.shape[0]
+        h = torch.empty(c, hidden, dtype=torch.float32, device=x.device)
+        hb = torch.empty(c, hidden, dtype=bf, device=x.device)
+        _ext.moe_prompt_norm(xc, w.post_norm, h, hb)
+        vals, ids = (h @ router.T).topk(top_k, dim=-1)
+        wts = torch.softmax(vals, dim=-1)
+        sg = torch.sigmoid(h @ sgw)
+        flat = ids.reshape(-1)
+        order = torch.argsort(flat, stable=True)
+        pos = torch.empty_like(order, dtype=torch.int32)
+        pos[order] = torch.arange(order.numel(), dtype=torch.int32, device=x.device)
+        offs = torch.cumsum(torch.bincount(flat, minlength=w.num_experts), 0, dtype=torch.int32)
+        xs = hb.index_select(0, order // top_k)
+        g = torch._grouped_mm(xs, w.experts_gate.transpose(1, 2), offs=offs)
+        u = torch._grouped_mm(xs, w.experts_up.transpose(1, 2), offs=offs)
+        _ext.silu_mul_bf16(g, u, g)
+        y = torch._grouped_mm(g, w.experts_down.transpose(1, 2), offs=offs)
+        sh = F.linear(hb, w.shared_gate_proj)
+        _ext.silu_mul_bf16(sh, F.linear(hb, w.shared_up_proj), sh)
+        shared = F.linear(sh, w.shared_down_proj)
+        _ext.moe_prompt_combine(xc, y, pos.view(c, top_k), wts, shared, sg, out[s:s + chunk])
+    return out
+
+
 class BlockAllocator:
     """Free list of physical KV blocks shared by every GQA layer's pool."""
 
@@ -280,6 +329,20 @@ class BatchedAttentionState:
             self._blocks[seq].extend(new)
             self._table_host[seq, have:need] = torch.tensor(new, dtype=torch.int32)
 
+    def reset(self) -> None:
+        """Every sequence back to an empty context (a fresh request per slot):
+        zero recurrent and conv states, pages returned, lengths and positions 0."""
+        for layer in self.rec:
+            self.rec[layer].zero_()
+            self.conv[layer].zero_()
+        for blocks in self._blocks:
+            self.allocator.free(blocks)
+            blocks.clear()
+        self._table_host.zero_()
+        self.lengths = [0] * self.batch
+        self.positions_host = [0] * self.batch
+        self.sync_tables()
+
     def sync_tables(self) -> None:
         """Upload the block table and lengths (call after reserve/set_length)."""
         self.block_table.copy_(self._table_host)
@@ -319,12 +382,13 @@ class BatchedAttentionState:
         self.reserve_next()
         return self.plan()
 
-    def prefill(self, x: torch.Tensor) -> torch.Tensor:
+    def prefill(self, x: torch.Tensor, after_layer=None) -> torch.Tensor:
         """T prompt tokens for every sequence at once: x [B, T, 2048] fp32 ->
         [B, T, 2048] fp32, every layer's state advanced by T tokens.  Equals T
         calls of ``step`` (router-ia's prompt loop, qwen36_chat_batch.py:
         255-258) with the DeltaNet recurrence in chunked form (K2) and the GQA
-        layers through the causal prefill kernel (K4)."""
+        layers through the causal prefill kernel (K4).  ``after_layer(layer,
+        x) -> x`` runs after each layer's attention (the full model's MoE)."""
         B, T, _ = x.shape
         if B != self.batch:
             raise ValueError(f"prefill expects all {self.batch} sequences, got {B}")
@@ -341,6 +405,8 @@ class BatchedAttentionState:
             else:
                 x, ws = gqa_prefill(x, w, self.k_pool[layer], self.v_pool[layer], self.block_table, self.inv_freq,
                                     self.seq_lens, self.positions, ws)
+            if after_layer is not None:
+                x = after_layer(layer, x)
         self.lengths = [n + T for n in self.lengths]
         self.positions_host = [p + T for p in self.positions_host]
         self.seq_lens.copy_(torch.tensor(self.lengths, dtype=torch.int32))

@@ -21,7 +21,7 @@ import torch.nn.functional as F
 
 from . import _ext
 from . import constants as C
-from .engine import BatchedAttentionState, GqaLaunch, MoePlan, _cdiv, moe_decode
+from .engine import BatchedAttentionState, GqaLaunch, MoePlan, _cdiv, moe_decode, moe_prefill
 from .weights import DeltaNetWeights, GqaWeights, MoeWeights
 
 
@@ -83,9 +83,30 @@ class DecodeModel:
         self.head_ws = (torch.zeros(_ext.lm_head_workspace_bytes(batch), dtype=torch.uint8, device=device)
                         if batch <= _ext.LM_HEAD_MAX_BATCH else None)
         self.ids = torch.zeros(batch, dtype=torch.int32, device=device)
+        self.hidden: torch.Tensor | None = None
 
     def _moe(self, layer: int, x: torch.Tensor) -> torch.Tensor:
         return moe_decode(x, self.moe[layer], self.plan, out=x)
+
+    def _moe_prompt(self, layer: int, x: torch.Tensor) -> torch.Tensor:
+        B, T, H = x.shape
+        return moe_prefill(x.reshape(B * T, H), self.moe[layer]).view(B, T, H)
+
+    def prefill(self, prompt: torch.Tensor) -> torch.Tensor:
+        """A prompt of T tokens for every sequence (``prompt`` [B, T] int32 on
+        the device): embedding rows -> 40 x (attention prefill + MoE over all
+        B T tokens) -> the greedy head on each sequence's last position.  The
+        state advances by T tokens and ``ids`` holds the first generated token
+        of every sequence (router-ia's prompt loop, qwen36_chat_batch.py:
+        255-268, with the whole prompt in one pass)."""
+        B, T = prompt.shape
+        if B != self.batch:
+            raise ValueError(f"prefill expects all {self.batch} sequences, got {B}")
+        x = self.head.embedding.index_select(0, prompt.reshape(-1)).float().view(B, T, C.HIDDEN)
+        x = self.state.prefill(x, after_layer=self._moe_prompt)
+        self.hidden = x[:, -1].contiguous()
+        greedy_head(self.hidden, self.head, self.ids, self.head_ws)
+        return self.ids
 
     def run(self, launch: GqaLaunch) -> None:
         """Device work of one step (what ``ModelGraph`` captures): embedding
@@ -93,6 +114,7 @@ class DecodeModel:
         then every sequence's position advances."""
         x = self.head.embedding.index_select(0, self.ids).float()
         x = self.state.run_layers(x, launch, after_layer=self._moe)
+        self.hidden = x  # the last step's final hidden state (before the head)
         greedy_head(x, self.head, self.ids, self.head_ws)
         _ext.advance_positions(self.state.seq_lens, self.state.positions)
 

@@ -5,6 +5,7 @@
     python router-ia_b200/ria_b200/profile_cases.py --kernel moe --batch 64 --iters 3
     python router-ia_b200/ria_b200/profile_cases.py --kernel head --batch 8 --iters 3
     python router-ia_b200/ria_b200/profile_cases.py --kernel model_step --batch 64
+    python router-ia_b200/ria_b200/profile_cases.py --kernel model_prefill --batch 64 --seq 2048
 
 Each case allocates only one layer's state (about 1 GB), so a multi-pass
 ``ncu`` capture of one launch stays small, while one launch still moves more
@@ -178,6 +179,28 @@ def model_step_case(batch: int, device) -> dict:
     return {"kernel": "model_step", "batch": batch, "ids": model.ids[:4].tolist()}
 
 
+def model_prefill_case(batch: int, seq: int, device) -> dict:
+    """Configuration 4's prompt prefill (``batch`` sequences x ``seq`` tokens
+    through the 40 layers with MoE and the head), the timed pass inside the
+    NVTX range ``prefill`` after a short warm-up prefill and a state reset."""
+    model = synthetic.config4_decode_model(device, batch, seq, extra_tokens=64, empty=True)
+    g = torch.Generator(device=device)
+    g.manual_seed(404)
+    model.prefill(torch.randint(0, model.head.vocab, (batch, 64), device=device, generator=g, dtype=torch.int32))
+    torch.cuda.synchronize(device)
+    model.state.reset()
+    ids = torch.randint(0, model.head.vocab, (batch, seq), device=device, generator=g, dtype=torch.int32)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(device)
+    torch.cuda.nvtx.range_push("prefill")
+    s.record()
+    model.prefill(ids)
+    e.record()
+    torch.cuda.synchronize(device)
+    torch.cuda.nvtx.range_pop()
+    return {"kernel": "model_prefill", "batch": batch, "seq": seq, "ms": s.elapsed_time(e)}
+
+
 def _time(fn, iters, device):
     for _ in range(3):
         fn()
@@ -193,7 +216,8 @@ def _time(fn, iters, device):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--kernel", choices=("gdn", "gqa", "prefill", "gqa_prefill", "moe", "head", "model_step", "all"),
+    ap.add_argument("--kernel", choices=("gdn", "gqa", "prefill", "gqa_prefill", "moe", "head", "model_step",
+                                         "model_prefill", "all"),
                     default="all")
     ap.add_argument("--seq", type=int, default=8192)
     ap.add_argument("--batch", type=int, default=64)
@@ -217,6 +241,8 @@ def main():
         print(head_case(args.batch, args.iters, dev), flush=True)
     if args.kernel == "model_step":
         print(model_step_case(args.batch, dev), flush=True)
+    if args.kernel == "model_prefill":
+        print(model_prefill_case(args.batch, args.seq, dev), flush=True)
     if _ext.device_error():
         raise SystemExit("device error word set")
 

@@ -224,13 +224,16 @@ def stratified_lengths(batch: int, lo: int, hi: int, seed: int) -> list[int]:
     return [vals[i] for i in order]
 
 
-def config4_decode_model(device, batch: int = 64, prompt: int = 2048, extra_tokens: int = 32, seed: int = 4):
+def config4_decode_model(device, batch: int = 64, prompt: int = 2048, extra_tokens: int = 32, seed: int = 4,
+                         empty: bool = False):
     """Benchmark configuration 4's decode-phase state on one GPU: a
     ``model.DecodeModel`` of the random-init 40-layer stack (every layer with
     its own attention and 256-expert MoE weights, ~63 GB), ``batch``
     sequences each holding a ``prompt``-token cache (KV ~ N(0, 1), DeltaNet
     and conv states ~ N(0, 0.1)), page room for ``extra_tokens`` more, and
-    random current token ids."""
+    random current token ids.  ``empty``: the sequences start with no context
+    instead (page room for ``prompt + extra_tokens`` tokens), for a run that
+    prefills the prompt itself."""
     from .model import DecodeModel, HeadWeights
     from .weights import DeltaNetWeights, GqaWeights
 
@@ -247,6 +250,9 @@ def config4_decode_model(device, batch: int = 64, prompt: int = 2048, extra_toke
     st = model.state
     g = torch.Generator(device=device)
     g.manual_seed(seed * 11)
+    if empty:
+        st.sync_tables()
+        return model
     for layer in st.rec:
         st.rec[layer].normal_(0.0, 0.1, generator=g)
         st.conv[layer].normal_(0.0, 0.1, generator=g)
