@@ -16,7 +16,8 @@
 // tensor-core steps.
 //   * gdn_chunk_prep_kernel: one 128-thread CTA per (chunk, value head,
 //     sequence), three CTAs per SM.  TMA loads of the Q/K tiles (3-D tensor
-//     maps, no multicast), gates and norms, G = [Q;K] K^T on the tensor cores,
+//     maps, no multicast), gates, G = [Q;K] [Q;K]^T on the tensor cores (the
+//     q / k norms from its diagonal),
 //     the causal score tile P and A, the 64x64 unit-lower-triangular inverse
 //     (16x16 diagonal blocks by substitution, off-diagonal blocks by tf32
 //     mma.sync), then U^T = V^T TU^T and the token-major W = TW K on the
@@ -131,28 +132,6 @@ __device__ __forceinline__ void load_row_bf16(const unsigned char* tile, int row
   }
 }
 
-__device__ __forceinline__ float sumsq_row(const unsigned char* box0, const unsigned char* box1, int r) {
-  float ss = 0.f;
-#pragma unroll
-  for (int part = 0; part < 2; ++part) {
-    const unsigned char* rowp = (part ? box1 : box0) + r * 128;
-#pragma unroll
-    for (int ch = 0; ch < 8; ++ch) {
-      // visit the row's 16-byte chunks in swizzled order so that the 32 lanes
-      // (32 different rows) spread over all banks
-      const uint4 u = *reinterpret_cast<const uint4*>(rowp + ((ch ^ (r & 7)) << 4));
-      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 f = __bfloat1622float2(h2[e]);
-        ss = fmaf(f.x, f.x, ss);
-        ss = fmaf(f.y, f.y, ss);
-      }
-    }
-  }
-  return ss;
-}
-
 // D (+)= A(16x8 tf32, row) * B(8x8 tf32, col), fp32 accumulate.
 __device__ __forceinline__ void mma_tf32_1688(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                               uint32_t b0, uint32_t b1) {
@@ -166,6 +145,14 @@ __device__ __forceinline__ uint32_t to_tf32(float x) {
   uint32_t r;
   asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
   return r;
+}
+
+// 2^x by the special-function unit (ex2.approx.ftz: relative error about
+// 2^-22, results below 2^-126 flushed to zero).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 // d[2][4] += X[16x16] * Y[16x16] for one warp; X, Y fp32 in SMEM with row
@@ -191,7 +178,8 @@ __device__ __forceinline__ void warp_mma16(float (&d)[2][4], const float* X, int
 
 // T = (I + A)^-1 for strictly-lower A (fp32 [64][kLd]) by 128 threads.  The
 // four 16x16 diagonal blocks are inverted by substitution (threads 0-63, one
-// column each; threads 64-127 meanwhile clear the upper blocks).  Off-diagonal
+// column each).  T's blocks above the diagonal are left unwritten: readers
+// take them as zero.  Off-diagonal
 // blocks follow in order of distance d from the diagonal, one warp per block,
 // on the tensor cores (tf32 in, fp32 accumulate):
 // T_ij = -T_ii (sum_{m=j}^{i-1} A_im T_mj).  Warp w's 16x16 scratch is A's
@@ -232,13 +220,6 @@ __device__ void invert_unit_lower64(float* A, float* T, int tid) {
     }
 #pragma unroll
     for (int ii = 0; ii < 16; ++ii) T[(16 * d + ii) * kLd + j] = col[ii];
-  } else {
-    for (int e = tid - 64; e < 6 * 256; e += 64) {
-      const int blk = e >> 8;
-      const int bi = blk < 3 ? 0 : (blk < 5 ? 1 : 2);
-      const int bj = blk < 3 ? blk + 1 : (blk < 5 ? blk - 1 : 3);
-      T[(16 * bi + ((e >> 4) & 15)) * kLd + 16 * bj + (e & 15)] = 0.f;
-    }
   }
   named_bar_sync(kBarPrep, 128);
   const int g = lane >> 2, tg = lane & 3;
@@ -356,65 +337,82 @@ __global__ void __launch_bounds__(128, 3)
     if (lt == 31) graw[0] = gscan;  // warp 0 total
   }
   mbar_wait_bounded(tma_qk, 0, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
-  // ---- G = [Q;K] K^T (raw q, k) runs while the gates and norms are formed
+  // ---- G = [Q;K] [Q;K]^T (raw q, k; N = 128 costs the M = 128 UMMA no more
+  // time than N = 64): columns 64 + j hold q_i.k_j and k_i.k_j, and the
+  // diagonal gives the squared row norms of q and k.
   if (lt == 0) {
     tc::fence_after_sync();
-    const uint32_t id = tc::idesc_bf16(128, 64, false, false);
+    const uint32_t id = tc::idesc_bf16(128, 128, false, false);
     for (int ks = 0; ks < 8; ++ks) {
-      const uint32_t kb = sbase + (ks < 4 ? kPX : kPY) + (ks & 3) * 32;
-      tc::mma_bf16(tm + kTmG, tc::sdesc_sw128(kb, 16, 1024), tc::sdesc_sw128(kb + kBox, 16, 1024), id, ks > 0);
+      const uint64_t d = tc::sdesc_sw128(sbase + (ks < 4 ? kPX : kPY) + (ks & 3) * 32, 16, 1024);
+      tc::mma_bf16(tm + kTmG, d, d, id, ks > 0);
     }
     tc::commit(mma);
   }
-  named_bar_sync(kBarPrep, 128);
   if (lt < kC) {
+    named_bar_sync(kBarPrep + 1, 64);  // warp 0's total is in graw
     gam[lt] = (lt >= 32 ? gscan + graw[0] : gscan) * kLog2e;
     bet[lt] = bv;
   }
-  {
-    const int r = lt & 63;
-    const uint32_t off = lt >= 64 ? kBox : 0;
-    const float rn = rsqrtf(sumsq_row(smem + kPX + off, smem + kPY + off, r) + 1e-6f);
-    if (lt < 64) sq[r] = rn; else sk[r] = rn;
-  }
-  named_bar_sync(kBarPrep, 128);
   mbar_wait_bounded(mma, 0, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
   tc::fence_after_sync();
+  {  // row lt's squared norm sits in column lt (warp w: columns 32w .. 32w + 31)
+    float v[32];
+    tc::ld32(my_lane + kTmG + 32 * warp, v);
+    tc::wait_ld();
+    // v[lane] by halving selects (static register indices only)
+#pragma unroll
+    for (int w = 16; w >= 1; w >>= 1) {
+      const bool hi = (lt & w) != 0;
+#pragma unroll
+      for (int e = 0; e < w; ++e) v[e] = hi ? v[e + w] : v[e];
+    }
+    const float rn = rsqrtf(v[0] + 1e-6f);
+    if (lt < 64) sq[lt] = rn; else sk[lt - 64] = rn;
+  }
+  named_bar_sync(kBarPrep, 128);
   if (lt < kC) ebk[lt] = bet[lt] * exp2f(gam[lt]) * sk[lt];
 
   // ---- P rows (lanes 0-63) staged over the Q box, A rows (lanes 64-127) to
-  // SMEM, eight columns at a time (a compact loop: three CTAs per SM share
-  // the instruction cache).  Rows 0-31 have no entries in columns 32-63
-  // (causal), so warps 0 and 2 stop at column 32.
+  // SMEM, 32 columns per TMEM load.  Rows 0-31 have no entries in columns
+  // 32-63 (causal), so warps 0 and 2 load one half only (warp 0 zero-fills
+  // its P row's second half; A's upper blocks are never read).
   {
     const bool is_p = lt < 64;
     const int i = lt & 63;
     const float gi = gam[i];
     const float si = is_p ? sq[i] * kQScale : bet[i] * sk[i];
-    const int jend = (lt & 32) ? 64 : 32;
+    const int halves = (lt & 32) ? 2 : 1;
     float* Arow = reinterpret_cast<float*>(smem + kPA) + i * kLd;
 #pragma unroll 1
-    for (int j0 = 0; j0 < 64; j0 += 8) {
-      float v[8];
-      tc::ld8(my_lane + kTmG + j0, v);
+    for (int hf = 0; hf < halves; ++hf) {
+      const int j0 = 32 * hf;
+      float v[32];
+      tc::ld32(my_lane + kTmG + 64 + j0, v);
       tc::wait_ld();
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const int j = j0 + e;
-        const bool keep = j < jend && (is_p ? j <= i : j < i);
-        v[e] = keep ? v[e] * si * sk[j] * exp2f(gi - gam[j]) : 0.f;
+      for (int e4 = 0; e4 < 32; e4 += 4) {
+        const float4 sk4 = *reinterpret_cast<const float4*>(sk + j0 + e4);
+        const float4 gm4 = *reinterpret_cast<const float4*>(gam + j0 + e4);
+        const float skv[4] = {sk4.x, sk4.y, sk4.z, sk4.w}, gmv[4] = {gm4.x, gm4.y, gm4.z, gm4.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int j = j0 + e4 + e;
+          const bool keep = is_p ? j <= i : j < i;
+          v[e4 + e] = keep ? v[e4 + e] * si * skv[e] * ex2_approx(gi - gmv[e]) : 0.f;
+        }
       }
       if (is_p) {
-        uint4 pk;
-        pk.x = pack_bf16x2(v[0], v[1]);
-        pk.y = pack_bf16x2(v[2], v[3]);
-        pk.z = pack_bf16x2(v[4], v[5]);
-        pk.w = pack_bf16x2(v[6], v[7]);
-        *reinterpret_cast<uint4*>(smem + kPX + tc::sw128_off(i, j0)) = pk;
+        store_row_bf16<32>(smem + kPX, i, j0, v);
       } else {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) Arow[j0 + e] = v[e];
+        for (int e = 0; e < 32; ++e) Arow[j0 + e] = v[e];
       }
+    }
+    if (lt < 32) {
+      const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+      for (int c8 = 32; c8 < 64; c8 += 8) *reinterpret_cast<uint4*>(smem + kPX + tc::sw128_off(i, c8)) = z;
     }
   }
   fence_proxy_async_smem();
@@ -433,15 +431,18 @@ __global__ void __launch_bounds__(128, 3)
   }
   invert_unit_lower64(reinterpret_cast<float*>(smem + kPA), reinterpret_cast<float*>(smem + kPT), lt);
   {  // TW = T diag(beta e^gamma s_k) (lanes 0-63), TU = T diag(beta) (lanes 64-127), bf16
+    // (T's row i is zero past its diagonal block: rows 0-31 stop at column 32)
     const int i = lt & 63;
+    const int lim = 16 * ((i >> 4) + 1);
     const float* Trow = reinterpret_cast<const float*>(smem + kPT) + i * kLd;
     const float* cs = lt < 64 ? ebk : bet;
     unsigned char* dst = smem + kPA + (lt < 64 ? 0 : kBox);
+    const int jn = i < 32 ? 32 : 64;
 #pragma unroll 1
-    for (int j0 = 0; j0 < 64; j0 += 8) {
+    for (int j0 = 0; j0 < jn; j0 += 8) {
       float v[8];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) v[e] = Trow[j0 + e] * cs[j0 + e];
+      for (int e = 0; e < 8; ++e) v[e] = j0 + e < lim ? Trow[j0 + e] * cs[j0 + e] : 0.f;
       uint4 pk;
       pk.x = pack_bf16x2(v[0], v[1]);
       pk.y = pack_bf16x2(v[2], v[3]);
@@ -449,6 +450,8 @@ __global__ void __launch_bounds__(128, 3)
       pk.w = pack_bf16x2(v[6], v[7]);
       *reinterpret_cast<uint4*>(dst + tc::sw128_off(i, j0)) = pk;
     }
+    for (int j0 = jn; j0 < 64; j0 += 8)
+      *reinterpret_cast<uint4*>(dst + tc::sw128_off(i, j0)) = make_uint4(0u, 0u, 0u, 0u);
   }
   fence_proxy_async_smem();
   tc::fence_before_sync();
@@ -516,9 +519,9 @@ __global__ void __launch_bounds__(128, 3)
     tma_store_2d(&tmW, smem + kPT, 0, rec_row + kRecUT / 128);
     tma_store_2d(&tmW, smem + kPT + kBox, 0, rec_row + kRecUT / 128 + 64);
     bulk_commit_group();
-    bulk_wait_all0();
+    bulk_wait_read0();  // the stores have read SMEM; their writes complete with the grid
   }
-  if (lt == 64) bulk_wait_all0();  // the P store
+  if (lt == 64) bulk_wait_read0();  // the P store
   if (warp == 0) tc::tmem_dealloc(tm, 128);
 }
 
