@@ -53,7 +53,6 @@ constexpr int kDV = 128;
 constexpr float kQScale = 0.08838834764831845f;  // 128 ** -0.5
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr uint32_t kBox = 8192;  // 64 rows x 128 bytes, 128-byte swizzled
-constexpr int kLd = 65;          // padded fp32 row of A and T (bank-conflict free)
 
 // Workspace record of one (sequence, value head, chunk).
 constexpr uint32_t kRecW = 0;          // W [64 tokens][128 dk] bf16 as two [64][64] boxes (dk 0-63, 64-127)
@@ -65,22 +64,32 @@ constexpr uint32_t kRecBytes = 41600;  // 325 rows of 128 bytes
 constexpr uint32_t kRecRows = kRecBytes / 128;
 
 // ---------------------------------------------------------------- prep SMEM
-// X = [Q dims 0-63 | K dims 0-63], Y = [Q dims 64-127 | K dims 64-127].  Once
-// G and the norms are done the Q boxes are reused: P is staged in the first
-// for its TMA store, then V (dims 0-63, 64-127) is loaded over both.  The A
-// region later holds TW | TU and then the W^T staging tile, the T region the
-// U^T staging tile.
+// X = [Q dims 0-63 | K dims 0-63], Y = [Q dims 64-127 | K dims 64-127]
+// (128-byte-swizzled 64-row boxes).  Once G is done, P is staged in the first
+// Q box for its TMA store, then V (dims 0-63, 64-127) is loaded over the two
+// Q boxes, and once U^T is computed its staging tile goes over V.  A and T
+// are fp32 and keep only their ten lower-triangular 16x16 blocks (padded rows
+// of kBl floats); after the inverse the bf16 operand tiles TW | TU go over A
+// and the front of T, and W is staged over them once its product is done.
+// Four CTAs fit on an SM.
+constexpr int kBl = 17;
+constexpr uint32_t kBlkBytes = 16 * kBl * 4;  // 1088
 constexpr uint32_t kPX = 0, kPY = 2 * kBox;
-constexpr uint32_t kPA = 4 * kBox;    // fp32 A [64][kLd]
-constexpr uint32_t kPT = kPA + 17 * 1024;  // fp32 T [64][kLd] (1024-byte aligned)
-constexpr uint32_t kPMisc = kPT + 64 * kLd * 4;
+constexpr uint32_t kPA = 4 * kBox;              // fp32 A, packed blocks
+constexpr uint32_t kPT = kPA + 10 * kBlkBytes;  // fp32 T, packed blocks
+constexpr uint32_t kPTw = kPA;                  // bf16 TW | TU (two boxes) once T is consumed
+constexpr uint32_t kPMisc = kPT + 10 * kBlkBytes;
 constexpr uint32_t kPGam = kPMisc, kPBet = kPMisc + 256, kPSq = kPMisc + 512, kPSk = kPMisc + 768,
-                   kPGraw = kPMisc + 1024, kPEbk = kPMisc + 1280;
-constexpr uint32_t kPBar = kPMisc + 1536;  // tma_qk, tma_v, mma, tslot
+                   kPEbk = kPMisc + 1024, kPGraw = kPMisc + 1280;
+constexpr uint32_t kPBar = kPMisc + 1296;  // tma_qk, tma_v, mma, tslot
 constexpr uint32_t kPSmem = kPBar + 32;
-static_assert(kPA % 1024 == 0 && kPT % 1024 == 0, "staging tiles need 1024-byte alignment");
-static_assert(64 * kLd * 4 <= kPT - kPA, "A region");
-static_assert(kPSmem * 3 <= 227 * 1024, "three prep CTAs per SM");
+static_assert(kPA % 1024 == 0, "operand tiles need 1024-byte alignment");
+static_assert(2 * kBox <= 20 * kBlkBytes, "TW | TU over A and T");
+static_assert(kPMisc % 16 == 0 && kPBar % 8 == 0, "misc alignment");
+static_assert(4 * (kPSmem + 1024) <= 228 * 1024, "four prep CTAs per SM");
+
+// Packed lower-triangular 16x16 block (bi, bj), bj <= bi.
+__device__ __forceinline__ int tri_blk(int bi, int bj) { return (bi * (bi + 1)) / 2 + bj; }
 
 // ---------------------------------------------------------------- recurrence SMEM
 // [W dk 0-63 | Q dk 0-63 | W dk 64-127 | Q dk 64-127]: per 64-dk half a
@@ -176,14 +185,13 @@ __device__ __forceinline__ void warp_mma16(float (&d)[2][4], const float* X, int
   }
 }
 
-// T = (I + A)^-1 for strictly-lower A (fp32 [64][kLd]) by 128 threads.  The
-// four 16x16 diagonal blocks are inverted by substitution (threads 0-63, one
-// column each).  T's blocks above the diagonal are left unwritten: readers
-// take them as zero.  Off-diagonal
-// blocks follow in order of distance d from the diagonal, one warp per block,
-// on the tensor cores (tf32 in, fp32 accumulate):
-// T_ij = -T_ii (sum_{m=j}^{i-1} A_im T_mj).  Warp w's 16x16 scratch is A's
-// block (0, w + 1), above the diagonal and never read as A.
+// T = (I + A)^-1 for strictly-lower A by 128 threads; A and T are fp32 in
+// packed lower blocks (tri_blk, row stride kBl).  The four 16x16 diagonal
+// blocks are inverted by substitution (threads 0-63, one column each; the
+// blocks' upper parts are written as zeros).  Off-diagonal blocks follow in
+// order of distance from the diagonal, one warp per block, on the tensor
+// cores (tf32 in, fp32 accumulate): T_ij = -T_ii (sum_{m=j}^{i-1} A_im T_mj),
+// the sum parked in T_ij's own block until T_ii multiplies it.
 __device__ void invert_unit_lower64(float* A, float* T, int tid) {
   const int warp = tid >> 5, lane = tid & 31;
   if (tid < 64) {
@@ -191,18 +199,18 @@ __device__ void invert_unit_lower64(float* A, float* T, int tid) {
     // (col[m] = 0 for m < jj, so the sum may run over all m < ii).  The next
     // row of A is loaded while this one is used, and four partial sums keep
     // the FMA chain short.
-    const int d = tid >> 4, jj = tid & 15, j = 16 * d + jj;
-    const float* Ad = A + 16 * d * kLd + 16 * d;
+    const int d = tid >> 4, jj = tid & 15;
+    const float* Ad = A + tri_blk(d, d) * 16 * kBl;
     float col[16];
     float cur[16], nxt[16];
 #pragma unroll
-    for (int m = 0; m < 16; ++m) cur[m] = m < 1 ? Ad[kLd + m] : 0.f;  // row 1
+    for (int m = 0; m < 16; ++m) cur[m] = m < 1 ? Ad[kBl + m] : 0.f;  // row 1
 #pragma unroll
     for (int ii = 0; ii < 16; ++ii) {  // cur holds row ii (ii >= 1); row ii + 1 loads meanwhile
       if (ii >= 1 && ii + 1 < 16) {
 #pragma unroll
         for (int m = 0; m < 16; ++m)
-          if (m <= ii) nxt[m] = Ad[(ii + 1) * kLd + m];
+          if (m <= ii) nxt[m] = Ad[(ii + 1) * kBl + m];
       }
       float acc[4] = {0.f, 0.f, 0.f, 0.f};
       if (ii >= 1) {
@@ -218,38 +226,38 @@ __device__ void invert_unit_lower64(float* A, float* T, int tid) {
           if (m <= ii) cur[m] = nxt[m];
       }
     }
+    float* Td = T + tri_blk(d, d) * 16 * kBl;
 #pragma unroll
-    for (int ii = 0; ii < 16; ++ii) T[(16 * d + ii) * kLd + j] = col[ii];
+    for (int ii = 0; ii < 16; ++ii) Td[ii * kBl + jj] = col[ii];
   }
   named_bar_sync(kBarPrep, 128);
   const int g = lane >> 2, tg = lane & 3;
-  float* zw = A + 16 * (warp + 1);  // warp-private 16x16 (row stride kLd)
 #pragma unroll
   for (int dist = 1; dist < 4; ++dist) {
     if (warp < 4 - dist) {
       const int bi = warp + dist, bj = warp;
       float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
       for (int mb = bj; mb < bi; ++mb)
-        warp_mma16(acc, A + (16 * bi) * kLd + 16 * mb, kLd, T + (16 * mb) * kLd + 16 * bj, kLd, lane);
+        warp_mma16(acc, A + tri_blk(bi, mb) * 16 * kBl, kBl, T + tri_blk(mb, bj) * 16 * kBl, kBl, lane);
+      float* z = T + tri_blk(bi, bj) * 16 * kBl;  // read by nobody before this level ends
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt) {
-        zw[g * kLd + 8 * nt + 2 * tg] = acc[nt][0];
-        zw[g * kLd + 8 * nt + 2 * tg + 1] = acc[nt][1];
-        zw[(g + 8) * kLd + 8 * nt + 2 * tg] = acc[nt][2];
-        zw[(g + 8) * kLd + 8 * nt + 2 * tg + 1] = acc[nt][3];
+        z[g * kBl + 8 * nt + 2 * tg] = acc[nt][0];
+        z[g * kBl + 8 * nt + 2 * tg + 1] = acc[nt][1];
+        z[(g + 8) * kBl + 8 * nt + 2 * tg] = acc[nt][2];
+        z[(g + 8) * kBl + 8 * nt + 2 * tg + 1] = acc[nt][3];
       }
       __syncwarp();
       float tt[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-      warp_mma16(tt, T + (16 * bi) * kLd + 16 * bi, kLd, zw, kLd, lane);
-      float* out = T + (16 * bi) * kLd + 16 * bj;
+      warp_mma16(tt, T + tri_blk(bi, bi) * 16 * kBl, kBl, z, kBl, lane);
+      __syncwarp();  // every lane has read the sum
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt) {
-        out[g * kLd + 8 * nt + 2 * tg] = -tt[nt][0];
-        out[g * kLd + 8 * nt + 2 * tg + 1] = -tt[nt][1];
-        out[(g + 8) * kLd + 8 * nt + 2 * tg] = -tt[nt][2];
-        out[(g + 8) * kLd + 8 * nt + 2 * tg + 1] = -tt[nt][3];
+        z[g * kBl + 8 * nt + 2 * tg] = -tt[nt][0];
+        z[g * kBl + 8 * nt + 2 * tg + 1] = -tt[nt][1];
+        z[(g + 8) * kBl + 8 * nt + 2 * tg] = -tt[nt][2];
+        z[(g + 8) * kBl + 8 * nt + 2 * tg + 1] = -tt[nt][3];
       }
-      __syncwarp();
     }
     named_bar_sync(kBarPrep, 128);
   }
@@ -268,7 +276,7 @@ struct PrepParams {
   unsigned int* err;
 };
 
-__global__ void __launch_bounds__(128, 3)
+__global__ void __launch_bounds__(128, 4)
     gdn_chunk_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                           const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmW,
                           const PrepParams p) {
@@ -373,17 +381,19 @@ __global__ void __launch_bounds__(128, 3)
   named_bar_sync(kBarPrep, 128);
   if (lt < kC) ebk[lt] = bet[lt] * exp2f(gam[lt]) * sk[lt];
 
-  // ---- P rows (lanes 0-63) staged over the Q box, A rows (lanes 64-127) to
-  // SMEM, 32 columns per TMEM load.  Rows 0-31 have no entries in columns
-  // 32-63 (causal), so warps 0 and 2 load one half only (warp 0 zero-fills
-  // its P row's second half; A's upper blocks are never read).
+  // ---- P rows (lanes 0-63) to the record, A rows (lanes 64-127) to SMEM,
+  // 32 columns per TMEM load.  Rows 0-31 have no entries in columns 32-63
+  // (causal), so warps 0 and 2 load one half only (warp 0 stores zeros for
+  // its P row's second half; A keeps lower blocks only).
   {
     const bool is_p = lt < 64;
     const int i = lt & 63;
+    const int bi = i >> 4;
     const float gi = gam[i];
     const float si = is_p ? sq[i] * kQScale : bet[i] * sk[i];
     const int halves = (lt & 32) ? 2 : 1;
-    float* Arow = reinterpret_cast<float*>(smem + kPA) + i * kLd;
+    float* Ab = reinterpret_cast<float*>(smem + kPA);
+
 #pragma unroll 1
     for (int hf = 0; hf < halves; ++hf) {
       const int j0 = 32 * hf;
@@ -406,21 +416,28 @@ __global__ void __launch_bounds__(128, 3)
         store_row_bf16<32>(smem + kPX, i, j0, v);
       } else {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) Arow[j0 + e] = v[e];
+        for (int gq = 0; gq < 2; ++gq) {
+          const int bj = 2 * hf + gq;
+          if (bj <= bi) {
+            float* dst = Ab + tri_blk(bi, bj) * 16 * kBl + (i & 15) * kBl;
+#pragma unroll
+            for (int e = 0; e < 16; ++e) dst[e] = v[16 * gq + e];
+          }
+        }
       }
     }
     if (lt < 32) {
-      const uint4 z = make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
-      for (int c8 = 32; c8 < 64; c8 += 8) *reinterpret_cast<uint4*>(smem + kPX + tc::sw128_off(i, c8)) = z;
+      for (int c8 = 32; c8 < 64; c8 += 8)
+        *reinterpret_cast<uint4*>(smem + kPX + tc::sw128_off(i, c8)) = make_uint4(0u, 0u, 0u, 0u);
     }
   }
   fence_proxy_async_smem();
   tc::fence_before_sync();
-  named_bar_sync(kBarPrep, 128);  // G consumed, A complete, P staged
+  named_bar_sync(kBarPrep, 128);  // G consumed, A complete, P staged over the first Q box
   // P to the record; once the store has read the staging tile, V comes in
-  // over the Q boxes (dims 0-63 over X, 64-127 over Y).  Thread 64 issues it:
-  // threads 0-63 run the diagonal-block substitution meanwhile.
+  // over the Q boxes (dims 0-63, 64-127).  Thread 64 issues both while
+  // threads 0-63 run the diagonal-block substitution.
   if (lt == 64) {
     tma_store_2d(&tmW, smem + kPX, 0, rec_row + kRecP / 128);
     bulk_commit_group();
@@ -430,28 +447,33 @@ __global__ void __launch_bounds__(128, 3)
     tma_load_3d(smem + kPY, &tmV, h * kDV + 64, c * kC, b, tma_v);
   }
   invert_unit_lower64(reinterpret_cast<float*>(smem + kPA), reinterpret_cast<float*>(smem + kPT), lt);
-  {  // TW = T diag(beta e^gamma s_k) (lanes 0-63), TU = T diag(beta) (lanes 64-127), bf16
-    // (T's row i is zero past its diagonal block: rows 0-31 stop at column 32)
+  {  // TW = T diag(beta e^gamma s_k) (lanes 0-63), TU = T diag(beta) (lanes 64-127), bf16;
+     // T's row i is zero past its diagonal block.  All of T is read before
+     // the tiles are written over A and T.
     const int i = lt & 63;
-    const int lim = 16 * ((i >> 4) + 1);
-    const float* Trow = reinterpret_cast<const float*>(smem + kPT) + i * kLd;
+    const int bi = i >> 4;
+    const float* Tb = reinterpret_cast<const float*>(smem + kPT);
     const float* cs = lt < 64 ? ebk : bet;
-    unsigned char* dst = smem + kPA + (lt < 64 ? 0 : kBox);
-    const int jn = i < 32 ? 32 : 64;
-#pragma unroll 1
-    for (int j0 = 0; j0 < jn; j0 += 8) {
-      float v[8];
+    uint32_t pk[32];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) v[e] = j0 + e < lim ? Trow[j0 + e] * cs[j0 + e] : 0.f;
-      uint4 pk;
-      pk.x = pack_bf16x2(v[0], v[1]);
-      pk.y = pack_bf16x2(v[2], v[3]);
-      pk.z = pack_bf16x2(v[4], v[5]);
-      pk.w = pack_bf16x2(v[6], v[7]);
-      *reinterpret_cast<uint4*>(dst + tc::sw128_off(i, j0)) = pk;
+    for (int bj = 0; bj < 4; ++bj) {
+      const float* trow = Tb + tri_blk(bi, bj) * 16 * kBl + (i & 15) * kBl;
+#pragma unroll
+      for (int e = 0; e < 16; e += 2) {
+        float x0 = 0.f, x1 = 0.f;
+        if (bj <= bi) {
+          x0 = trow[e] * cs[16 * bj + e];
+          x1 = trow[e + 1] * cs[16 * bj + e + 1];
+        }
+        pk[8 * bj + e / 2] = pack_bf16x2(x0, x1);
+      }
     }
-    for (int j0 = jn; j0 < 64; j0 += 8)
-      *reinterpret_cast<uint4*>(dst + tc::sw128_off(i, j0)) = make_uint4(0u, 0u, 0u, 0u);
+    named_bar_sync(kBarPrep, 128);
+    unsigned char* dst = smem + kPTw + (lt < 64 ? 0 : kBox);
+#pragma unroll
+    for (int c8 = 0; c8 < 8; ++c8)
+      *reinterpret_cast<uint4*>(dst + tc::sw128_off(i, 8 * c8)) =
+          make_uint4(pk[4 * c8], pk[4 * c8 + 1], pk[4 * c8 + 2], pk[4 * c8 + 3]);
   }
   fence_proxy_async_smem();
   tc::fence_before_sync();
@@ -465,7 +487,7 @@ __global__ void __launch_bounds__(128, 3)
     const uint32_t id = tc::idesc_bf16(128, 64, true, false);
     for (int ks = 0; ks < 4; ++ks)
       tc::mma_bf16(tm + kTmU, tc::sdesc_sw128(sbase + kPX + ks * 2048, kPY - kPX, 1024),
-                   tc::sdesc_sw128(sbase + kPA + kBox + ks * 32, 16, 1024), id, ks > 0);
+                   tc::sdesc_sw128(sbase + kPTw + kBox + ks * 32, 16, 1024), id, ks > 0);
     tc::commit(mma);
   }
   {
@@ -479,49 +501,55 @@ __global__ void __launch_bounds__(128, 3)
   }
   mbar_wait_bounded(mma, 1, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
   tc::fence_after_sync();
-  {  // U^T (row = dv) staged over T (two boxes)
-    float v[64];
-    tc::ld32(my_lane + kTmU, v);
-    tc::ld32(my_lane + kTmU + 32, v + 32);
-    tc::wait_ld();
-    store_row_bf16<64>(smem + kPT, lt, 0, v);
+  {  // U^T row lt (dv) staged over V (consumed): rows 0-63 in the first Q box, 64-127 in the second
+    unsigned char* tile = smem + (lt < 64 ? kPX : kPY);
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      float v[32];
+      tc::ld32(my_lane + kTmU + 32 * hf, v);
+      tc::wait_ld();
+      store_row_bf16<32>(tile, lt & 63, 32 * hf, v);
+    }
   }
+  fence_proxy_async_smem();
   tc::fence_before_sync();
-  named_bar_sync(kBarPrep, 128);  // U^T is read out of TMEM
+  named_bar_sync(kBarPrep, 128);  // U^T is read out of TMEM and staged
+  if (lt == 64) {
+    tma_store_2d(&tmW, smem + kPX, 0, rec_row + kRecUT / 128);
+    tma_store_2d(&tmW, smem + kPY, 0, rec_row + kRecUT / 128 + 64);
+    bulk_commit_group();
+  }
   // ---- W = TW K, token-major: A = [TW; TU] (the TU rows give unused rows
   // 64-127), B = the K tile (MN-major, dk across the two boxes), N = 128 dk
   if (lt == 0) {
     tc::fence_after_sync();
     const uint32_t id = tc::idesc_bf16(128, 128, false, true);
     for (int ks = 0; ks < 4; ++ks)
-      tc::mma_bf16(tm + kTmW, tc::sdesc_sw128(sbase + kPA + ks * 32, 16, 1024),
+      tc::mma_bf16(tm + kTmW, tc::sdesc_sw128(sbase + kPTw + ks * 32, 16, 1024),
                    tc::sdesc_sw128(sbase + kPX + kBox + ks * 2048, kPY - kPX, 1024), id, ks > 0);
     tc::commit(mma);
   }
   mbar_wait_bounded(mma, 0, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
   tc::fence_after_sync();
-  if (lt < 64) {  // W rows (tokens) staged over TW|TU: dk 0-63 and dk 64-127 boxes
-    float v[64];
+  if (lt < 64) {  // W row lt (token) staged over TW | TU (consumed): dk 0-63 and dk 64-127 boxes
 #pragma unroll
-    for (int hb = 0; hb < 2; ++hb) {
-      tc::ld32(my_lane + kTmW + 64 * hb, v);
-      tc::ld32(my_lane + kTmW + 64 * hb + 32, v + 32);
+    for (int q32 = 0; q32 < 4; ++q32) {
+      float v[32];
+      tc::ld32(my_lane + kTmW + 32 * q32, v);
       tc::wait_ld();
-      store_row_bf16<64>(smem + kPA + hb * kBox, lt, 0, v);
+      store_row_bf16<32>(smem + kPTw + (q32 >> 1) * kBox, lt, 32 * (q32 & 1), v);
     }
   }
   fence_proxy_async_smem();
   tc::fence_before_sync();
   __syncthreads();
   if (lt == 0) {
-    tma_store_2d(&tmW, smem + kPA, 0, rec_row + kRecW / 128);
-    tma_store_2d(&tmW, smem + kPA + kBox, 0, rec_row + kRecW / 128 + 64);
-    tma_store_2d(&tmW, smem + kPT, 0, rec_row + kRecUT / 128);
-    tma_store_2d(&tmW, smem + kPT + kBox, 0, rec_row + kRecUT / 128 + 64);
+    tma_store_2d(&tmW, smem + kPTw, 0, rec_row + kRecW / 128);
+    tma_store_2d(&tmW, smem + kPTw + kBox, 0, rec_row + kRecW / 128 + 64);
     bulk_commit_group();
     bulk_wait_read0();  // the stores have read SMEM; their writes complete with the grid
   }
-  if (lt == 64) bulk_wait_read0();  // the P store
+  if (lt == 64) bulk_wait_read0();  // the U^T stores
   if (warp == 0) tc::tmem_dealloc(tm, 128);
 }
 
