@@ -188,10 +188,11 @@ __device__ __forceinline__ void warp_mma16(float (&d)[2][4], const float* X, int
 // T = (I + A)^-1 for strictly-lower A by 128 threads; A and T are fp32 in
 // packed lower blocks (tri_blk, row stride kBl).  The four 16x16 diagonal
 // blocks are inverted by substitution (threads 0-63, one column each; the
-// blocks' upper parts are written as zeros).  Off-diagonal blocks follow in
-// order of distance from the diagonal, one warp per block, on the tensor
-// cores (tf32 in, fp32 accumulate): T_ij = -T_ii (sum_{m=j}^{i-1} A_im T_mj),
-// the sum parked in T_ij's own block until T_ii multiplies it.
+// blocks' upper parts are written as zeros).  The off-diagonal blocks follow
+// by the 2x2 block rule L^-1 = [[L11^-1, 0], [-L22^-1 L21 L11^-1, L22^-1]],
+// first inside each 32x32 diagonal half, then for the lower-left 32x32
+// quarter with all four warps, on the tensor cores (tf32 in, fp32
+// accumulate).
 __device__ void invert_unit_lower64(float* A, float* T, int tid) {
   const int warp = tid >> 5, lane = tid & 31;
   if (tid < 64) {
@@ -232,35 +233,47 @@ __device__ void invert_unit_lower64(float* A, float* T, int tid) {
   }
   named_bar_sync(kBarPrep, 128);
   const int g = lane >> 2, tg = lane & 3;
+  auto blk = [&](float* M, int bi, int bj) { return M + tri_blk(bi, bj) * 16 * kBl; };
+  auto put = [&](float* z, const float (&acc)[2][4], float sgn) {
 #pragma unroll
-  for (int dist = 1; dist < 4; ++dist) {
-    if (warp < 4 - dist) {
-      const int bi = warp + dist, bj = warp;
-      float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-      for (int mb = bj; mb < bi; ++mb)
-        warp_mma16(acc, A + tri_blk(bi, mb) * 16 * kBl, kBl, T + tri_blk(mb, bj) * 16 * kBl, kBl, lane);
-      float* z = T + tri_blk(bi, bj) * 16 * kBl;  // read by nobody before this level ends
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt) {
-        z[g * kBl + 8 * nt + 2 * tg] = acc[nt][0];
-        z[g * kBl + 8 * nt + 2 * tg + 1] = acc[nt][1];
-        z[(g + 8) * kBl + 8 * nt + 2 * tg] = acc[nt][2];
-        z[(g + 8) * kBl + 8 * nt + 2 * tg + 1] = acc[nt][3];
-      }
-      __syncwarp();
-      float tt[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-      warp_mma16(tt, T + tri_blk(bi, bi) * 16 * kBl, kBl, z, kBl, lane);
-      __syncwarp();  // every lane has read the sum
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt) {
-        z[g * kBl + 8 * nt + 2 * tg] = -tt[nt][0];
-        z[g * kBl + 8 * nt + 2 * tg + 1] = -tt[nt][1];
-        z[(g + 8) * kBl + 8 * nt + 2 * tg] = -tt[nt][2];
-        z[(g + 8) * kBl + 8 * nt + 2 * tg + 1] = -tt[nt][3];
-      }
+    for (int nt = 0; nt < 2; ++nt) {
+      z[g * kBl + 8 * nt + 2 * tg] = sgn * acc[nt][0];
+      z[g * kBl + 8 * nt + 2 * tg + 1] = sgn * acc[nt][1];
+      z[(g + 8) * kBl + 8 * nt + 2 * tg] = sgn * acc[nt][2];
+      z[(g + 8) * kBl + 8 * nt + 2 * tg + 1] = sgn * acc[nt][3];
     }
-    named_bar_sync(kBarPrep, 128);
+  };
+  // 32x32 diagonal halves: T10 = -T11 A10 T00 (warp 0), T32 = -T33 A32 T22
+  // (warp 1), the sum parked in the result's own block.
+  if (warp < 2) {
+    const int bi = 2 * warp + 1, bj = 2 * warp;
+    float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    warp_mma16(acc, blk(A, bi, bj), kBl, blk(T, bj, bj), kBl, lane);
+    float* z = blk(T, bi, bj);
+    put(z, acc, 1.f);
+    __syncwarp();
+    float tt[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    warp_mma16(tt, blk(T, bi, bi), kBl, z, kBl, lane);
+    __syncwarp();  // every lane has read the sum
+    put(z, tt, -1.f);
   }
+  named_bar_sync(kBarPrep, 128);
+  // The lower-left 32x32 quarter, T[2:4, 0:2] = -T[2:4, 2:4] (A[2:4, 0:2]
+  // T[0:2, 0:2]), warp w on block (2 + w / 2, w % 2): first Z = A T into the
+  // block, then the product with the lower-right half (read before anyone
+  // overwrites a Z block).
+  const int bi = 2 + (warp >> 1), bj = warp & 1;
+  {
+    float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    for (int m = bj; m < 2; ++m) warp_mma16(acc, blk(A, bi, m), kBl, blk(T, m, bj), kBl, lane);
+    put(blk(T, bi, bj), acc, 1.f);
+  }
+  named_bar_sync(kBarPrep, 128);
+  float tt[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+  for (int m = 2; m <= bi; ++m) warp_mma16(tt, blk(T, bi, m), kBl, blk(T, m, bj), kBl, lane);
+  named_bar_sync(kBarPrep, 128);
+  put(blk(T, bi, bj), tt, -1.f);
+  named_bar_sync(kBarPrep, 128);
 }
 
 struct PrepParams {
