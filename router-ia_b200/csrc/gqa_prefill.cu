@@ -133,36 +133,63 @@ __global__ void __launch_bounds__(256) gqa_prefill_prep_kernel(const PrepParams 
   }
   __syncthreads();
   constexpr int kTasks = kHq + 2 * kHkv;  // per token: q heads, k heads, v heads
-  for (int task = warp; task < kPrepTokens * kTasks; task += 8) {
-    const int tt = task / kTasks, kind = task % kTasks;
-    const int t = tb + tt;
-    if (t >= p.T) break;  // tasks run in token order
-    if (kind < kHq) {
-      const int h = kind;
-      float x[8];
-      load8(p.q + static_cast<int64_t>(b) * p.qs_b + static_cast<int64_t>(t) * p.qs_t + h * 2 * kD + lane * 8, x);
-      norm_rope_8(x, p.q_norm_w, cs_tab[tt], sn_tab[tt], lane);
-      *reinterpret_cast<uint4*>(p.qbuf + ((static_cast<int64_t>(b) * p.T + t) * kHq + h) * kD + lane * 8) =
-          pack8(x, 0.0625f);
-      continue;
+  constexpr int kPerWarp = kPrepTokens * kTasks / 8;
+  constexpr int kInFlight = 4;  // rows a warp loads before it works on them
+  static_assert(kPerWarp % kInFlight == 0, "task batches");
+  for (int i0 = 0; i0 < kPerWarp; i0 += kInFlight) {
+    uint4 raw[kInFlight];
+#pragma unroll
+    for (int u = 0; u < kInFlight; ++u) {  // warp task i: token i / kTasks, row kind i % kTasks
+      const int task = warp + 8 * (i0 + u);
+      const int tt = task / kTasks, kind = task % kTasks;
+      const int t = tb + tt;
+      raw[u] = make_uint4(0u, 0u, 0u, 0u);
+      if (t >= p.T) continue;
+      const __nv_bfloat16* src =
+          kind < kHq ? p.q + static_cast<int64_t>(b) * p.qs_b + static_cast<int64_t>(t) * p.qs_t + kind * 2 * kD
+          : kind < kHq + kHkv
+              ? p.k + static_cast<int64_t>(b) * p.ks_b + static_cast<int64_t>(t) * p.ks_t + (kind - kHq) * kD
+              : p.v + static_cast<int64_t>(b) * p.vs_b + static_cast<int64_t>(t) * p.vs_t + (kind - kHq - kHkv) * kD;
+      raw[u] = *reinterpret_cast<const uint4*>(src + lane * 8);
     }
-    const int cidx = L0 + t;
-    const int lp = cidx / kBlock;
-    const int phys = (lp < p.bt_stride) ? p.block_table[static_cast<int64_t>(b) * p.bt_stride + lp] : -1;
-    if (phys < 0 || phys >= p.num_blocks) {
-      if (lane == 0) ria_set_error(p.err, RIA_DEVERR_BAD_BLOCK);
-      continue;
-    }
-    const int kvh = (kind - kHq) & 1;
-    const int64_t row = static_cast<int64_t>(kvh) * p.pool_tokens + static_cast<int64_t>(phys) * kBlock + (cidx % kBlock);
-    if (kind < kHq + kHkv) {
+#pragma unroll
+    for (int u = 0; u < kInFlight; ++u) {
+      const int task = warp + 8 * (i0 + u);
+      const int tt = task / kTasks, kind = task % kTasks;
+      const int t = tb + tt;
+      if (t >= p.T) continue;  // warp-uniform
       float x[8];
-      load8(p.k + static_cast<int64_t>(b) * p.ks_b + static_cast<int64_t>(t) * p.ks_t + kvh * kD + lane * 8, x);
-      norm_rope_8(x, p.k_norm_w, cs_tab[tt], sn_tab[tt], lane);
-      *reinterpret_cast<uint4*>(p.k_pool + row * kD + lane * 8) = pack8(x, 1.0f);
-    } else {
-      *reinterpret_cast<uint4*>(p.v_pool + row * kD + lane * 8) = *reinterpret_cast<const uint4*>(
-          p.v + static_cast<int64_t>(b) * p.vs_b + static_cast<int64_t>(t) * p.vs_t + kvh * kD + lane * 8);
+      {
+        const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&raw[u]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = __bfloat1622float2(r2[i]);
+          x[2 * i] = f.x;
+          x[2 * i + 1] = f.y;
+        }
+      }
+      if (kind < kHq) {
+        norm_rope_8(x, p.q_norm_w, cs_tab[tt], sn_tab[tt], lane);
+        *reinterpret_cast<uint4*>(p.qbuf + ((static_cast<int64_t>(b) * p.T + t) * kHq + kind) * kD + lane * 8) =
+            pack8(x, 0.0625f);
+        continue;
+      }
+      const int cidx = L0 + t;
+      const int lp = cidx / kBlock;
+      const int phys = (lp < p.bt_stride) ? p.block_table[static_cast<int64_t>(b) * p.bt_stride + lp] : -1;
+      if (phys < 0 || phys >= p.num_blocks) {
+        if (lane == 0) ria_set_error(p.err, RIA_DEVERR_BAD_BLOCK);
+        continue;
+      }
+      const int kvh = (kind - kHq) & 1;
+      const int64_t row =
+          static_cast<int64_t>(kvh) * p.pool_tokens + static_cast<int64_t>(phys) * kBlock + (cidx % kBlock);
+      if (kind < kHq + kHkv) {
+        norm_rope_8(x, p.k_norm_w, cs_tab[tt], sn_tab[tt], lane);
+        *reinterpret_cast<uint4*>(p.k_pool + row * kD + lane * 8) = pack8(x, 1.0f);
+      } else {
+        *reinterpret_cast<uint4*>(p.v_pool + row * kD + lane * 8) = raw[u];
+      }
     }
   }
 }
