@@ -126,6 +126,7 @@ __device__ __forceinline__ float conv_silu(uint2 sraw, uint2 wraw, __nv_bfloat16
 
 __global__ void __launch_bounds__(kThreads, 2) gdn_decode_kernel(const GdnParams p) {
   extern __shared__ __align__(1024) unsigned char smem[];
+  pdl_wait();
   float* stage = reinterpret_cast<float*>(smem + kOffStage);
   float* red = reinterpret_cast<float*>(smem + kOffRed);
   float* qs = reinterpret_cast<float*>(smem + kOffQ);
@@ -406,6 +407,8 @@ extern "C" int ria_gdn_decode_step(const void* mixed, int64_t mixed_stride, cons
   }
   const int units = batch * kHk;
   const int grid = std::min(units, 2 * ria::num_sms());
-  gdn_decode_kernel<<<grid, kThreads, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(p);
+  const cudaError_t le = ria::launch_pdl(gdn_decode_kernel, grid, dim3(kThreads), kSmemBytes,
+                                        static_cast<cudaStream_t>(stream), p);
+  if (le != cudaSuccess) return ria::fail(RIA_ERR_CUDA, "ria_gdn_decode_step: %s", cudaGetErrorString(le));
   return ria::check_launch("ria_gdn_decode_step");
 }

@@ -90,6 +90,7 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_gemv_kernel(const float* __r
   __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(smem);  // [B][k]
   __shared__ float red[kWarps];
   auto norm = [&]() {
+    pdl_wait();  // x is the previous kernel's output (the weights were already requested)
     for (int b = 0; b < B; ++b) {  // the reduction order of rmsnorm_rows_kernel
       const float* xr = x + b * xs;
       float ss = 0.f;
@@ -132,6 +133,7 @@ __global__ void __launch_bounds__(kThreads) gemv_residual_kernel(const __nv_bflo
   extern __shared__ __align__(16) unsigned char smem[];
   __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem);  // [B][k]
   auto stage = [&]() {
+    pdl_wait();  // a and x0 are earlier kernels' outputs (the weights were already requested)
     for (int b = 0; b < B; ++b)
       for (int i = threadIdx.x * 8; i < k; i += kThreads * 8)
         *reinterpret_cast<uint4*>(xs + b * k + i) = *reinterpret_cast<const uint4*>(a + b * as + i);
@@ -174,7 +176,9 @@ cudaError_t launch_rg(const float* x, int64_t xs, const float* nw, const __nv_bf
   const int smem = B * KC * 256 * 2;
   cudaError_t e =
       cudaFuncSetAttribute(rmsnorm_gemv_kernel<B, KC, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e == cudaSuccess) rmsnorm_gemv_kernel<B, KC, D><<<grid, kThreads, smem, st>>>(x, xs, nw, w, ws, out, os, n);
+  if (e == cudaSuccess)
+    e = ria::launch_pdl(rmsnorm_gemv_kernel<B, KC, D>, dim3(grid), dim3(kThreads), smem, st, x, xs, nw, w, ws, out, os,
+                        n);
   return e;
 }
 
@@ -185,7 +189,8 @@ cudaError_t launch_gr(const __nv_bfloat16* a, int64_t as, const __nv_bfloat16* w
   cudaError_t e =
       cudaFuncSetAttribute(gemv_residual_kernel<B, KC, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e == cudaSuccess)
-    gemv_residual_kernel<B, KC, D><<<grid, kThreads, smem, st>>>(a, as, w, ws, x0, x0s, out, os, n);
+    e = ria::launch_pdl(gemv_residual_kernel<B, KC, D>, dim3(grid), dim3(kThreads), smem, st, a, as, w, ws, x0, x0s,
+                        out, os, n);
   return e;
 }
 

@@ -95,6 +95,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     gqa_decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                       const GqaParams p) {
   extern __shared__ __align__(1024) unsigned char smem[];
+  pdl_wait();
   __nv_bfloat16* qsm = reinterpret_cast<__nv_bfloat16*>(smem + kOffQ);
   float* kn = reinterpret_cast<float*>(smem + kOffKn);
   float* red = reinterpret_cast<float*>(smem + kOffRed);
@@ -405,6 +406,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // Second pass: merge split partials in log-sum-exp form, apply the gate.
 __global__ void __launch_bounds__(kD) gqa_combine_kernel(const GqaParams p) {
+  pdl_wait();
   const int b = blockIdx.x;
   const int hq = blockIdx.y;
   const int d = threadIdx.x;
@@ -589,11 +591,14 @@ extern "C" int ria_gqa_decode_paged(const void* q, int64_t q_stride, const void*
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   dim3 grid(max_splits, kHkv, batch);
-  gqa_decode_kernel<<<grid, kThreads, kSmemBytes, st>>>(tmK, tmV, p);
+  cudaError_t le = ria::launch_pdl(gqa_decode_kernel, grid, dim3(kThreads), kSmemBytes, st, tmK, tmV, p);
+  if (le != cudaSuccess) return ria::fail(RIA_ERR_CUDA, "ria_gqa_decode_paged: %s", cudaGetErrorString(le));
   rc = ria::check_launch("ria_gqa_decode_paged");
   if (rc) return rc;
   if (max_splits > 1) {
-    gqa_combine_kernel<<<dim3(batch, kHq), kD, 0, st>>>(p);
+    le = ria::launch_pdl(gqa_combine_kernel, dim3(batch, kHq), dim3(kD), 0, st, p);
+    if (le != cudaSuccess)
+      return ria::fail(RIA_ERR_CUDA, "ria_gqa_decode_paged (combine): %s", cudaGetErrorString(le));
     rc = ria::check_launch("ria_gqa_decode_paged (combine)");
   }
   return rc;

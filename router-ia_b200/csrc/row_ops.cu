@@ -11,6 +11,7 @@ __global__ void __launch_bounds__(256) rmsnorm_rows_kernel(const float* __restri
                                                            const float* __restrict__ w, __nv_bfloat16* __restrict__ out,
                                                            int64_t os, int n) {
   __shared__ float red[8];
+  pdl_wait();
   const int row = blockIdx.x;
   const float* xr = x + row * xs;
   float ss = 0.f;
@@ -37,6 +38,7 @@ __global__ void __launch_bounds__(256) rmsnorm_rows_kernel(const float* __restri
 
 __global__ void residual_add_kernel(const float* __restrict__ x0, int64_t xs, const __nv_bfloat16* __restrict__ proj,
                                     int64_t ps, float* __restrict__ out, int64_t os, int n) {
+  pdl_wait();
   const int64_t row = blockIdx.x;  // rows on x: up to 2^31 - 1 of them
   const int i = (blockIdx.y * blockDim.x + threadIdx.x) * 4;
   if (i >= n) return;
@@ -88,6 +90,7 @@ __global__ void rope_apply_kernel(float* x, int head_dim, int rope_dim, const fl
 }
 
 __global__ void advance_kernel(int32_t* lens, int32_t* pos, int n) {
+  pdl_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) {
     lens[i] += 1;
@@ -101,7 +104,9 @@ extern "C" int ria_advance_positions(int32_t* seq_lens, int32_t* positions, int3
   if (batch < 0) return ria::fail(RIA_ERR_INVALID, "ria_advance_positions: batch < 0");
   if (batch == 0) return RIA_OK;
   if (!seq_lens || !positions) return ria::fail(RIA_ERR_INVALID, "ria_advance_positions: null pointer");
-  advance_kernel<<<(batch + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(seq_lens, positions, batch);
+  const cudaError_t e = ria::launch_pdl(advance_kernel, dim3((batch + 255) / 256), dim3(256), 0,
+                                       static_cast<cudaStream_t>(stream), seq_lens, positions, batch);
+  if (e != cudaSuccess) return ria::fail(RIA_ERR_CUDA, "ria_advance_positions: %s", cudaGetErrorString(e));
   return ria::check_launch("ria_advance_positions");
 }
 
@@ -112,8 +117,9 @@ extern "C" int ria_rmsnorm_rows(const float* x, int64_t x_stride, const float* w
   if (!x || !weight || !out) return ria::fail(RIA_ERR_INVALID, "ria_rmsnorm_rows: null pointer");
   if (!ria::aligned(x, 16) || !ria::aligned(weight, 16) || !ria::aligned(out, 8) || x_stride % 4 || out_stride % 4)
     return ria::fail(RIA_ERR_INVALID, "ria_rmsnorm_rows: misaligned rows");
-  rmsnorm_rows_kernel<<<rows, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      x, x_stride, weight, static_cast<__nv_bfloat16*>(out), out_stride, n);
+  const cudaError_t e = ria::launch_pdl(rmsnorm_rows_kernel, dim3(rows), dim3(256), 0, static_cast<cudaStream_t>(stream),
+                                       x, x_stride, weight, static_cast<__nv_bfloat16*>(out), out_stride, n);
+  if (e != cudaSuccess) return ria::fail(RIA_ERR_CUDA, "ria_rmsnorm_rows: %s", cudaGetErrorString(e));
   return ria::check_launch("ria_rmsnorm_rows");
 }
 
@@ -126,8 +132,10 @@ extern "C" int ria_residual_add(const float* x0, int64_t x0_stride, const void* 
       proj_stride % 4)
     return ria::fail(RIA_ERR_INVALID, "ria_residual_add: misaligned rows");
   dim3 grid(rows, (n / 4 + 255) / 256);
-  residual_add_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      x0, x0_stride, static_cast<const __nv_bfloat16*>(proj), proj_stride, out, out_stride, n);
+  const cudaError_t e =
+      ria::launch_pdl(residual_add_kernel, grid, dim3(256), 0, static_cast<cudaStream_t>(stream), x0, x0_stride,
+                      static_cast<const __nv_bfloat16*>(proj), proj_stride, out, out_stride, n);
+  if (e != cudaSuccess) return ria::fail(RIA_ERR_CUDA, "ria_residual_add: %s", cudaGetErrorString(e));
   return ria::check_launch("ria_residual_add");
 }
 
