@@ -3,6 +3,8 @@
 // decay / beta gates, and the gated RMSNorm of the chunked rule's output.
 // Each restates, for T tokens at once, the per-token arithmetic of
 // router-ia's _linear_stateful (qwen36_attention_cache.py:176-271).
+#include <climits>
+
 #include "ria_capi_internal.h"
 #include "ria_common.cuh"
 
@@ -42,6 +44,58 @@ __global__ void conv1d_prefill_kernel(const __nv_bfloat16* __restrict__ x, int64
     h0 = h1;
     h1 = h2;
     h2 = h3;
+  }
+}
+
+// The same conv for aligned channel pairs: a thread owns two channels and
+// eight consecutive tokens, loads its eleven inputs (three of history from x
+// or the state, then its own eight) at once and writes eight bf16 pairs, so
+// every thread has one round trip to memory in flight instead of a serial
+// walk over the prompt.  Same arithmetic and order as conv1d_prefill_kernel.
+constexpr int kConvGroup = 8;
+__global__ void __launch_bounds__(256) conv1d_prefill_pairs_kernel(
+    const __nv_bfloat16* __restrict__ x, int64_t xs_b, int64_t xs_t, const __nv_bfloat16* __restrict__ state,
+    const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out, int64_t os_b, int64_t os_t, int T,
+    int pairs, int groups) {
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int b = blockIdx.y;
+  if (idx >= static_cast<int64_t>(pairs) * groups) return;
+  const int c = 2 * static_cast<int>(idx % pairs);
+  const int t0 = static_cast<int>(idx / pairs) * kConvGroup;
+  const __nv_bfloat16* xc = x + static_cast<int64_t>(b) * xs_b + c;
+  const __nv_bfloat16* st = state + (static_cast<int64_t>(b) * 2 * pairs + c) * 4;  // channel c, then c + 1
+  float2 h[kConvGroup + 3];  // inputs at tokens t0 - 3 .. t0 + 7
+#pragma unroll
+  for (int i = 0; i < kConvGroup + 3; ++i) {
+    const int t = t0 - 3 + i;
+    if (t >= 0) {
+      h[i] = t < T ? __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(xc + static_cast<int64_t>(t) * xs_t))
+                   : make_float2(0.f, 0.f);
+    } else {
+      h[i] = make_float2(__bfloat162float(st[4 + t]), __bfloat162float(st[8 + t]));
+    }
+  }
+  float w0[4], w1[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    w0[j] = __bfloat162float(w[c * 4 + j]);
+    w1[j] = __bfloat162float(w[c * 4 + 4 + j]);
+  }
+  __nv_bfloat16* oc = out + static_cast<int64_t>(b) * os_b + c;
+#pragma unroll
+  for (int k = 0; k < kConvGroup; ++k) {
+    const int t = t0 + k;
+    if (t >= T) break;
+    float a0 = w0[0] * h[k].x, a1 = w1[0] * h[k].y;
+    a0 = fmaf(w0[1], h[k + 1].x, a0);
+    a1 = fmaf(w1[1], h[k + 1].y, a1);
+    a0 = fmaf(w0[2], h[k + 2].x, a0);
+    a1 = fmaf(w1[2], h[k + 2].y, a1);
+    a0 = fmaf(w0[3], h[k + 3].x, a0);
+    a1 = fmaf(w1[3], h[k + 3].y, a1);
+    const float y0 = bf16_round(a0), y1 = bf16_round(a1);
+    *reinterpret_cast<__nv_bfloat162*>(oc + static_cast<int64_t>(t) * os_t) =
+        __floats2bfloat162_rn(y0 / (1.0f + expf(-y0)), y1 / (1.0f + expf(-y1)));
   }
 }
 
@@ -117,10 +171,21 @@ extern "C" int ria_conv1d_prefill(const void* x, int64_t x_stride_b, int64_t x_s
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(x);
   __nv_bfloat16* sb = static_cast<__nv_bfloat16*>(conv_state);
-  dim3 grid((channels + 255) / 256, (seq_len + kConvTile - 1) / kConvTile, batch);
-  conv1d_prefill_kernel<<<grid, 256, 0, st>>>(xb, x_stride_b, x_stride_t, sb, static_cast<const __nv_bfloat16*>(weight),
-                                              static_cast<__nv_bfloat16*>(out), out_stride_b, out_stride_t, seq_len,
-                                              channels);
+  const bool pairs_ok = channels % 2 == 0 && ria::aligned(x, 4) && ria::aligned(out, 4) && x_stride_b % 2 == 0 &&
+                        x_stride_t % 2 == 0 && out_stride_b % 2 == 0 && out_stride_t % 2 == 0;
+  const int groups = (seq_len + kConvGroup - 1) / kConvGroup;
+  const int64_t threads = static_cast<int64_t>(channels / 2) * groups;
+  if (pairs_ok && (threads + 255) / 256 <= INT32_MAX) {
+    conv1d_prefill_pairs_kernel<<<dim3(static_cast<unsigned>((threads + 255) / 256), batch), 256, 0, st>>>(
+        xb, x_stride_b, x_stride_t, sb, static_cast<const __nv_bfloat16*>(weight), static_cast<__nv_bfloat16*>(out),
+        out_stride_b, out_stride_t, seq_len, channels / 2, groups);
+  } else {
+    dim3 grid((channels + 255) / 256, (seq_len + kConvTile - 1) / kConvTile, batch);
+    conv1d_prefill_kernel<<<grid, 256, 0, st>>>(xb, x_stride_b, x_stride_t, sb,
+                                                static_cast<const __nv_bfloat16*>(weight),
+                                                static_cast<__nv_bfloat16*>(out), out_stride_b, out_stride_t, seq_len,
+                                                channels);
+  }
   int rc = ria::check_launch("ria_conv1d_prefill");
   if (rc) return rc;
   conv1d_state_kernel<<<dim3((channels + 255) / 256, batch), 256, 0, st>>>(xb, x_stride_b, x_stride_t, sb, seq_len,

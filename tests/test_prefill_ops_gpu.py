@@ -19,11 +19,12 @@ pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("T", [1, 2, 5, 70, 300])
-def test_conv1d_prefill_equals_steps(cuda_device, T):
+@pytest.mark.parametrize("offset", [16, 17])  # channel pairs aligned (pair kernel) or not (per-channel kernel)
+def test_conv1d_prefill_equals_steps(cuda_device, T, offset):
     B, Cc = 2, 512
     g = torch.Generator().manual_seed(T)
     wide = torch.randn(B, T, Cc + 64, generator=g).to(torch.bfloat16)  # a strided view, like the projection
-    x = wide[:, :, 16:16 + Cc]
+    x = wide[:, :, offset:offset + Cc]
     state0 = torch.randn(B, Cc, 4, generator=g).to(torch.bfloat16)
     weight = (torch.rand(Cc, 1, 4, generator=g) - 0.5).to(torch.bfloat16)
     xd, st = x.to(cuda_device), state0.to(cuda_device).contiguous()
