@@ -582,12 +582,19 @@ extern "C" int ria_gqa_decode_paged(const void* q, int64_t q_stride, const void*
   p.num_blocks = static_cast<int>(pool_tokens / kBlock);
   p.err = ria::device_error_word();
 
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(gqa_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    if (e != cudaSuccess)
-      return ria::fail(RIA_ERR_CUDA, "ria_gqa_decode_paged: smem attribute: %s", cudaGetErrorString(e));
-    attr_set = true;
+  {  // the SMEM opt-in is a per-device function attribute
+    static std::mutex mu;
+    static bool attr_set[64] = {false};
+    int dev = -1;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+      cudaError_t e =
+          cudaFuncSetAttribute(gqa_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+      if (e != cudaSuccess)
+        return ria::fail(RIA_ERR_CUDA, "ria_gqa_decode_paged: smem attribute: %s", cudaGetErrorString(e));
+      if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    }
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   dim3 grid(max_splits, kHkv, batch);

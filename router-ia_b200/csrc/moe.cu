@@ -49,6 +49,7 @@
 // lo parts into the 8 columns of one MMA, halving the MMA count.
 #include <algorithm>
 #include <cmath>
+#include <mutex>
 
 #include "ria_capi_internal.h"
 #include "ria_common.cuh"
@@ -710,8 +711,12 @@ extern "C" int ria_moe_decode(const float* residual, int64_t residual_stride, co
   const int ids_bytes = batch * top_k * 4;
   const int gu_smem = 2 * kTokens * kXStride * 2 + 2 * kWarps * 16 * kTokens * 4 + ids_bytes;
   const int dn_smem = 2 * kTokens * kHStride * 2 + ids_bytes;
-  static bool attr_set = false;
-  if (!attr_set) {
+  static std::mutex attr_mu;  // the SMEM opt-ins are per-device function attributes
+  static bool attr_set[64] = {false};
+  int dev = -1;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> attr_lock(attr_mu);
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
     const int max_ids = kMaxPairs * 4;
     cudaError_t e = cudaFuncSetAttribute(moe_route_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, kLogitSmem);
     if (e == cudaSuccess)
@@ -725,7 +730,7 @@ extern "C" int ria_moe_decode(const float* residual, int64_t residual_stride, co
                                2 * kTokens * kHStride * 2 + max_ids);
     if (e != cudaSuccess)
       return ria::fail(RIA_ERR_CUDA, "ria_moe_decode: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-    attr_set = true;
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
   MoeParams p;
   p.residual = residual;
