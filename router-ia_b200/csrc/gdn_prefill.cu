@@ -15,11 +15,11 @@
 // and runs in its own kernel, so the state recurrence is a short chain of
 // tensor-core steps.
 //   * gdn_chunk_prep_kernel: one 128-thread CTA per (chunk, value head,
-//     sequence), three CTAs per SM.  TMA loads of the Q/K tiles (3-D tensor
+//     sequence), four CTAs per SM.  TMA loads of the Q/K tiles (3-D tensor
 //     maps, no multicast), gates, G = [Q;K] [Q;K]^T on the tensor cores (the
-//     q / k norms from its diagonal),
-//     the causal score tile P and A, the 64x64 unit-lower-triangular inverse
-//     (16x16 diagonal blocks by substitution, off-diagonal blocks by tf32
+//     q / k norms from its diagonal), the causal score tile P and A, the
+//     64x64 unit-lower-triangular inverse (16x16 diagonal blocks by
+//     substitution, off-diagonal blocks by the 2x2 block rule on tf32
 //     mma.sync), then U^T = V^T TU^T and the token-major W = TW K on the
 //     tensor cores.  Writes one 41,600-byte record per (sequence, head, chunk)
 //     to the workspace: W [64][128 dk] bf16, U^T [128 dv][64] bf16, P [64][64] bf16
@@ -30,8 +30,8 @@
 //     the whole prompt; per chunk: bf16 copy of S^T into TMEM, then
 //     [X | O] = S^T [W | Qr]^T as one N = 128 product (A read from TMEM),
 //     V'^T = U^T - X (raw and column-scaled, both back into TMEM as bf16),
-//     S^T += V's^T K and O += V'^T P^T.  The chunk's operands (Q, K, W^T, U^T, P, scalars) arrive
-//     by TMA through a three-slot ring refilled as soon as a chunk's MMAs are
+//     S^T += V's^T K and O += V'^T P^T.  The chunk's operands (Q, K, W, U^T,
+//     P, scalars) arrive by TMA through a three-slot ring refilled as soon as a chunk's MMAs are
 //     complete; O is double-buffered in TMEM so the output of chunk c-1 is
 //     written while chunk c's MMAs run.
 // When the workspace holds fewer chunks than the prompt, the host runs the
