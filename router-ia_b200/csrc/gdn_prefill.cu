@@ -25,8 +25,8 @@
 //     to the workspace: W [64][128 dk] bf16, U^T [128 dv][64] bf16, P [64][64] bf16
 //     and the chunk scalars (e^gamma_C, the per-token state-update scale
 //     s_k e^(gamma_C - gamma), the per-token output scale e^gamma s_q 128^-0.5).
-//   * gdn_chunk_recurrence_kernel: one 256-thread CTA per (sequence, value
-//     head).  The fp32 state S^T (lane = dv, column = dk) stays in TMEM for
+//   * gdn_chunk_recurrence_kernel: one 512-thread CTA per (sequence, value
+//     head), four threads per TMEM lane, each on a quarter of the columns.  The fp32 state S^T (lane = dv, column = dk) stays in TMEM for
 //     the whole prompt; per chunk: bf16 copy of S^T into TMEM, then
 //     [X | O] = S^T [W | Qr]^T as one N = 128 product (A read from TMEM),
 //     V'^T = U^T - X (raw and column-scaled, both back into TMEM as bf16),
@@ -583,7 +583,7 @@ __device__ __forceinline__ void pack16(const float* v, uint32_t* pk) {
   for (int j = 0; j < 16; ++j) pk[j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
 }
 
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(512, 1)
     gdn_chunk_recurrence_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                                 const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmO,
                                 const RecParams p) {
@@ -593,7 +593,7 @@ __global__ void __launch_bounds__(256, 1)
   const int hk = h / p.group;
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
-  const int wg = tid >> 7;   // column half handled by this warpgroup
+  const int wg = tid >> 7;   // column quarter handled by this warpgroup
   const int lt = tid & 127;  // TMEM lane = dv
   const int lane = tid & 31;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kRBar);
@@ -650,9 +650,8 @@ __global__ void __launch_bounds__(256, 1)
 
   {  // initial state: warpgroup wg loads dk columns [64 wg, 64 wg + 64)
     const float* s0 = p.init_state ? p.init_state + static_cast<int64_t>(b * p.Hv + h) * kDK * kDV : nullptr;
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      const int k0 = 64 * wg + 32 * half;
+    {
+      const int k0 = 32 * wg;
       float v[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) v[i] = s0 ? s0[(k0 + i) * kDV + lt] : 0.f;
@@ -669,17 +668,17 @@ __global__ void __launch_bounds__(256, 1)
   auto stage_output = [&](int j) {
     mbar_wait_bounded(bar_o, j & 1, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
     tc::fence_after_sync();
-    float o[32];
-    tc::ld32(my_lane + kTD + 128 * (j & 1) + 64 + 32 * wg, o);
+    float o[16];
+    tc::ld16(my_lane + kTD + 128 * (j & 1) + 64 + 16 * wg, o);
     tc::wait_ld();
     unsigned char* stg = smem + (j % kSlots) * kSlotBytes + kSlWQ + (lt >> 6) * kBox;
     const bool odd = lane & 1;
     const int col = (lt & 63) & ~1;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
+    for (int i = 0; i < 8; ++i) {
       const float send = odd ? o[2 * i] : o[2 * i + 1];
       const float recv = __shfl_xor_sync(0xffffffffu, send, 1);
-      const int t = 32 * wg + 2 * i + (odd ? 1 : 0);
+      const int t = 16 * wg + 2 * i + (odd ? 1 : 0);
       const uint32_t pk = odd ? pack_bf16x2(recv, o[2 * i + 1]) : pack_bf16x2(o[2 * i], recv);
       *reinterpret_cast<uint32_t*>(stg + tc::sw128_off(t, col)) = pk;
     }
@@ -710,28 +709,24 @@ __global__ void __launch_bounds__(256, 1)
 
     // ---- bf16 S^T into TMEM (A operand of X and O), S^T *= e^gamma_C; Q rows -> Qr
     {
-      const int k0 = 64 * wg;
-      float v[64];
+      const int k0 = 32 * wg;
+      float v[32];
       uint32_t pk[16];
       tc::ld32(my_lane + kTS + k0, v);
-      tc::ld32(my_lane + kTS + k0 + 32, v + 32);
       tc::wait_ld();
       pack16(v, pk);
       tc::st16(my_lane + sb + k0 / 2, pk);
-      pack16(v + 32, pk);
-      tc::st16(my_lane + sb + k0 / 2 + 16, pk);
 #pragma unroll
-      for (int i = 0; i < 64; ++i) v[i] *= eC;
+      for (int i = 0; i < 32; ++i) v[i] *= eC;
       tc::st32(my_lane + kTS + k0, v);
-      tc::st32(my_lane + kTS + k0 + 32, v + 32);
     }
     {  // Qr = diag(output scale) Q: thread -> (row, 64-dim box, half of the row)
       const int r = tid & 63;
       unsigned char* rowp = slot + kSlWQ + (((tid >> 6) & 1) ? 3 : 1) * kBox + r * 128;
       const float sc = scal[68 + r];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const int ch = (4 * (tid >> 7) + c) ^ (r & 7);
+      for (int c = 0; c < 2; ++c) {
+        const int ch = (2 * (tid >> 7) + c) ^ (r & 7);
         uint4 u = *reinterpret_cast<uint4*>(rowp + ch * 16);
         __nv_bfloat162* h2 = reinterpret_cast<__nv_bfloat162*>(&u);
 #pragma unroll
@@ -763,19 +758,21 @@ __global__ void __launch_bounds__(256, 1)
     mbar_wait_bounded(bar_x, j & 1, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
     tc::fence_after_sync();
     {
-      float x[32], u[32];
-      uint32_t pk[16];
-      tc::ld32(my_lane + dd + 32 * wg, x);
-      load_row_bf16<32>(slot + kSlUT, lt, 32 * wg, u);
+      float x[16], u[16];
+      uint32_t pk[8];
+      tc::ld16(my_lane + dd + 16 * wg, x);
+      load_row_bf16<16>(slot + kSlUT, lt, 16 * wg, u);
       tc::wait_ld();
 #pragma unroll
-      for (int i = 0; i < 32; ++i) u[i] -= x[i];
-      pack16(u, pk);
-      tc::st16(my_lane + kTV + 16 * wg, pk);
+      for (int i = 0; i < 16; ++i) u[i] -= x[i];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) u[i] *= scal[4 + 32 * wg + i];
-      pack16(u, pk);
-      tc::st16(my_lane + kTVs + 16 * wg, pk);
+      for (int i = 0; i < 8; ++i) pk[i] = pack_bf16x2(u[2 * i], u[2 * i + 1]);
+      tc::st8(my_lane + kTV + 8 * wg, pk);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) u[i] *= scal[4 + 16 * wg + i];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) pk[i] = pack_bf16x2(u[2 * i], u[2 * i + 1]);
+      tc::st8(my_lane + kTVs + 8 * wg, pk);
       tc::wait_st();
     }
     tc::fence_before_sync();
@@ -807,9 +804,8 @@ __global__ void __launch_bounds__(256, 1)
   if (tid == kStoreTid) bulk_wait_all0();
   {
     float* sf = p.final_state + static_cast<int64_t>(b * p.Hv + h) * kDK * kDV;
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      const int k0 = 64 * wg + 32 * half;
+    {
+      const int k0 = 32 * wg;
       float v[32];
       tc::ld32(my_lane + kTS + k0, v);
       tc::wait_ld();
@@ -932,7 +928,7 @@ extern "C" int ria_gdn_chunk_prefill(const void* q, int64_t q_stride_b, int64_t 
     if (rc) return rc;
     rp.c0 = c0;
     rp.init_state = c0 == 0 ? initial_state : final_state;
-    gdn_chunk_recurrence_kernel<<<dim3(num_v_heads, batch), 256, kRSmem, st>>>(tmQ, tmK, tmW, tmO, rp);
+    gdn_chunk_recurrence_kernel<<<dim3(num_v_heads, batch), 512, kRSmem, st>>>(tmQ, tmK, tmW, tmO, rp);
     rc = ria::check_launch("ria_gdn_chunk_prefill (recurrence)");
     if (rc) return rc;
   }
