@@ -32,6 +32,7 @@ template <int B, int KC, int D, class P, class F>
 __device__ __forceinline__ void gemv_rows(const __nv_bfloat16* __restrict__ w, int64_t ws,
                                           const __nv_bfloat16* xs, int n, P&& pro, F&& f) {
   constexpr int k = KC * 256;
+  pdl_wait();  // nothing is read before the preceding kernel is complete, weights included
   const int lane = threadIdx.x & 31;
   const int warps = gridDim.x * kWarps;
   const int row0 = blockIdx.x * kWarps + (threadIdx.x >> 5);
@@ -90,7 +91,6 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_gemv_kernel(const float* __r
   __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(smem);  // [B][k]
   __shared__ float red[kWarps];
   auto norm = [&]() {
-    pdl_wait();  // x is the previous kernel's output (the weights were already requested)
     for (int b = 0; b < B; ++b) {  // the reduction order of rmsnorm_rows_kernel
       const float* xr = x + b * xs;
       float ss = 0.f;
@@ -133,7 +133,6 @@ __global__ void __launch_bounds__(kThreads) gemv_residual_kernel(const __nv_bflo
   extern __shared__ __align__(16) unsigned char smem[];
   __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem);  // [B][k]
   auto stage = [&]() {
-    pdl_wait();  // a and x0 are earlier kernels' outputs (the weights were already requested)
     for (int b = 0; b < B; ++b)
       for (int i = threadIdx.x * 8; i < k; i += kThreads * 8)
         *reinterpret_cast<uint4*>(xs + b * k + i) = *reinterpret_cast<const uint4*>(a + b * as + i);
