@@ -67,30 +67,30 @@ struct PrepParams {
 
 // RMSNorm (1+w) and partial RoPE of one 256-dim head row held as 8 values per
 // lane (lane l has dims 8l..8l+7); dims [0,64) rotate-half inside the slice.
-// cs_tab / sn_tab: cos / sin of position x inv_freq[f], f = 0..31.
-__device__ __forceinline__ void norm_rope_8(float (&x)[8], const float* w, const float* cs_tab, const float* sn_tab,
-                                            int lane) {
+// w1: this lane's 8 values of (1 + norm weight), held in registers.
+// cs_row / sn_row: cos / sin of position x inv_freq[f], f = 0..31, in SMEM.
+__device__ __forceinline__ void norm_rope_8(float (&x)[8], const float (&w1)[8], const float* cs_row,
+                                            const float* sn_row, int lane) {
   float ss = 0.f;
 #pragma unroll
   for (int i = 0; i < 8; ++i) ss += x[i] * x[i];
   ss = warp_sum(ss);
   const float r = rsqrtf(ss * (1.0f / kD) + 1e-6f);
 #pragma unroll
-  for (int i = 0; i < 8; ++i) x[i] = x[i] * r * (1.0f + w[lane * 8 + i]);
-  float partner[8];
+  for (int i = 0; i < 8; ++i) x[i] = x[i] * r * w1[i];
+  float partner[8];  // lanes 0-3 <-> 4-7: dims d and d + 32 of the rotated slice
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const float up = __shfl_down_sync(0xffffffffu, x[i], 4);
-    const float dn = __shfl_up_sync(0xffffffffu, x[i], 4);
-    partner[i] = (lane < 4) ? up : dn;
-  }
+  for (int i = 0; i < 8; ++i) partner[i] = __shfl_xor_sync(0xffffffffu, x[i], 4);
   if (lane < kRope / 8) {
+    const int f0 = (lane * 8) & (kRope / 2 - 1);
+    float cs[8], sn[8];
+    *reinterpret_cast<float4*>(cs) = *reinterpret_cast<const float4*>(cs_row + f0);
+    *reinterpret_cast<float4*>(cs + 4) = *reinterpret_cast<const float4*>(cs_row + f0 + 4);
+    *reinterpret_cast<float4*>(sn) = *reinterpret_cast<const float4*>(sn_row + f0);
+    *reinterpret_cast<float4*>(sn + 4) = *reinterpret_cast<const float4*>(sn_row + f0 + 4);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int d = lane * 8 + i;
-      const float cs = cs_tab[d & (kRope / 2 - 1)], sn = sn_tab[d & (kRope / 2 - 1)];
-      x[i] = (d < kRope / 2) ? (x[i] * cs - partner[i] * sn) : (x[i] * cs + partner[i] * sn);
-    }
+    for (int i = 0; i < 8; ++i)
+      x[i] = (lane < kRope / 16) ? (x[i] * cs[i] - partner[i] * sn[i]) : (x[i] * cs[i] + partner[i] * sn[i]);
   }
 }
 
@@ -119,8 +119,9 @@ constexpr int kPrepTokens = 8;  // prompt tokens per prep CTA
 // One CTA per 8 prompt tokens: the tokens' RoPE angles once (cos / sin of
 // position x inv_freq, 32 frequencies each), then 8 x (16 q heads + 2 k
 // heads) RMSNorm + RoPE rows and 8 x 2 V rows spread over the 8 warps.
-__global__ void __launch_bounds__(256) gqa_prefill_prep_kernel(const PrepParams p) {
-  __shared__ float cs_tab[kPrepTokens][kRope / 2], sn_tab[kPrepTokens][kRope / 2];
+__global__ void __launch_bounds__(256, 4) gqa_prefill_prep_kernel(const PrepParams p) {
+  __shared__ __align__(16) float cs_tab[kPrepTokens][kRope / 2];
+  __shared__ __align__(16) float sn_tab[kPrepTokens][kRope / 2];
   const int tb = blockIdx.x * kPrepTokens, b = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int L0 = p.seq_lens[b];
@@ -132,6 +133,9 @@ __global__ void __launch_bounds__(256) gqa_prefill_prep_kernel(const PrepParams 
     sn_tab[tt][f] = sn;
   }
   __syncthreads();
+  float wq1[8];  // (1 + q norm weight) for this lane's 8 dims (the k weight is read per k row: 2 of 20 rows)
+#pragma unroll
+  for (int i = 0; i < 8; ++i) wq1[i] = 1.0f + p.q_norm_w[lane * 8 + i];
   constexpr int kTasks = kHq + 2 * kHkv;  // per token: q heads, k heads, v heads
   constexpr int kPerWarp = kPrepTokens * kTasks / 8;
   constexpr int kInFlight = 4;  // rows a warp loads before it works on them
@@ -169,7 +173,7 @@ __global__ void __launch_bounds__(256) gqa_prefill_prep_kernel(const PrepParams 
         }
       }
       if (kind < kHq) {
-        norm_rope_8(x, p.q_norm_w, cs_tab[tt], sn_tab[tt], lane);
+        norm_rope_8(x, wq1, cs_tab[tt], sn_tab[tt], lane);
         *reinterpret_cast<uint4*>(p.qbuf + ((static_cast<int64_t>(b) * p.T + t) * kHq + kind) * kD + lane * 8) =
             pack8(x, 0.0625f);
         continue;
@@ -185,7 +189,10 @@ __global__ void __launch_bounds__(256) gqa_prefill_prep_kernel(const PrepParams 
       const int64_t row =
           static_cast<int64_t>(kvh) * p.pool_tokens + static_cast<int64_t>(phys) * kBlock + (cidx % kBlock);
       if (kind < kHq + kHkv) {
-        norm_rope_8(x, p.k_norm_w, cs_tab[tt], sn_tab[tt], lane);
+        float wk1[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) wk1[i] = 1.0f + p.k_norm_w[lane * 8 + i];
+        norm_rope_8(x, wk1, cs_tab[tt], sn_tab[tt], lane);
         *reinterpret_cast<uint4*>(p.k_pool + row * kD + lane * 8) = pack8(x, 1.0f);
       } else {
         *reinterpret_cast<uint4*>(p.v_pool + row * kD + lane * 8) = raw[u];
