@@ -331,7 +331,7 @@ __global__ void __launch_bounds__(128, 4)
     tma_load_3d(smem + kPY, &tmQ, hk * kDK + 64, c * kC, b, tma_qk);
     tma_load_3d(smem + kPY + kBox, &tmK, hk * kDK + 64, c * kC, b, tma_qk);
   }
-  if (warp == 0) {
+  if (warp == 1) {  // beside thread 0's barrier set-up and TMA issue
     tc::tmem_alloc(tslot, 128);
     tc::tmem_relinquish();
   }
@@ -563,7 +563,7 @@ __global__ void __launch_bounds__(128, 4)
     bulk_wait_read0();  // the stores have read SMEM; their writes complete with the grid
   }
   if (lt == 64) bulk_wait_read0();  // the U^T stores
-  if (warp == 0) tc::tmem_dealloc(tm, 128);
+  if (warp == 1) tc::tmem_dealloc(tm, 128);
 }
 
 struct RecParams {
