@@ -45,8 +45,13 @@ RIA_API const char* ria_last_error_string(void);
 RIA_API int ria_abi_version(void);
 
 /* Reads (and optionally clears) the device error word that kernels set when a
- * bounded wait gives up or a block-table entry is out of range.  Synchronous.
- * *code_out = 0 means no device-side error was recorded. */
+ * bounded wait gives up, a block-table entry or slot is out of range, or a
+ * sequence needs more KV splits than a GQA decode launch provides.
+ * Synchronous.  *code_out = 0 means no device-side error was recorded;
+ * otherwise the first code set: 1, 2 or 5 a bounded wait gave up (DeltaNet
+ * decode, GQA decode, prefill kernels), 3 a block id outside the pool, 6 a
+ * state slot outside the pool, 7 a too-small GQA split plan (that sequence was
+ * left untouched: no pool, workspace or output write). */
 RIA_API int ria_device_error(int clear, unsigned int* code_out);
 
 /* ------------------------------------------------------------------------
@@ -120,9 +125,11 @@ RIA_API int ria_gqa_decode_paged(const void* q, int64_t q_stride, const void* k,
 
 /* Allocation-free variant of ria_gqa_decode_paged.  No counterpart in the
  * reference (router-ia has no device kernels); it exists for callers that
- * cannot allocate device memory where they decode -- code being captured into
- * a CUDA graph, runtimes that own all GPU memory or hold a hard VRAM budget,
- * plugin interfaces that provide no workspace.  Same arguments as
+ * cannot allocate device memory where they decode: host runtimes that carve
+ * all GPU memory into their own pools up front, processes held to a hard VRAM
+ * budget, plugin interfaces that pass inputs and outputs but no workspace --
+ * for them a cudaMalloc at decode time fails, breaks the budget or bypasses
+ * the host's accounting.  Same arguments as
  * ria_gqa_decode_paged without the workspace: the split partials go to a
  * fixed RIA_GQA_STATIC_SCRATCH_BYTES array inside the library, present on
  * every GPU that loads the library until the process exits.  Calls needing
@@ -230,7 +237,8 @@ RIA_API int ria_gated_rmsnorm(const void* o, int64_t o_stride, const void* z, in
  * with tcgen05 MMAs whose A / B operands are staged K-major (0) or MN-major (1)
  * in 128-byte-swizzled shared memory -- the operand layouts the prefill
  * kernels use.  a_mn_major: 0 = A K-major in shared memory, 1 = MN-major,
- * 2 = A in tensor memory (bf16 pairs per 32-bit column).  n, k in {64, 128}.
+ * 2 = A in tensor memory (16-bit pairs per 32-bit column); adding 4 makes both
+ * operands fp16 instead of bf16.  n, k in {64, 128}.
  * Used by the tests to pin the descriptor encodings against a reference
  * matmul. */
 RIA_API int ria_umma_selftest(int32_t a_mn_major, int32_t b_mn_major, int32_t n, int32_t k, const float* a,

@@ -9,6 +9,7 @@
 
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <stdint.h>
 
 #ifndef RIA_SPIN_LIMIT
@@ -27,6 +28,7 @@ enum RiaDeviceError : unsigned int {
   RIA_DEVERR_MBAR_TIMEOUT_CHUNK = 4,
   RIA_DEVERR_MBAR_TIMEOUT_PREFILL = 5,
   RIA_DEVERR_BAD_SLOT = 6,
+  RIA_DEVERR_SPLIT_PLAN = 7,  // a sequence needs more KV splits than were launched
 };
 
 __device__ __forceinline__ void ria_set_error(unsigned int* err, unsigned int code) {
@@ -189,6 +191,11 @@ __device__ __forceinline__ void mma_bf16_16816(float* d, uint32_t a0, uint32_t a
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  __half2 v = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
 }
 

@@ -5,7 +5,7 @@
 // Descriptor encodings follow the sm100 UMMA descriptor definitions
 // (CUTLASS cute/arch/mma_sm100_desc.hpp):
 //   instruction descriptor (32 bit): [4,6) D format (1 = F32), [7,10) A format
-//     (1 = BF16), [10,13) B format, 13 negate A, 14 negate B, 15 A major
+//     (0 = F16, 1 = BF16), [10,13) B format, 13 negate A, 14 negate B, 15 A major
 //     (0 = K-major, 1 = MN-major), 16 B major, [17,23) N >> 3, [24,29) M >> 4.
 //   shared-memory descriptor (64 bit): [0,14) start address >> 4, [16,30)
 //     leading byte offset >> 4, [32,46) stride byte offset >> 4, [46,48)
@@ -44,7 +44,9 @@ __device__ __forceinline__ void fence_before_sync() {
 }
 __device__ __forceinline__ void fence_after_sync() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-// D[tmem] (+)= A[smem desc] * B[smem desc]; issued by one thread.
+// D[tmem] (+)= A[smem desc] * B[smem desc]; issued by one thread.  kind::f16
+// covers bf16 and fp16 operands alike: the instruction descriptor names the
+// type (idesc_bf16 / idesc_f16).
 __device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                          bool accumulate) {
   asm volatile(
@@ -147,6 +149,13 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int m, int n, bool a_mn_major,
   return (1u << 4) | (1u << 7) | (1u << 10) | ((negate_a ? 1u : 0u) << 13) | ((a_mn_major ? 1u : 0u) << 15) |
          ((b_mn_major ? 1u : 0u) << 16) | (static_cast<uint32_t>(n >> 3) << 17) |
          (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+// Instruction descriptor: fp16 A/B (format 0), fp32 D, M x N, operand majors.
+// Same operand layouts as bf16; A and B of one MMA always share the type.
+__host__ __device__ constexpr uint32_t idesc_f16(int m, int n, bool a_mn_major, bool b_mn_major) {
+  return (1u << 4) | ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) |
+         (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
 }
 
 // Shared-memory descriptor for a 128-byte-swizzled operand starting at

@@ -1,5 +1,6 @@
 // Self-test of the tcgen05 operand layouts used by the prefill kernels:
-// D[128 x N] = A[128 x K] * B[K x N] with bf16 operands staged in shared
+// D[128 x N] = A[128 x K] * B[K x N] with bf16 (or, with a_mode bit 2, fp16)
+// operands staged in shared
 // memory in K-major or MN-major 128-byte-swizzled tiles, or A held in TMEM
 // (a_mode 2: bf16 pairs packed into 32-bit columns), fp32 accumulation in
 // TMEM, and the result read back with tcgen05.ld.  Every address the MMA reads
@@ -14,8 +15,15 @@ namespace {
 constexpr int kM = 128;
 constexpr int kRegion = 32768;
 
+__device__ __forceinline__ uint16_t to16(float x, bool f16) {
+  if (f16) return __half_as_ushort(__float2half_rn(x));
+  return __bfloat16_as_ushort(__float2bfloat16_rn(x));
+}
+
 __global__ void __launch_bounds__(128, 1) umma_selftest_kernel(int a_mode, int b_mn, int n, int k, const float* A,
                                                                const float* B, float* D, unsigned int* err) {
+  const bool f16 = (a_mode & 4) != 0;
+  a_mode &= 3;
   extern __shared__ __align__(1024) unsigned char smem[];
   unsigned char* sa = smem;
   unsigned char* sb = smem + kRegion;
@@ -29,23 +37,23 @@ __global__ void __launch_bounds__(128, 1) umma_selftest_kernel(int a_mode, int b
   // Stage A (kM x k) and B (k x n) as bf16 in the requested layouts.
   for (int idx = tid; idx < (a_tmem ? 0 : kM * k); idx += blockDim.x) {
     const int m = idx / k, kk = idx % k;
-    const __nv_bfloat16 v = __float2bfloat16_rn(A[idx]);
+    const uint16_t v = to16(A[idx], f16);
     uint32_t off;
     if (!a_mn)  // rows = m, 64-wide K boxes of kM rows each
       off = (kk >> 6) * (kM * 128) + tc::sw128_off(m, kk & 63);
     else  // rows = k, 64-wide M blocks of k rows each
       off = (m >> 6) * (k * 128) + tc::sw128_off(kk, m & 63);
-    *reinterpret_cast<__nv_bfloat16*>(sa + off) = v;
+    *reinterpret_cast<uint16_t*>(sa + off) = v;
   }
   for (int idx = tid; idx < k * n; idx += blockDim.x) {
     const int kk = idx / n, nn = idx % n;
-    const __nv_bfloat16 v = __float2bfloat16_rn(B[idx]);
+    const uint16_t v = to16(B[idx], f16);
     uint32_t off;
     if (!b_mn)  // rows = n, 64-wide K boxes of n rows each
       off = (kk >> 6) * (n * 128) + tc::sw128_off(nn, kk & 63);
     else  // rows = k, 64-wide N blocks of k rows each
       off = (nn >> 6) * (k * 128) + tc::sw128_off(kk, nn & 63);
-    *reinterpret_cast<__nv_bfloat16*>(sb + off) = v;
+    *reinterpret_cast<uint16_t*>(sb + off) = v;
   }
   fence_proxy_async_smem();
   if (tid == 0) {
@@ -64,7 +72,8 @@ __global__ void __launch_bounds__(128, 1) umma_selftest_kernel(int a_mode, int b
     for (int j0 = 0; j0 < k / 2; j0 += 16) {
       uint32_t r[16];
       for (int j = 0; j < 16; ++j)
-        r[j] = pack_bf16x2(A[tid * k + 2 * (j0 + j)], A[tid * k + 2 * (j0 + j) + 1]);
+        r[j] = f16 ? pack_f16x2(A[tid * k + 2 * (j0 + j)], A[tid * k + 2 * (j0 + j) + 1])
+                   : pack_bf16x2(A[tid * k + 2 * (j0 + j)], A[tid * k + 2 * (j0 + j) + 1]);
       tc::st16(tc::taddr(tbase, warp * 32, kAcol + j0), r);
     }
     tc::wait_st();
@@ -74,7 +83,7 @@ __global__ void __launch_bounds__(128, 1) umma_selftest_kernel(int a_mode, int b
   }
 
   if (tid == 0) {
-    const uint32_t idesc = tc::idesc_bf16(kM, n, a_mn, b_mn);
+    const uint32_t idesc = f16 ? tc::idesc_f16(kM, n, a_mn, b_mn) : tc::idesc_bf16(kM, n, a_mn, b_mn);
     const uint32_t abase = smem_u32(sa), bbase = smem_u32(sb);
     for (int ks = 0; ks < k / 16; ++ks) {
       uint64_t ad, bd;
@@ -114,7 +123,8 @@ extern "C" int ria_umma_selftest(int32_t a_mn_major, int32_t b_mn_major, int32_t
                                  const float* b, float* d, ria_stream_t stream) {
   if ((n != 64 && n != 128) || (k != 64 && k != 128))
     return ria::fail(RIA_ERR_INVALID, "ria_umma_selftest: n and k must be 64 or 128");
-  if (a_mn_major < 0 || a_mn_major > 2) return ria::fail(RIA_ERR_INVALID, "ria_umma_selftest: a_mode must be 0, 1 or 2");
+  if ((a_mn_major & 3) > 2 || (a_mn_major & ~7) != 0)
+    return ria::fail(RIA_ERR_INVALID, "ria_umma_selftest: a_mode must be 0, 1 or 2, plus 4 for fp16 operands");
   if (!a || !b || !d) return ria::fail(RIA_ERR_INVALID, "ria_umma_selftest: null pointer");
   const int smem = 2 * kRegion + 64;
   cudaError_t e = cudaFuncSetAttribute(umma_selftest_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);

@@ -328,17 +328,17 @@ def gated_rmsnorm(o, z, weight, out):
     _check(rc, "ria_gated_rmsnorm")
 
 
-def umma_selftest(a, b, a_mn_major: int, b_mn_major: bool):
+def umma_selftest(a, b, a_mn_major: int, b_mn_major: bool, f16: bool = False):
     """d = a @ b through one tcgen05 MMA chain (a: [128, k], b: [k, n] fp32
-    CUDA tensors; operands rounded to bf16).  a_mn_major: 0 K-major, 1
-    MN-major (shared memory), 2 A held in tensor memory."""
+    CUDA tensors; operands rounded to bf16, or fp16 with ``f16``).  a_mn_major:
+    0 K-major, 1 MN-major (shared memory), 2 A held in tensor memory."""
     _require_cuda(a, b)
     a = a.float().contiguous()
     b = b.float().contiguous()
     n, k = b.shape[1], a.shape[1]
     d = torch.empty(128, n, dtype=torch.float32, device=a.device)
     with _Hooked("umma_selftest"):
-        rc = lib().ria_umma_selftest(int(a_mn_major), int(b_mn_major), n, k, a.data_ptr(), b.data_ptr(),
+        rc = lib().ria_umma_selftest(int(a_mn_major) | (4 if f16 else 0), int(b_mn_major), n, k, a.data_ptr(), b.data_ptr(),
                                      d.data_ptr(), _stream(a))
     _check(rc, "ria_umma_selftest")
     return d
