@@ -114,10 +114,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int L = p.seq_lens ? p.seq_lens[b] : p.seq_len0;
   const int total = L + 1;
   const int npages = cdiv(total, kBlock);
+  const int nsplit = cdiv(npages, p.split_pages);
+  // A split plan too small for this sequence (the launch covers
+  // max_splits * split_pages pages): record it and leave the sequence alone --
+  // no pool, partial or output write, since the trailing splits (the one that
+  // appends the new token among them) were never launched.
+  if (nsplit > static_cast<int>(gridDim.x)) {
+    if (split == 0 && kvh == 0 && tid == 0) ria_set_error(p.err, RIA_DEVERR_SPLIT_PLAN);
+    return;
+  }
   const int p_begin = split * p.split_pages;
   if (p_begin >= npages) return;
   const int p_end = min(npages, p_begin + p.split_pages);
-  const int nsplit = cdiv(npages, p.split_pages);
   const int my_pages = p_end - p_begin;
   const int pos = p.positions ? p.positions[b] : p.position0;
   const int32_t* bt = p.block_table + static_cast<int64_t>(b) * p.bt_stride;
@@ -411,10 +419,11 @@ __global__ void __launch_bounds__(kD) gqa_combine_kernel(const GqaParams p) {
   const int hq = blockIdx.y;
   const int d = threadIdx.x;
   const int npages = cdiv((p.seq_lens ? p.seq_lens[b] : p.seq_len0) + 1, kBlock);
-  // Splits past max_splits were never launched (the host sizes max_splits for
-  // the longest sequence); never read partials beyond the workspace.
-  const int nsplit = min(cdiv(npages, p.split_pages), p.max_splits);
-  if (nsplit <= 1) return;
+  // A sequence needing more splits than were launched was skipped by the
+  // attention kernel (device error RIA_DEVERR_SPLIT_PLAN): leave its output
+  // alone and never read partials beyond the workspace.
+  const int nsplit = cdiv(npages, p.split_pages);
+  if (nsplit <= 1 || nsplit > p.max_splits) return;
   const float* lse = p.part_lse + static_cast<int64_t>(b) * p.max_splits * kHq + hq;
   // Per-split weights 2^(lse - max) once, in chunks of kD splits in shared
   // memory; then each thread sums its dimension over the chunk with 16
@@ -528,6 +537,10 @@ extern "C" int ria_gqa_decode_paged(const void* q, int64_t q_stride, const void*
   if (split_pages < 1 || max_splits < 1)
     return ria::fail(RIA_ERR_INVALID, "ria_gqa_decode_paged: split_pages=%d max_splits=%d must be >= 1", split_pages,
                      max_splits);
+  if (!seq_lens && (seq_len0 / kBlock) + 1 > static_cast<int64_t>(split_pages) * max_splits)
+    return ria::fail(RIA_ERR_INVALID,
+                     "ria_gqa_decode_paged: seq_len0=%d needs %d pages, more than split_pages=%d x max_splits=%d",
+                     seq_len0, seq_len0 / kBlock + 1, split_pages, max_splits);
   if (max_splits > 65535)
     return ria::fail(RIA_ERR_INVALID, "ria_gqa_decode_paged: max_splits=%d exceeds the grid limit", max_splits);
   if (pool_tokens <= 0 || pool_tokens % kBlock != 0)
@@ -614,12 +627,14 @@ extern "C" int ria_gqa_decode_paged(const void* q, int64_t q_stride, const void*
 // ---------------------------------------------------------------- allocation-free variant
 //
 // Some callers cannot allocate device memory at the point where they decode:
-// code that is being captured into a CUDA graph (cudaMalloc is not allowed
-// during capture and synchronises the device), host runtimes that own all GPU
-// memory through their own pool or hold a hard VRAM budget, and plugin
-// interfaces that hand a kernel its inputs and outputs but no workspace.  For
-// them ria_gqa_decode_paged_static keeps the split partials in a fixed array
-// that is part of the library image instead of a caller workspace.
+// host runtimes that own all GPU memory through their own pools, processes
+// held to a hard VRAM budget, and plugin interfaces that hand a kernel its
+// inputs and outputs but no workspace -- a cudaMalloc there fails, breaks the
+// budget or bypasses the host's accounting.  For them
+// ria_gqa_decode_paged_static keeps the split partials in a fixed array that
+// is part of the library image instead of a caller workspace.  Its first call
+// on a device looks the array's address up (cudaGetSymbolAddress with that
+// device current); make that first call before any stream capture.
 //
 // The array lives for as long as the library is loaded, on every GPU that
 // loads it (RIA_GQA_STATIC_SCRATCH_BYTES each).  All calls on a device share

@@ -142,3 +142,55 @@ def test_out_of_range_block_is_reported_not_faulted(cuda_device):
                           launch.split_pages, launch.max_splits, seq_len0=100, position0=100)
     assert _ext.device_error(clear=True) != 0
     assert _ext.device_error() == 0
+
+
+def test_undersized_split_plan_is_reported_and_skipped(cuda_device):
+    """A split plan smaller than a sequence needs (max_splits x split_pages
+    pages < its pages) is caught in-kernel: the device error word reads 7
+    (RIA_DEVERR_SPLIT_PLAN), and that sequence's output, workspace partials
+    and pool rows are left untouched; the other sequence is still served."""
+    gen = torch.Generator().manual_seed(12)
+    wt = synthetic.gqa_weights(12)
+    w = GqaWeights.from_tensors(wt, cuda_device)
+    lengths = [1000, 100]  # 16 and 2 pages; 3 splits of 2 pages cover only 6
+    k_pool, v_pool, table, caches = _build_pool(lengths, 1, gen, cuda_device)
+    proj = torch.randn(2, C.GQA_PROJ_WIDTH, generator=gen).to(torch.bfloat16)
+    pd = proj.to(cuda_device)
+    seq_lens = torch.tensor(lengths, dtype=torch.int32, device=cuda_device)
+    pos = torch.tensor(lengths, dtype=torch.int32, device=cuda_device)
+    split_pages, max_splits = 2, 3
+    out = torch.full((2, 4096), 7.0, dtype=torch.bfloat16, device=cuda_device)
+    ws = torch.full((_ext.gqa_workspace_bytes(2, max_splits) // 4,), -3.0, device=cuda_device)
+    k_before, v_before = k_pool.clone(), v_pool.clone()
+    _ext.device_error(clear=True)
+    _ext.gqa_decode_paged(pd[:, :8192], pd[:, 8192:8704], pd[:, 8704:], w.q_norm, w.k_norm,
+                          rope_inv_freq(cuda_device), k_pool, v_pool, table, seq_lens, pos, out, ws, split_pages,
+                          max_splits)
+    assert _ext.device_error(clear=True) == 7
+    assert torch.all(out[0] == 7.0)
+    per_seq = ws[: 2 * max_splits * 16 * 256].view(2, max_splits, 16, 256)
+    assert torch.all(per_seq[0] == -3.0)
+    lse = ws[2 * max_splits * 16 * 256:].view(2, max_splits, 16)
+    assert torch.all(lse[0] == -3.0)
+    ids0 = caches[0][2]
+    rows0 = (ids0[:, None] * C.KV_BLOCK + torch.arange(C.KV_BLOCK)[None]).reshape(-1).to(cuda_device)
+    assert torch.equal(k_pool[:, rows0], k_before[:, rows0]) and torch.equal(v_pool[:, rows0], v_before[:, rows0])
+    # the second sequence (one split, direct output) is computed as usual
+    kc, vc, _ = caches[1]
+    ref, _, _ = O.gqa_kernel_ref(proj[1, :8192], proj[1, 8192:8704], proj[1, 8704:], wt, kc, vc, lengths[1])
+    assert O.max_err_bf16(out[1].float().cpu(), ref) < OUT_MAX_ABS
+    assert _ext.device_error() == 0
+
+
+def test_undersized_split_plan_rejected_on_host_for_scalar_length(cuda_device):
+    """With host scalars (batch 1) the same condition is an argument error."""
+    gen = torch.Generator().manual_seed(13)
+    w = GqaWeights.from_tensors(synthetic.gqa_weights(13), cuda_device)
+    k_pool, v_pool, table, _ = _build_pool([1000], 0, gen, cuda_device)
+    pd = torch.randn(1, C.GQA_PROJ_WIDTH, generator=gen).to(torch.bfloat16).to(cuda_device)
+    out = torch.empty(1, 4096, dtype=torch.bfloat16, device=cuda_device)
+    ws = torch.empty(_ext.gqa_workspace_bytes(1, 3) // 4, device=cuda_device)
+    with pytest.raises(ValueError, match="pages"):
+        _ext.gqa_decode_paged(pd[:, :8192], pd[:, 8192:8704], pd[:, 8704:], w.q_norm, w.k_norm,
+                              rope_inv_freq(cuda_device), k_pool, v_pool, table, None, None, out, ws, 2, 3,
+                              seq_len0=1000, position0=1000)
