@@ -10,11 +10,17 @@ sequence.  Metric: decode tokens/s (whole job) with the fraction of the HBM
 roofline of the dominant kernel.
 
 Multi-GPU (torchrun): each rank decodes its own 256 sequences (weak scaling, no
-collective on the path); the elapsed time is the max over ranks.
+collective on the path); the elapsed time is the max over ranks.  Two more
+multi-GPU lines ride along at N > 1: the fixed 256-sequence job split 256/N
+per GPU (strong scaling) and benchmark configuration 4 with 64 requests per
+GPU (512 at N = 8).
 
-``--impl reference`` times router-ia's algorithm on the host cores (the CPU
-oracle port of qwen36_attention_cache's layer steps, one sequence at a time as
-the reference runs) on a bounded sample of the same workload.
+``--impl reference`` times router-ia itself: the unmodified reference package
+installed under ``baseline/_ref`` (its ``qwen36_attention_cache.step_attention``
+on the host cores, one sequence at a time as router-ia runs, through a
+synthetic safetensors checkpoint) on a bounded sample of the same workload.
+The ``cpu_baseline`` of this arm's own line is the CPU oracle port of the same
+layer steps (weights converted to fp32 once).
 """
 
 from __future__ import annotations
@@ -39,14 +45,15 @@ for _p in (str(REPO / "router-ia_b200"), str(REPO)):
 import torch  # noqa: E402
 
 METRIC = "attn decode tokens/s/GPU + %HBM peak; DeltaNet chunked prefill tokens/s"
+REF_DIR = REPO / "baseline" / "_ref"  # the unmodified reference, pip-installed here
 UNIT = "tokens/s"
 B_DN = 4_292_736  # algorithmic bytes of K1 per (sequence, layer)
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 # DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) over algorithmic
-# bytes, from one ncu capture of each kernel on a small case
-# (profiles/gqa_decode_kernel_b32_l4096.md: 280.3 / 269.3 MB;
-#  profiles/gdn_decode_kernel_b64.md: 222.0 / 274.7 MB, written state partly
-#  still in L2 at kernel end).  Traffic of a full launch = ratio x its bytes.
+# bytes, from one ncu capture of each kernel on a small case (K3: 32
+# sequences at 4096 cached tokens, 280.3 of 269.3 MB; K1: 64 sequences,
+# 222.0 of 274.7 MB, the written state partly still in L2 at kernel end).
+# Traffic of a full launch = ratio x its algorithmic bytes.
 TRAFFIC_RATIO = {"gqa_decode": 280.3 / 269.3, "gdn_decode": 222.0 / 274.7}
 
 
@@ -62,6 +69,8 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true")
     ap.add_argument("--cpu-sample", type=int, default=4, help="sequences in the CPU baseline sample")
+    ap.add_argument("--reference-gpu-anchor", action="store_true",
+                    help="(internal) time the reference's own attention on cuda:0 and print one JSON line")
     return ap.parse_args()
 
 
@@ -160,28 +169,50 @@ class EventHook:
 
 
 # --------------------------------------------------------------------------- workload
-def build_engine(args, device, rank, world, headroom):
+def build_layers(device):
+    """The 40-layer stack's attention weights, seeded random init on the device."""
     from ria_b200 import constants as C, synthetic
-    from ria_b200.engine import BatchedAttentionState
-    from ria_b200.sharding import balanced_assignment
     from ria_b200.weights import DeltaNetWeights, GqaWeights
 
-    # Each rank decodes args.batch sequences whose KV lengths are a stratified
-    # sample of U[len_lo, len_hi] (the same multiset on every rank and at every
-    # GPU count: weak scaling with fixed work per GPU).  The job's request list
-    # is the ranks' lists concatenated; the cost-balanced assignment keeps
-    # each rank's list.
-    per_rank = synthetic.stratified_lengths(args.batch, args.len_lo, args.len_hi, seed=0)
-    requests = per_rank * world
-    lengths = [requests[i] for i in balanced_assignment(requests, world)[rank]]
     layers = {}
     for layer in range(C.NUM_LAYERS):
         t = synthetic.layer_weights_on_device(layer, device, seed=0)
         cls = GqaWeights if C.is_full_attention_layer(layer) else DeltaNetWeights
         layers[layer] = cls.from_tensors(t, device)
         del t
+    return layers
+
+
+def weak_lengths(args, rank, world):
+    """Each rank decodes args.batch sequences whose KV lengths are a stratified
+    sample of U[len_lo, len_hi] (the same multiset on every rank and at every
+    GPU count: weak scaling with fixed work per GPU).  The job's request list
+    is the ranks' lists concatenated; the cost-balanced assignment keeps each
+    rank's list."""
+    from ria_b200 import synthetic
+    from ria_b200.sharding import balanced_assignment
+
+    per_rank = synthetic.stratified_lengths(args.batch, args.len_lo, args.len_hi, seed=0)
+    requests = per_rank * world
+    return [requests[i] for i in balanced_assignment(requests, world)[rank]]
+
+
+def strong_lengths(args, rank, world):
+    """The fixed job of args.batch sequences (the N = 1 workload) split over
+    the ranks by the cost-balanced assignment: args.batch / world each."""
+    from ria_b200 import synthetic
+    from ria_b200.sharding import balanced_assignment
+
+    requests = synthetic.stratified_lengths(args.batch, args.len_lo, args.len_hi, seed=0)
+    return [requests[i] for i in balanced_assignment(requests, world)[rank]]
+
+
+def build_engine(args, device, rank, world, headroom, layers, lengths):
+    from ria_b200 import constants as C
+    from ria_b200.engine import BatchedAttentionState
+
     blocks = [math.ceil((n + headroom) / C.KV_BLOCK) for n in lengths]
-    eng = BatchedAttentionState(layers, batch=args.batch, pool_blocks=sum(blocks) + 8,
+    eng = BatchedAttentionState(layers, batch=len(lengths), pool_blocks=sum(blocks) + 8,
                                 max_blocks_per_seq=max(blocks) + 1, device=device)
     g = torch.Generator(device=device)
     g.manual_seed(1234 + rank)
@@ -204,12 +235,12 @@ def gqa_bytes(lengths):
     return sum(2048 * n + 2048 + 24576 for n in lengths)
 
 
-def run_ours(args, rank, world, device):
+def run_ours(args, rank, world, device, layers):
     from ria_b200 import _ext
 
     headroom = args.warmup + 2 * args.steps + 4
     t_setup = time.perf_counter()
-    eng, lengths = build_engine(args, device, rank, world, headroom)
+    eng, lengths = build_engine(args, device, rank, world, headroom, layers, weak_lengths(args, rank, world))
     setup_s = time.perf_counter() - t_setup
     x = torch.randn(args.batch, 2048, device=device).to(torch.bfloat16).float()
 
@@ -623,9 +654,9 @@ def moe_extra(device, batches=(1, 8, 64), iters=20, warmup=3):
     return out
 
 
-def config4_e2e(device, batch=64, prompt=2048, gen=256):
-    """Benchmark configuration 4 on one GPU: its per-GPU share of the 512
-    requests (64 sequences) of the random-init 40-layer 35B-A3B stack, each a
+def config4_e2e(device, batch=64, prompt=2048, gen=256, rank=0, world=1):
+    """Benchmark configuration 4 on N GPUs: each GPU serves its share of 64
+    requests (512 at N = 8) of the random-init 40-layer 35B-A3B stack, each a
     2048-token random-id prompt, then 256 greedily generated tokens.  Prefill:
     the whole prompt in one pass per layer (chunked DeltaNet K2, GQA prefill
     K4, the prompt MoE as grouped library GEMMs) and the greedy head on the
@@ -636,7 +667,10 @@ def config4_e2e(device, batch=64, prompt=2048, gen=256):
     time per step with its algorithmic bytes (attention and head weights,
     DeltaNet state read + write, KV read, the weights of the experts each
     layer's batch chose, counted on the first step) and HBM fraction, and the
-    whole job's generated tokens/s (prefill + every decode step)."""
+    whole job's generated tokens/s (prefill + every decode step).  With N > 1
+    every rank runs its own 64 requests (different prompts, replicated
+    weights, no collective on the path) and each phase's time is the max over
+    ranks."""
     from ria_b200 import constants as C, synthetic
     from ria_b200.model import ModelGraph
     from ria_b200.weights import DeltaNetWeights
@@ -645,7 +679,7 @@ def config4_e2e(device, batch=64, prompt=2048, gen=256):
     model = synthetic.config4_decode_model(device, batch, prompt, extra_tokens=gen + 8, empty=True)
     st, attn, head = model.state, model.state.layers, model.head
     g = torch.Generator(device=device)
-    g.manual_seed(404)
+    g.manual_seed(404 + rank)
     # library set-up on a short prompt, then a fresh state
     model.prefill(torch.randint(0, head.vocab, (batch, 64), device=device, generator=g, dtype=torch.int32))
     torch.cuda.synchronize(device)
@@ -653,6 +687,7 @@ def config4_e2e(device, batch=64, prompt=2048, gen=256):
     ids = torch.randint(0, head.vocab, (batch, prompt), device=device, generator=g, dtype=torch.int32)
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
     torch.cuda.synchronize(device)
+    barrier(world, device)
     ev[0].record()
     model.prefill(ids)  # -> the first generated token
     ev[1].record()
@@ -674,14 +709,16 @@ def config4_e2e(device, batch=64, prompt=2048, gen=256):
     steps = gen - 2
     lens0 = sum(st.lengths) / batch
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(device)
+    barrier(world, device)
     s.record()
     for _ in range(steps):
         graph.step()
     e.record()
     torch.cuda.synchronize(device)
-    prefill_ms = ev[0].elapsed_time(ev[1])
-    eager_ms = ev[1].elapsed_time(ev[2])
-    step_ms = s.elapsed_time(e) / steps
+    prefill_ms = reduce_max(ev[0].elapsed_time(ev[1]), world, device)
+    eager_ms = reduce_max(ev[1].elapsed_time(ev[2]), world, device)
+    step_ms = reduce_max(s.elapsed_time(e), world, device) / steps
     total_s = (prefill_ms + eager_ms + steps * step_ms) / 1e3
     n_dn = sum(1 for w in attn.values() if isinstance(w, DeltaNetWeights))
     n_gqa = C.NUM_LAYERS - n_dn
@@ -694,15 +731,248 @@ def config4_e2e(device, batch=64, prompt=2048, gen=256):
     gbs = nbytes / (step_ms * 1e-3) / 1e9
     del graph, model, st, attn, head
     torch.cuda.empty_cache()
-    return {"workload": f"config 4 on one GPU: {batch} sequences x ({prompt}-token random-id prompt + {gen} greedy "
-                        "tokens), 40 layers with 256-expert top-8 MoE + shared expert",
-            "prefill_ms": prefill_ms, "prefill_tokens_per_s": batch * prompt / (prefill_ms * 1e-3),
-            "decode_ms_per_step": step_ms, "decode_tokens_per_s": batch / (step_ms * 1e-3),
-            "e2e_generated_tokens_per_s": batch * gen / total_s, "e2e_s": total_s,
+    return {"workload": f"config 4 on {world} GPU(s): {batch} sequences per GPU, {batch * world} in total, each a "
+                        f"{prompt}-token random-id prompt + {gen} greedy tokens; 40 layers with 256-expert top-8 MoE "
+                        "+ shared expert; requests sharded by sequence, no collective",
+            "requests": batch * world, "n_gpus": world,
+            "prefill_ms": prefill_ms, "prefill_tokens_per_s": world * batch * prompt / (prefill_ms * 1e-3),
+            "decode_ms_per_step": step_ms, "decode_tokens_per_s": world * batch / (step_ms * 1e-3),
+            "e2e_generated_tokens_per_s": world * batch * gen / total_s,
+            "e2e_generated_tokens_per_s_per_gpu": batch * gen / total_s, "e2e_s": total_s,
             "active_experts_per_layer": sum(active) / len(active), "decode_bytes_per_step": nbytes,
             "decode_moe_bytes_share": moe_bytes / nbytes,
             "decode_roofline": {"bound": "hbm", "achieved": gbs, "peak": p["hbm_gbs"], "unit": "GB/s",
                                 "frac": gbs / p["hbm_gbs"], "peak_source": p["source"]}}
+
+
+def strong_scaling(args, rank, world, device, layers):
+    """Benchmark configuration 3 as a fixed job: the N = 1 workload's
+    args.batch sequences split args.batch / N per GPU by the cost-balanced
+    assignment (no collective on the path); the whole job's decode tokens/s,
+    elapsed time the max over ranks."""
+    headroom = args.warmup + args.steps + 4
+    lengths = strong_lengths(args, rank, world)
+    eng, _ = build_engine(args, device, rank, world, headroom, layers, lengths)
+    x = torch.randn(len(lengths), 2048, device=device).to(torch.bfloat16).float()
+    for _ in range(args.warmup):
+        eng.step(x)
+    torch.cuda.synchronize(device)
+    barrier(world, device)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(args.steps):
+        eng.step(x)
+    e.record()
+    torch.cuda.synchronize(device)
+    ms = reduce_max(s.elapsed_time(e), world, device)
+    kv_max = reduce_max(float(sum(lengths)), world, device)
+    del eng
+    torch.cuda.empty_cache()
+    return {"workload": f"config3 fixed job: {args.batch} sequences in total, {args.batch // world} per GPU",
+            "sequences_total": args.batch, "sequences_per_gpu": len(lengths), "kv_tokens_per_gpu_max": int(kv_max),
+            "tokens_per_s": args.batch * args.steps / (ms * 1e-3), "ms_per_step": ms / args.steps,
+            "scaling": "strong", "steps": args.steps, "warmup": args.warmup}
+
+
+def dropin_b1_stack(device, L=4096, tokens=20, warmup=3):
+    """One batch-1 token through all 40 layers via this package's
+    ``router_ia.qwen36_attention_cache.step_attention``, called layer by layer
+    exactly as router-ia's ``run_forward_token`` calls the reference module
+    (qwen36_chat_batch.py:181-207; per-call Python, split planning and the
+    registry lookups included; no MoE), with 4096 cached tokens on every GQA
+    layer.  Weights are registered in memory (the same seeded weights the
+    reference anchor writes to its checkpoint)."""
+    from ria_b200 import constants as C, synthetic
+    from router_ia import qwen36_attention_cache as cache
+
+    root = Path(tempfile.mkdtemp(prefix="ria_dropin_"))
+    for layer in range(C.NUM_LAYERS):
+        cache.register_layer_weights(root, layer, synthetic.layer_weights_on_device(layer, device, seed=0))
+    dev = f"cuda:{device.index}"
+    state = cache.state_for(root, dev)
+    state.reset()
+    cache.activate(root, state)
+    g = torch.Generator(device=device)
+    g.manual_seed(17)
+    for layer in range(C.NUM_LAYERS):
+        if C.is_full_attention_layer(layer):
+            state.full_keys[layer] = torch.randn(1, 2, L, 256, device=device, generator=g).to(torch.bfloat16)
+            state.full_values[layer] = torch.randn(1, 2, L, 256, device=device, generator=g).to(torch.bfloat16)
+        else:
+            state.linear_states[layer] = torch.randn(1, 32, 128, 128, device=device, generator=g) * 0.1
+    state.tokens_seen = L
+    x0 = torch.randn(1, 2048, device=device, generator=g)
+
+    def token(x):
+        for layer in range(C.NUM_LAYERS):
+            x = cache.step_attention(root, layer, x, dev)
+        state.tokens_seen += 1
+        return x
+
+    for _ in range(warmup):
+        token(x0)
+    torch.cuda.synchronize(device)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(tokens):
+        token(x0)
+    e.record()
+    torch.cuda.synchronize(device)
+    ms = s.elapsed_time(e) / tokens
+    cache.deactivate(root)
+    cache.reset(root)
+    return {"ms_per_token": ms, "tokens": tokens, "kv_tokens": L}
+
+
+def reference_gpu_anchor(L=4096, tokens=20, warmup=3):
+    """router-ia's own ``qwen36_attention_cache`` (the unmodified install in
+    baseline/_ref) on cuda:0: the same batch-1 40-layer token as
+    ``dropin_b1_stack``, through the reference's stock CUDA path (fp16
+    projections, fp32 ``torch.cat`` KV of 4096 cached tokens per GQA layer),
+    weights read from a synthetic safetensors checkpoint with the reference
+    tensor names and kept resident in its VRAM cache (QWEN36_VRAM_CACHE_GB)."""
+    ref = import_reference()
+    from ria_b200 import constants as C, synthetic
+    from ria_b200.weights import write_checkpoint
+
+    device = torch.device("cuda", 0)
+    root = Path(tempfile.mkdtemp(prefix="ria_refanchor_"))
+    write_checkpoint(root, {layer: {k: v.cpu() for k, v in synthetic.layer_weights_on_device(layer, device, seed=0).items()}
+                            for layer in range(C.NUM_LAYERS)})
+    dev = "cuda:0"
+    state = ref.state_for(root, dev)
+    state.reset()
+    ref.activate(root, state)
+    g = torch.Generator(device=device)
+    g.manual_seed(17)
+    for layer in range(C.NUM_LAYERS):
+        if C.is_full_attention_layer(layer):
+            state.full_keys[layer] = torch.randn(1, 2, L, 256, device=device, generator=g).to(torch.bfloat16).float()
+            state.full_values[layer] = torch.randn(1, 2, L, 256, device=device, generator=g).to(torch.bfloat16).float()
+        else:
+            state.linear_states[layer] = torch.randn(1, 32, 128, 128, device=device, generator=g) * 0.1
+    state.tokens_seen = L
+    x0 = torch.randn(1, 2048, device=device, generator=g)
+
+    def token(x):
+        for layer in range(C.NUM_LAYERS):
+            x = ref.step_attention(root, layer, x, dev)
+        state.tokens_seen += 1
+        return x
+
+    for _ in range(warmup):
+        token(x0)
+    torch.cuda.synchronize(device)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(tokens):
+        token(x0)
+    e.record()
+    torch.cuda.synchronize(device)
+    ms = s.elapsed_time(e) / tokens
+    ref.deactivate(root)
+    return {"ms_per_token": ms, "tokens": tokens, "kv_tokens": L, "module": str(Path(ref.__file__).relative_to(REPO))}
+
+
+def gpu_anchor(device):
+    """The batch-1 40-layer token through the drop-in module (this process)
+    and through the reference's own module on the same GPU (a subprocess, so
+    that ``router_ia`` names the reference package there)."""
+    ours = dropin_b1_stack(device)
+    env = dict(os.environ, QWEN36_VRAM_CACHE_GB="16", CUDA_VISIBLE_DEVICES=os.environ.get("CUDA_VISIBLE_DEVICES", "0"))
+    ref = None
+    try:
+        out = subprocess.run([sys.executable, str(REPO / "bench.py"), "--reference-gpu-anchor"], env=env,
+                             capture_output=True, text=True, timeout=900)
+        lines = [ln for ln in out.stdout.splitlines() if ln.startswith("{")]
+        ref = json.loads(lines[-1]) if out.returncode == 0 and lines else {"error": out.stderr[-600:]}
+    except (subprocess.TimeoutExpired, OSError, ValueError) as exc:
+        ref = {"error": str(exc)[-300:]}
+    res = {"workload": "1 sequence, 30 DeltaNet + 10 GQA layers, 4096 cached tokens, one token through "
+                       "qwen36_attention_cache.step_attention per layer (no MoE)",
+           "ours_ms_per_token": ours["ms_per_token"], "reference": ref}
+    if ref and "ms_per_token" in ref:
+        res["reference_ms_per_token"] = ref["ms_per_token"]
+        res["speedup_vs_reference"] = ref["ms_per_token"] / ours["ms_per_token"]
+    return res
+
+
+def import_reference():
+    """router-ia's ``qwen36_attention_cache`` from the unmodified install under
+    baseline/_ref (``pip install --target baseline/_ref`` of the reference's
+    v2 package).  Raises if it is missing or if this package's module of the
+    same name is already imported."""
+    if not (REF_DIR / "router_ia" / "qwen36_attention_cache.py").is_file():
+        raise RuntimeError("the reference is not installed under baseline/_ref")
+    if "router_ia" in sys.modules and not str(getattr(sys.modules["router_ia"], "__file__", "")).startswith(str(REF_DIR)):
+        raise RuntimeError("router_ia already names this package's module in this process")
+    sys.path.insert(0, str(REF_DIR))
+    import router_ia.qwen36_attention_cache as ref
+
+    if not Path(ref.__file__).resolve().is_relative_to(REF_DIR.resolve()):
+        raise RuntimeError(f"imported {ref.__file__}, not the reference install")
+    return ref
+
+
+def reference_cpu(args, steps, warmup, sample):
+    """router-ia itself on the host cores: the reference's own
+    ``step_attention`` (qwen36_attention_cache.py:376-379 -> _linear_stateful
+    :224-282 / _full_stateful :285-324, its CPU fp32 path with the per-call
+    weight fetch of qwen36_cached_loop.py:527-560) one sequence at a time as
+    router-ia runs, on ``sample`` sequences at stratified KV lengths of the
+    workload: per timed step, one DeltaNet and one GQA layer step per sampled
+    sequence, extrapolated to 30 + 10 layers.  Weights: the seeded synthetic
+    layer 0 (DeltaNet) and layer 3 (GQA) written as a safetensors checkpoint
+    with the reference tensor names."""
+    ref = import_reference()
+    from ria_b200 import synthetic
+    from ria_b200.weights import write_checkpoint
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    lengths = sorted(synthetic.stratified_lengths(args.batch, args.len_lo, args.len_hi, seed=0))
+    picks = [lengths[int((i + 0.5) * len(lengths) / sample)] for i in range(sample)]
+    root = Path(tempfile.mkdtemp(prefix="ria_refcpu_"))
+    write_checkpoint(root, {0: synthetic.layer_weights(0, 0), 3: synthetic.layer_weights(3, 0)})
+    g = torch.Generator().manual_seed(0)
+    seqs = []
+    for n in picks:
+        kc = torch.randn(1, 2, n, 256, generator=g).to(torch.bfloat16).float()
+        vc = torch.randn(1, 2, n, 256, generator=g).to(torch.bfloat16).float()
+        conv = (torch.randn(1, 8192, 4, generator=g) * 0.1).to(torch.bfloat16)
+        rec = torch.randn(1, 32, 128, 128, generator=g) * 0.1
+        seqs.append((n, kc, vc, conv, rec))
+    x = torch.randn(1, 2048, generator=g).to(torch.bfloat16).float()
+    state = ref.state_for(root, "cpu")
+    state.reset()
+    ref.activate(root, state)
+    per_token = []
+    for it in range(warmup + steps):
+        t_tok = 0.0
+        for n, kc, vc, conv, rec in seqs:
+            state.linear_states[0], state.linear_conv_states[0] = rec.clone(), conv.clone()
+            state.full_keys[3], state.full_values[3] = kc, vc
+            state.tokens_seen = n
+            t0 = time.perf_counter()
+            ref.step_attention(root, 0, x, "cpu")
+            t1 = time.perf_counter()
+            ref.step_attention(root, 3, x, "cpu")
+            t2 = time.perf_counter()
+            t_tok += 30 * (t1 - t0) + 10 * (t2 - t1)
+        if it >= warmup:
+            per_token.append(t_tok / len(seqs))
+    ref.deactivate(root)
+    sec_per_token = statistics.mean(per_token)
+    return {
+        "value": 1.0 / sec_per_token,
+        "unit": UNIT,
+        "cores": torch.get_num_threads(),
+        "kind": "reference",
+        "sample": (f"router-ia's own step_attention (baseline/_ref) on {sample} sequences at KV lengths {picks} "
+                   f"(strata of the workload), one DeltaNet and one GQA layer step each per timed step, "
+                   f"extrapolated to 30+10 layers; {steps} timed steps"),
+        "cpu": _cpu_model(),
+    }
 
 
 # --------------------------------------------------------------------------- CPU reference (oracle port)
@@ -774,10 +1044,18 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
 
+    if args.reference_gpu_anchor:
+        print(json.dumps(reference_gpu_anchor()), flush=True)
+        return
+
     if args.impl == "reference":
         if rank != 0:
             return
-        ref = cpu_reference(args, steps=args.steps, warmup=args.warmup, sample=args.cpu_sample)
+        try:
+            ref = reference_cpu(args, steps=args.steps, warmup=args.warmup, sample=args.cpu_sample)
+        except RuntimeError as exc:
+            print(json.dumps({"impl": "reference", "unavailable": str(exc)}), flush=True)
+            return
         line = {
             "metric": METRIC, "impl": "reference", "value": ref["value"], "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 / ref["value"],
@@ -798,15 +1076,34 @@ def main():
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
     try:
-        line = run_ours(args, rank, world, device)
-        if rank == 0 and not args.no_extras:
-            line["config1_gqa_b1_l4096"] = config1_latency(device)
-            line["config2_prefill"] = config2_prefill(device)
-            line["gqa_prefill_1x8192"] = gqa_prefill_extra(device)
-            line["decode_b1_stack_l4096"] = decode_b1_stack(device)
-            line["config0_deltanet_b1"] = config0_deltanet(device)
-            line["moe_block"] = moe_extra(device)
-            line["config4_e2e_b64"] = config4_e2e(device)
+        layers = build_layers(device)
+        line = run_ours(args, rank, world, device, layers)
+        if not args.no_extras:
+            if world > 1:
+                # multi-GPU lines, every rank taking part: the fixed 256-sequence
+                # job split 256/N (strong scaling) and configuration 4 with 64
+                # requests per GPU
+                strong = strong_scaling(args, rank, world, device, layers)
+                del layers
+                torch.cuda.empty_cache()
+                c4 = config4_e2e(device, rank=rank, world=world)
+                if rank == 0:
+                    line["strong_scaling"] = strong
+                    line["config4_e2e"] = c4
+            else:
+                line["strong_scaling"] = {"same_as": "value (the N = 1 fixed job is the headline workload)",
+                                          "tokens_per_s": line["value"], "ms_per_step": line["ms_per_step"],
+                                          "sequences_per_gpu": args.batch, "scaling": "strong"}
+                del layers
+                torch.cuda.empty_cache()
+                line["config1_gqa_b1_l4096"] = config1_latency(device)
+                line["config2_prefill"] = config2_prefill(device)
+                line["gqa_prefill_1x8192"] = gqa_prefill_extra(device)
+                line["decode_b1_stack_l4096"] = decode_b1_stack(device)
+                line["dropin_vs_reference_b1_l4096"] = gpu_anchor(device)
+                line["config0_deltanet_b1"] = config0_deltanet(device)
+                line["moe_block"] = moe_extra(device)
+                line["config4_e2e"] = config4_e2e(device)
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_reference(args, steps=2, warmup=1, sample=args.cpu_sample)
         if rank == 0:

@@ -149,6 +149,24 @@ RIA_API int ria_gqa_decode_paged_static(const void* q, int64_t q_stride, const v
                                         int64_t out_stride, int32_t batch, int32_t split_pages, int32_t max_splits,
                                         ria_stream_t stream);
 
+/* Append one token's post-RoPE K and V rows per sequence to the paged cache:
+ * the storage step of _append_full_kv (qwen36_attention_cache.py:365-373; the
+ * reference's limit checks, :344-363, stay with the caller).  The GQA decode
+ * and prefill kernels fuse this write into their attention pass; this entry
+ * point serves callers that compute K/V themselves.
+ * k_new, v_new [B, 512] (2 KV heads x 256), bf16 or, with inputs_f32, f32
+ *        (rounded to bf16), rows 16-byte aligned (k_stride / v_stride in
+ *        elements).
+ * k_pool, v_pool, block_table, block_table_stride: as ria_gqa_decode_paged.
+ * seq_lens [B]: the row index each token goes to (the cached length); NULL
+ *        for batch 1 with seq_len0.
+ * A block id outside the pool is recorded as device error 3 and that
+ * sequence is left untouched. */
+RIA_API int ria_kv_append_paged(const void* k_new, int64_t k_stride, const void* v_new, int64_t v_stride,
+                                int32_t inputs_f32, void* k_pool, void* v_pool, int64_t pool_tokens,
+                                const int32_t* block_table, int32_t block_table_stride, const int32_t* seq_lens,
+                                int32_t seq_len0, int32_t batch, ria_stream_t stream);
+
 /* Split size heuristic used by the Python host: KV blocks per split so that the
  * grid holds a few waves of CTAs for `total_blocks` blocks of work. */
 RIA_API int32_t ria_gqa_decode_split_pages(int64_t total_blocks, int32_t num_kv_heads);
@@ -252,14 +270,21 @@ RIA_API int ria_umma_selftest(int32_t a_mn_major, int32_t b_mn_major, int32_t n,
  * Replaces rmsnorm (qwen36_op_probe.py:55-67) on the layer input. */
 RIA_API int ria_rmsnorm_rows(const float* x, int64_t x_stride, const float* weight, void* out, int64_t out_stride, int32_t rows,
                      int32_t n, ria_stream_t stream);
+/* The same norm with an fp16 output: the input of the fp16 in-projections
+ * (router-ia's CUDA path runs its projections on fp16 weights,
+ * qwen36_cached_loop.py:552-557). */
+RIA_API int ria_rmsnorm_rows_f16(const float* x, int64_t x_stride, const float* weight, void* out,
+                                 int64_t out_stride, int32_t rows, int32_t n, ria_stream_t stream);
 
 /* Small-batch projections (batch <= 8), weight-streaming GEMVs with the
  * neighbouring row ops fused (the "projection fusion" of the layer steps):
  *
- * ria_rmsnorm_gemv: out[b, n] (bf16) = W[n, :] . bf16(rmsnorm(x[b]) * (1 + norm_w)),
+ * ria_rmsnorm_gemv: out[b, n] (bf16) = W[n, :] . fp16(rmsnorm(x[b]) * (1 + norm_w)),
  *   the layer's input RMSNorm (qwen36_op_probe.py:55-67) and its fused
  *   in-projection (qwen36_attention_cache.py:228-240 DeltaNet, :289-297 GQA);
- *   x [batch, k] f32, W [n, k] bf16 (row stride w_stride), out bf16.
+ *   x [batch, k] f32, W [n, k] fp16 (row stride w_stride), fp32 accumulation,
+ *   out bf16 -- the activations the ria_rmsnorm_rows_f16 + fp16 GEMM path
+ *   produces.
  * ria_gemv_residual: out[b, n] (f32) = x0[b, n] + bf16(W[n, :] . a[b]), the
  *   out-projection and the residual add that end the layer (:272-277, :318-321);
  *   a [batch, k] bf16, x0 / out f32.

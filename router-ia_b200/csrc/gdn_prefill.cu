@@ -22,14 +22,15 @@
 //     substitution, off-diagonal blocks by the 2x2 block rule on tf32
 //     mma.sync), then U^T = V^T TU^T and the token-major W = TW K on the
 //     tensor cores.  Writes one 41,600-byte record per (sequence, head, chunk)
-//     to the workspace: W [64][128 dk] fp16, U^T [128 dv][64] fp16, P [64][64] fp16
+//     to the workspace: W [64][128 dk] bf16, U^T [128 dv][64] fp16, P [64][64] bf16
 //     and the chunk scalars (e^gamma_C, the per-token state-update scale
 //     s_k e^(gamma_C - gamma), the per-token output scale e^gamma s_q 128^-0.5).
 //   * gdn_chunk_recurrence_kernel: one 512-thread CTA per (sequence, value
 //     head), four threads per TMEM lane, each on a quarter of the columns.  The fp32 state S^T (lane = dv, column = dk) stays in TMEM for
-//     the whole prompt; per chunk: fp16 copy of S^T into TMEM, then
+//     the whole prompt; per chunk: bf16 copy of S^T into TMEM, then
 //     [X | O] = S^T [W | Qr]^T as one N = 128 product (A read from TMEM),
-//     V'^T = U^T - X (raw and column-scaled, both back into TMEM as fp16),
+//     V'^T = U^T - X (raw as bf16 for O, column-scaled as fp16 for the state,
+//     both back into TMEM),
 //     S^T += V's^T K and O += V'^T P^T.  The chunk's operands (Q, K, W, U^T,
 //     P, scalars) arrive by TMA through a three-slot ring refilled as soon as a chunk's MMAs are
 //     complete; O is double-buffered in TMEM so the output of chunk c-1 is
@@ -39,17 +40,21 @@
 // product is an M = 128 UMMA (tcgen05.mma cta_group::1 kind::f16, fp32
 // accumulation in TMEM); every wait is bounded.
 //
-// Operand precision: q, k, v arrive as bf16 and the Gram product [Q;K][Q;K]^T
-// runs on them as they are (exact products).  Every other tensor-core operand
-// is fp16 (11-bit significand, rounding 2^-11 against bf16's 2^-8): P, the
-// T-inverse tiles TW and TU, U^T, W, the state copy S^T, V'^T and V's^T, and
-// the K, V and Qr tiles converted in shared memory.  With bf16 operands the
-// final fp32 state sat about 3e-3 (relative RMS) from the token-by-token rule,
-// set by the roundings of TU, U^T and V's^T; fp16 brings it to about 4e-4 at
-// the same instruction count.  fp16's range holds every operand for inputs
-// below 65504 in magnitude (q and k are normalised, T has unit diagonal and
-// entries of order one, the state and U are of the order of v) -- the range
-// router-ia's own CUDA path computes q, k and v in (its projections are fp16).
+// Operand precision: q, k, v arrive as bf16.  The products that feed the
+// state run on fp16 operands (11-bit significand: rounding 2^-12 against
+// bf16's 2^-9): U^T = V^T TU^T (TU and V in fp16, U^T stored fp16) and the
+// state update S^T += V's^T K (V's^T and K in fp16), with K and V converted
+// in shared memory.  With bf16 there, the final fp32 state sat about 3e-3
+// (relative RMS) from the token-by-token rule, set by the roundings of TU,
+// U^T and V's^T; fp16 brings it to about 4e-4 at the same instruction count.
+// The other products keep bf16 operands (the Gram product on the raw q / k,
+// W = TW K, [X | O] = S^T [W | Qr]^T with a bf16 copy of the state, O +=
+// V'^T P^T): they reach the final state only through tokens whose weight in it
+// has decayed, and the outputs through errors far inside their bar.  fp16's
+// range holds every fp16 operand for inputs below 65504 in magnitude (T has a
+// unit diagonal and entries of order one; U and the state are of the order of
+// v) -- the range router-ia's own CUDA path computes q, k and v in (its
+// projections are fp16).
 #include <algorithm>
 #include <climits>
 
@@ -67,9 +72,9 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr uint32_t kBox = 8192;  // 64 rows x 128 bytes, 128-byte swizzled
 
 // Workspace record of one (sequence, value head, chunk).
-constexpr uint32_t kRecW = 0;          // W [64 tokens][128 dk] fp16 as two [64][64] boxes (dk 0-63, 64-127)
+constexpr uint32_t kRecW = 0;          // W [64 tokens][128 dk] bf16 as two [64][64] boxes (dk 0-63, 64-127)
 constexpr uint32_t kRecUT = 16384;     // U^T [128 dv][64 tokens] fp16
-constexpr uint32_t kRecP = 32768;      // P [64 t][64 j] fp16
+constexpr uint32_t kRecP = 32768;      // P [64 t][64 j] bf16
 constexpr uint32_t kRecScal = 40960;   // f32: [0] e^gamma_C, [4..67] state scale, [68..131] output scale
 constexpr uint32_t kScalBytes = 528;   // 132 floats
 constexpr uint32_t kRecBytes = 41600;  // 325 rows of 128 bytes
@@ -81,7 +86,7 @@ constexpr uint32_t kRecRows = kRecBytes / 128;
 // Q box for its TMA store, then V (dims 0-63, 64-127) is loaded over the two
 // Q boxes, and once U^T is computed its staging tile goes over V.  A and T
 // are fp32 and keep only their ten lower-triangular 16x16 blocks (padded rows
-// of kBl floats); after the inverse the fp16 operand tiles TW | TU go over A
+// of kBl floats); after the inverse the operand tiles TW (bf16) | TU (fp16) go over A
 // and the front of T, and W is staged over them once its product is done.
 // Four CTAs fit on an SM.
 constexpr int kBl = 17;
@@ -89,7 +94,7 @@ constexpr uint32_t kBlkBytes = 16 * kBl * 4;  // 1088
 constexpr uint32_t kPX = 0, kPY = 2 * kBox;
 constexpr uint32_t kPA = 4 * kBox;              // fp32 A, packed blocks
 constexpr uint32_t kPT = kPA + 10 * kBlkBytes;  // fp32 T, packed blocks
-constexpr uint32_t kPTw = kPA;                  // fp16 TW | TU (two boxes) once T is consumed
+constexpr uint32_t kPTw = kPA;                  // TW (bf16) | TU (fp16), two boxes, once T is consumed
 constexpr uint32_t kPMisc = kPT + 10 * kBlkBytes;
 constexpr uint32_t kPGam = kPMisc, kPBet = kPMisc + 256, kPSq = kPMisc + 512, kPSk = kPMisc + 768,
                    kPEbk = kPMisc + 1024, kPGraw = kPMisc + 1280;
@@ -119,23 +124,27 @@ constexpr uint32_t kRSmem = kRBar + 128;
 constexpr uint32_t kChunkTx = 9 * kBox + kScalBytes;
 static_assert(kRSmem <= 227 * 1024, "recurrence SMEM");
 
-// Recurrence TMEM columns: S^T fp32, [X | O] (two buffers of 128), fp16 S^T,
-// fp16 V'^T, fp16 V's^T -- all 512 columns.
+// Recurrence TMEM columns: S^T fp32, [X | O] (two buffers of 128), bf16 S^T,
+// bf16 V'^T, fp16 V's^T -- all 512 columns.
 constexpr uint32_t kTS = 0, kTD = 128, kTSb = 384, kTV = 448, kTVs = 480;
 
 constexpr uint32_t kBarPrep = 1;
 
-// N fp32 values as fp16 into row `row`, columns col0.. of a 128-byte-swizzled
-// 16-bit tile (the internal operand type, see the file comment).
-template <int N>
-__device__ __forceinline__ void store_row_f16(unsigned char* tile, int row, int col0, const float* v) {
+__device__ __forceinline__ uint32_t pack16x2(bool f16, float lo, float hi) {
+  return f16 ? pack_f16x2(lo, hi) : pack_bf16x2(lo, hi);
+}
+
+// N fp32 values as fp16 (F16) or bf16 into row `row`, columns col0.. of a
+// 128-byte-swizzled 16-bit tile.
+template <bool F16, int N>
+__device__ __forceinline__ void store_row(unsigned char* tile, int row, int col0, const float* v) {
 #pragma unroll
   for (int i = 0; i < N; i += 8) {
     uint4 pk;
-    pk.x = pack_f16x2(v[i], v[i + 1]);
-    pk.y = pack_f16x2(v[i + 2], v[i + 3]);
-    pk.z = pack_f16x2(v[i + 4], v[i + 5]);
-    pk.w = pack_f16x2(v[i + 6], v[i + 7]);
+    pk.x = pack16x2(F16, v[i], v[i + 1]);
+    pk.y = pack16x2(F16, v[i + 2], v[i + 3]);
+    pk.z = pack16x2(F16, v[i + 4], v[i + 5]);
+    pk.w = pack16x2(F16, v[i + 6], v[i + 7]);
     *reinterpret_cast<uint4*>(tile + tc::sw128_off(row, col0 + i)) = pk;
   }
 }
@@ -457,7 +466,7 @@ __global__ void __launch_bounds__(128, 4)
         }
       }
       if (is_p) {
-        store_row_f16<32>(smem + kPX, i, j0, v);
+        store_row<false, 32>(smem + kPX, i, j0, v);
       } else {
 #pragma unroll
         for (int gq = 0; gq < 2; ++gq) {
@@ -476,9 +485,6 @@ __global__ void __launch_bounds__(128, 4)
         *reinterpret_cast<uint4*>(smem + kPX + tc::sw128_off(i, c8)) = make_uint4(0u, 0u, 0u, 0u);
     }
   }
-  // The Gram product has read the K tile: to fp16 for W = TW K.
-  bf16_to_f16_inplace(smem + kPX + kBox, kBox / 16, lt, 128);
-  bf16_to_f16_inplace(smem + kPY + kBox, kBox / 16, lt, 128);
   fence_proxy_async_smem();
   tc::fence_before_sync();
   named_bar_sync(kBarPrep, 128);  // G consumed, A complete, P staged over the first Q box
@@ -494,7 +500,7 @@ __global__ void __launch_bounds__(128, 4)
     tma_load_3d(smem + kPY, &tmV, h * kDV + 64, c * kC, b, tma_v);
   }
   invert_unit_lower64(reinterpret_cast<float*>(smem + kPA), reinterpret_cast<float*>(smem + kPT), lt);
-  {  // TW = T diag(beta e^gamma s_k) (lanes 0-63), TU = T diag(beta) (lanes 64-127), fp16;
+  {  // TW = T diag(beta e^gamma s_k) (lanes 0-63, bf16), TU = T diag(beta) (lanes 64-127, fp16);
      // T's row i is zero past its diagonal block.  All of T is read before
      // the tiles are written over A and T.
     const int i = lt & 63;
@@ -512,7 +518,7 @@ __global__ void __launch_bounds__(128, 4)
           x0 = trow[e] * cs[16 * bj + e];
           x1 = trow[e + 1] * cs[16 * bj + e + 1];
         }
-        pk[8 * bj + e / 2] = pack_f16x2(x0, x1);
+        pk[8 * bj + e / 2] = pack16x2(lt >= 64, x0, x1);
       }
     }
     named_bar_sync(kBarPrep, 128);
@@ -558,7 +564,7 @@ __global__ void __launch_bounds__(128, 4)
       float v[32];
       tc::ld32(my_lane + kTmU + 32 * hf, v);
       tc::wait_ld();
-      store_row_f16<32>(tile, lt & 63, 32 * hf, v);
+      store_row<true, 32>(tile, lt & 63, 32 * hf, v);
     }
   }
   fence_proxy_async_smem();
@@ -573,7 +579,7 @@ __global__ void __launch_bounds__(128, 4)
   // 64-127), B = the K tile (MN-major, dk across the two boxes), N = 128 dk
   if (lt == 0) {
     tc::fence_after_sync();
-    const uint32_t id = tc::idesc_f16(128, 128, false, true);
+    const uint32_t id = tc::idesc_bf16(128, 128, false, true);
     for (int ks = 0; ks < 4; ++ks)
       tc::mma_bf16(tm + kTmW, tc::sdesc_sw128(sbase + kPTw + ks * 32, 16, 1024),
                    tc::sdesc_sw128(sbase + kPX + kBox + ks * 2048, kPY - kPX, 1024), id, ks > 0);
@@ -587,7 +593,7 @@ __global__ void __launch_bounds__(128, 4)
       float v[32];
       tc::ld32(my_lane + kTmW + 32 * q32, v);
       tc::wait_ld();
-      store_row_f16<32>(smem + kPTw + (q32 >> 1) * kBox, lt, 32 * (q32 & 1), v);
+      store_row<false, 32>(smem + kPTw + (q32 >> 1) * kBox, lt, 32 * (q32 & 1), v);
     }
   }
   fence_proxy_async_smem();
@@ -615,9 +621,9 @@ struct RecParams {
   unsigned int* err;
 };
 
-__device__ __forceinline__ void pack16_f16(const float* v, uint32_t* pk) {
+__device__ __forceinline__ void pack16(const float* v, uint32_t* pk) {
 #pragma unroll
-  for (int j = 0; j < 16; ++j) pk[j] = pack_f16x2(v[2 * j], v[2 * j + 1]);
+  for (int j = 0; j < 16; ++j) pk[j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
 }
 
 __global__ void __launch_bounds__(512, 1)
@@ -739,19 +745,19 @@ __global__ void __launch_bounds__(512, 1)
     unsigned char* slot = smem + s * kSlotBytes;
     const uint32_t aslot = sbase + s * kSlotBytes;
     const float* scal = reinterpret_cast<const float*>(slot + kSlScal);
-    const uint32_t sb = kTSb;                  // fp16 S^T
+    const uint32_t sb = kTSb;                  // bf16 S^T
     const uint32_t dd = kTD + 128 * (j & 1);  // this chunk's [X | O]
     mbar_wait_bounded(&full[s], (j / kSlots) & 1, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
     const float eC = scal[0];
 
-    // ---- fp16 S^T into TMEM (A operand of X and O), S^T *= e^gamma_C; Q rows -> Qr (fp16)
+    // ---- bf16 S^T into TMEM (A operand of X and O), S^T *= e^gamma_C; Q rows -> Qr
     {
       const int k0 = 32 * wg;
       float v[32];
       uint32_t pk[16];
       tc::ld32(my_lane + kTS + k0, v);
       tc::wait_ld();
-      pack16_f16(v, pk);
+      pack16(v, pk);
       tc::st16(my_lane + sb + k0 / 2, pk);
 #pragma unroll
       for (int i = 0; i < 32; ++i) v[i] *= eC;
@@ -769,7 +775,7 @@ __global__ void __launch_bounds__(512, 1)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const float2 f = __bfloat1622float2(h2[e]);
-          reinterpret_cast<uint32_t*>(&u)[e] = pack_f16x2(f.x * sc, f.y * sc);
+          h2[e] = __floats2bfloat162_rn(f.x * sc, f.y * sc);
         }
         *reinterpret_cast<uint4*>(rowp + ch * 16) = u;
       }
@@ -784,7 +790,7 @@ __global__ void __launch_bounds__(512, 1)
     // ---- [X | O] = S^T [W | Qr]^T; meanwhile the previous chunk's output goes to staging
     if (tid == 0) {
       tc::fence_after_sync();
-      const uint32_t idXO = tc::idesc_f16(128, 128, false, false);
+      const uint32_t idXO = tc::idesc_bf16(128, 128, false, false);
       for (int ks = 0; ks < 8; ++ks)
         tc::mma_bf16_ts(tm + dd, tm + sb + ks * 8,
                         tc::sdesc_sw128(aslot + kSlWQ + (ks >> 2) * (2 * kBox) + (ks & 3) * 32, 16, 1024), idXO,
@@ -793,7 +799,7 @@ __global__ void __launch_bounds__(512, 1)
     }
     if (j > 0) stage_output(j - 1);
 
-    // ---- V'^T = U^T - X: raw (for O) and column-scaled (for the state), fp16 into TMEM
+    // ---- V'^T = U^T - X: raw (bf16, for O) and column-scaled (fp16, for the state) into TMEM
     mbar_wait_bounded(bar_x, j & 1, p.err, RIA_DEVERR_MBAR_TIMEOUT_PREFILL);
     tc::fence_after_sync();
     {
@@ -805,7 +811,7 @@ __global__ void __launch_bounds__(512, 1)
 #pragma unroll
       for (int i = 0; i < 16; ++i) u[i] -= x[i];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) pk[i] = pack_f16x2(u[2 * i], u[2 * i + 1]);
+      for (int i = 0; i < 8; ++i) pk[i] = pack_bf16x2(u[2 * i], u[2 * i + 1]);
       tc::st8(my_lane + kTV + 8 * wg, pk);
 #pragma unroll
       for (int i = 0; i < 16; ++i) u[i] *= scal[4 + 16 * wg + i];
@@ -825,7 +831,7 @@ __global__ void __launch_bounds__(512, 1)
         tc::mma_bf16_ts(tm + kTS, tm + kTVs + ks * 8, tc::sdesc_sw128(aslot + kSlK + ks * 2048, kBox, 1024), idS,
                         true);
       tc::commit(bar_s);
-      const uint32_t idO = tc::idesc_f16(128, 64, false, false);
+      const uint32_t idO = tc::idesc_bf16(128, 64, false, false);
       for (int ks = 0; ks < 4; ++ks)
         tc::mma_bf16_ts(tm + dd + 64, tm + kTV + ks * 8, tc::sdesc_sw128(aslot + kSlP + ks * 32, 16, 1024), idO,
                         true);

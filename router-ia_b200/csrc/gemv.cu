@@ -10,13 +10,35 @@
 // weight row (coalesced, read once), multiplies them with the B input rows
 // staged in shared memory, and the warp reduces.  The in-projection CTA first
 // recomputes the RMSNorm of its B input rows with the same reduction order as
-// ria_rmsnorm_rows, so both paths produce the same bf16 activations.
+// ria_rmsnorm_rows_f16, so both paths produce the same fp16 activations.
+//
+// Types: the in-projection runs on fp16 weights and fp16 normalised inputs
+// (fp32 accumulation, bf16 output), the out-projection on bf16 weights and
+// the bf16 attention output.  fp16 for the in-projection input keeps the
+// layer within the attention path's per-token bars against the fp32 CPU
+// path: rounding the normalised input to bf16 (2^-9) moved single tokens'
+// attention contribution by up to ~1.9e-2 relative RMS, fp16 (2^-12) by
+// ~6e-3.  router-ia's own CUDA path runs these projections on fp16 weights.
 #include <algorithm>
 
 #include "ria_capi_internal.h"
 #include "ria_common.cuh"
 
 namespace {
+
+__device__ __forceinline__ float2 to_float2(__nv_bfloat162 v) { return __bfloat1622float2(v); }
+__device__ __forceinline__ float2 to_float2(__half2 v) { return __half22float2(v); }
+
+template <class T>
+struct Vec2;
+template <>
+struct Vec2<__nv_bfloat16> {
+  using type = __nv_bfloat162;
+};
+template <>
+struct Vec2<__half> {
+  using type = __half2;
+};
 
 constexpr int kMaxBatch = 8;
 constexpr int kThreads = 256;
@@ -28,9 +50,9 @@ constexpr int kWarps = kThreads / 32;
 // while row r is reduced.  pro() runs once the first rows' loads are issued
 // (it stages the inputs, so the two overlap); f(row, acc[B]) consumes each
 // finished row (lane 0's values are the sums).
-template <int B, int KC, int D, class P, class F>
-__device__ __forceinline__ void gemv_rows(const __nv_bfloat16* __restrict__ w, int64_t ws,
-                                          const __nv_bfloat16* xs, int n, P&& pro, F&& f) {
+template <class T, int B, int KC, int D, class P, class F>
+__device__ __forceinline__ void gemv_rows(const T* __restrict__ w, int64_t ws, const T* xs, int n, P&& pro, F&& f) {
+  using T2 = typename Vec2<T>::type;
   constexpr int k = KC * 256;
   pdl_wait();  // nothing is read before the preceding kernel is complete, weights included
   const int lane = threadIdx.x & 31;
@@ -54,15 +76,15 @@ __device__ __forceinline__ void gemv_rows(const __nv_bfloat16* __restrict__ w, i
     for (int b = 0; b < B; ++b) acc[b] = 0.f;
 #pragma unroll
     for (int c = 0; c < KC; ++c) {
-      const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&ring[0][c]);
+      const T2* w2 = reinterpret_cast<const T2*>(&ring[0][c]);
 #pragma unroll
       for (int b = 0; b < B; ++b) {
         const uint4 u = *reinterpret_cast<const uint4*>(xs + b * k + c * 256 + lane * 8);
-        const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&u);
+        const T2* x2 = reinterpret_cast<const T2*>(&u);
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float2 wf = __bfloat1622float2(w2[e]);
-          const float2 xf = __bfloat1622float2(x2[e]);
+          const float2 wf = to_float2(w2[e]);
+          const float2 xf = to_float2(x2[e]);
           acc[b] = fmaf(wf.x, xf.x, acc[b]);
           acc[b] = fmaf(wf.y, xf.y, acc[b]);
         }
@@ -80,15 +102,15 @@ __device__ __forceinline__ void gemv_rows(const __nv_bfloat16* __restrict__ w, i
   }
 }
 
-// out[b, :] = bf16(W . bf16(rmsnorm(x[b]) * (1 + norm_w)))
+// out[b, :] = bf16(W . fp16(rmsnorm(x[b]) * (1 + norm_w))), W fp16
 template <int B, int KC, int D>
 __global__ void __launch_bounds__(kThreads) rmsnorm_gemv_kernel(const float* __restrict__ x, int64_t xs,
                                                                 const float* __restrict__ norm_w,
-                                                                const __nv_bfloat16* __restrict__ w, int64_t ws,
+                                                                const __half* __restrict__ w, int64_t ws,
                                                                 __nv_bfloat16* __restrict__ out, int64_t os, int n) {
   constexpr int k = KC * 256;
   extern __shared__ __align__(16) unsigned char smem[];
-  __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(smem);  // [B][k]
+  __half* h = reinterpret_cast<__half*>(smem);  // [B][k]
   __shared__ float red[kWarps];
   auto norm = [&]() {
     for (int b = 0; b < B; ++b) {  // the reduction order of rmsnorm_rows_kernel
@@ -108,14 +130,14 @@ __global__ void __launch_bounds__(kThreads) rmsnorm_gemv_kernel(const float* __r
         const float4 v = *reinterpret_cast<const float4*>(xr + i);
         const float4 ww = *reinterpret_cast<const float4*>(norm_w + i);
         uint2 pk;
-        pk.x = pack_bf16x2(v.x * r * (1.f + ww.x), v.y * r * (1.f + ww.y));
-        pk.y = pack_bf16x2(v.z * r * (1.f + ww.z), v.w * r * (1.f + ww.w));
+        pk.x = pack_f16x2(v.x * r * (1.f + ww.x), v.y * r * (1.f + ww.y));
+        pk.y = pack_f16x2(v.z * r * (1.f + ww.z), v.w * r * (1.f + ww.w));
         *reinterpret_cast<uint2*>(h + b * k + i) = pk;
       }
       __syncthreads();  // red is reused by the next row; h is complete
     }
   };
-  gemv_rows<B, KC, D>(w, ws, h, n, norm, [&](int row, const float (&acc)[B]) {
+  gemv_rows<__half, B, KC, D>(w, ws, h, n, norm, [&](int row, const float (&acc)[B]) {
     if ((threadIdx.x & 31) == 0)
 #pragma unroll
       for (int b = 0; b < B; ++b) out[b * os + row] = __float2bfloat16_rn(acc[b]);
@@ -138,7 +160,7 @@ __global__ void __launch_bounds__(kThreads) gemv_residual_kernel(const __nv_bflo
         *reinterpret_cast<uint4*>(xs + b * k + i) = *reinterpret_cast<const uint4*>(a + b * as + i);
     __syncthreads();
   };
-  gemv_rows<B, KC, D>(w, ws, xs, n, stage, [&](int row, const float (&acc)[B]) {
+  gemv_rows<__nv_bfloat16, B, KC, D>(w, ws, xs, n, stage, [&](int row, const float (&acc)[B]) {
     if ((threadIdx.x & 31) == 0)
 #pragma unroll
       for (int b = 0; b < B; ++b) out[b * os + row] = x0[b * x0s + row] + bf16_round(acc[b]);
@@ -170,7 +192,7 @@ Shape shape_for(int n, int kc) {
 }
 
 template <int B, int KC, int D>
-cudaError_t launch_rg(const float* x, int64_t xs, const float* nw, const __nv_bfloat16* w, int64_t ws,
+cudaError_t launch_rg(const float* x, int64_t xs, const float* nw, const __half* w, int64_t ws,
                       __nv_bfloat16* out, int64_t os, int n, int grid, cudaStream_t st) {
   const int smem = B * KC * 256 * 2;
   cudaError_t e =
@@ -219,7 +241,7 @@ extern "C" int ria_rmsnorm_gemv(const float* x, int64_t x_stride, const float* n
   if (x_stride % 4 || !ria::aligned(x, 16) || !ria::aligned(norm_weight, 16))
     return ria::fail(RIA_ERR_INVALID, "ria_rmsnorm_gemv: x rows must be 16-byte aligned");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const __nv_bfloat16* wb = static_cast<const __nv_bfloat16*>(w);
+  const __half* wb = static_cast<const __half*>(w);
   __nv_bfloat16* ob = static_cast<__nv_bfloat16*>(out);
   const int kc = k / 256;
   const Shape sh = shape_for(n, kc);

@@ -7,8 +7,9 @@ namespace {
 
 // One CTA per row; fp32 in, bf16 out; x * rsqrt(mean(x^2) + 1e-6) * (1 + w)
 // (router-ia qwen36_op_probe.py:55-67).
+template <bool F16>
 __global__ void __launch_bounds__(256) rmsnorm_rows_kernel(const float* __restrict__ x, int64_t xs,
-                                                           const float* __restrict__ w, __nv_bfloat16* __restrict__ out,
+                                                           const float* __restrict__ w, uint16_t* __restrict__ out,
                                                            int64_t os, int n) {
   __shared__ float red[8];
   pdl_wait();
@@ -25,13 +26,18 @@ __global__ void __launch_bounds__(256) rmsnorm_rows_kernel(const float* __restri
   float tot = 0.f;
   for (int i = 0; i < (int)(blockDim.x >> 5); ++i) tot += red[i];
   const float r = rsqrtf(tot / static_cast<float>(n) + 1e-6f);
-  __nv_bfloat16* o = out + row * os;
+  uint16_t* o = out + row * os;
   for (int i = threadIdx.x * 4; i < n; i += blockDim.x * 4) {
     const float4 v = *reinterpret_cast<const float4*>(xr + i);
     const float4 ww = *reinterpret_cast<const float4*>(w + i);
     uint2 pk;
-    pk.x = pack_bf16x2(v.x * r * (1.f + ww.x), v.y * r * (1.f + ww.y));
-    pk.y = pack_bf16x2(v.z * r * (1.f + ww.z), v.w * r * (1.f + ww.w));
+    if (F16) {
+      pk.x = pack_f16x2(v.x * r * (1.f + ww.x), v.y * r * (1.f + ww.y));
+      pk.y = pack_f16x2(v.z * r * (1.f + ww.z), v.w * r * (1.f + ww.w));
+    } else {
+      pk.x = pack_bf16x2(v.x * r * (1.f + ww.x), v.y * r * (1.f + ww.y));
+      pk.y = pack_bf16x2(v.z * r * (1.f + ww.z), v.w * r * (1.f + ww.w));
+    }
     *reinterpret_cast<uint2*>(o + i) = pk;
   }
 }
@@ -110,17 +116,33 @@ extern "C" int ria_advance_positions(int32_t* seq_lens, int32_t* positions, int3
   return ria::check_launch("ria_advance_positions");
 }
 
+namespace {
+
+template <bool F16>
+int rmsnorm_rows_impl(const char* what, const float* x, int64_t x_stride, const float* weight, void* out,
+                      int64_t out_stride, int32_t rows, int32_t n, ria_stream_t stream) {
+  if (rows < 0 || n <= 0 || n % 4 != 0) return ria::fail(RIA_ERR_INVALID, "%s: bad rows/n", what);
+  if (rows == 0) return RIA_OK;
+  if (!x || !weight || !out) return ria::fail(RIA_ERR_INVALID, "%s: null pointer", what);
+  if (!ria::aligned(x, 16) || !ria::aligned(weight, 16) || !ria::aligned(out, 8) || x_stride % 4 || out_stride % 4)
+    return ria::fail(RIA_ERR_INVALID, "%s: misaligned rows", what);
+  const cudaError_t e = ria::launch_pdl(rmsnorm_rows_kernel<F16>, dim3(rows), dim3(256), 0,
+                                       static_cast<cudaStream_t>(stream), x, x_stride, weight,
+                                       static_cast<uint16_t*>(out), out_stride, n);
+  if (e != cudaSuccess) return ria::fail(RIA_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return ria::check_launch(what);
+}
+
+}  // namespace
+
 extern "C" int ria_rmsnorm_rows(const float* x, int64_t x_stride, const float* weight, void* out, int64_t out_stride,
                                 int32_t rows, int32_t n, ria_stream_t stream) {
-  if (rows < 0 || n <= 0 || n % 4 != 0) return ria::fail(RIA_ERR_INVALID, "ria_rmsnorm_rows: bad rows/n");
-  if (rows == 0) return RIA_OK;
-  if (!x || !weight || !out) return ria::fail(RIA_ERR_INVALID, "ria_rmsnorm_rows: null pointer");
-  if (!ria::aligned(x, 16) || !ria::aligned(weight, 16) || !ria::aligned(out, 8) || x_stride % 4 || out_stride % 4)
-    return ria::fail(RIA_ERR_INVALID, "ria_rmsnorm_rows: misaligned rows");
-  const cudaError_t e = ria::launch_pdl(rmsnorm_rows_kernel, dim3(rows), dim3(256), 0, static_cast<cudaStream_t>(stream),
-                                       x, x_stride, weight, static_cast<__nv_bfloat16*>(out), out_stride, n);
-  if (e != cudaSuccess) return ria::fail(RIA_ERR_CUDA, "ria_rmsnorm_rows: %s", cudaGetErrorString(e));
-  return ria::check_launch("ria_rmsnorm_rows");
+  return rmsnorm_rows_impl<false>("ria_rmsnorm_rows", x, x_stride, weight, out, out_stride, rows, n, stream);
+}
+
+extern "C" int ria_rmsnorm_rows_f16(const float* x, int64_t x_stride, const float* weight, void* out,
+                                    int64_t out_stride, int32_t rows, int32_t n, ria_stream_t stream) {
+  return rmsnorm_rows_impl<true>("ria_rmsnorm_rows_f16", x, x_stride, weight, out, out_stride, rows, n, stream);
 }
 
 extern "C" int ria_residual_add(const float* x0, int64_t x0_stride, const void* proj, int64_t proj_stride, float* out,

@@ -113,11 +113,14 @@ _SIGNATURES: dict[str, tuple[object, list]] = {
     "ria_umma_selftest": (c_int, [c_int32, c_int32, c_int32, c_int32, c_void_p, c_void_p, c_void_p, c_void_p]),
     "ria_advance_positions": (c_int, [c_void_p, c_void_p, c_int32, c_void_p]),
     "ria_rmsnorm_rows": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int32, c_int32, c_void_p]),
+    "ria_rmsnorm_rows_f16": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int32, c_int32, c_void_p]),
     "ria_residual_add": (
         c_int, [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_int32, c_int32, c_void_p]),
     "ria_conv1d_step": (
         c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int64, c_int32, c_int32, c_void_p]),
     "ria_rope_apply": (c_int, [c_void_p, c_int32, c_int32, c_int32, c_void_p, c_int64, c_void_p]),
+    "ria_kv_append_paged": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_int32, c_void_p, c_void_p, c_int64,
+                                    c_void_p, c_int32, c_void_p, c_int32, c_int32, c_void_p]),
 }
 
 
@@ -354,8 +357,10 @@ GEMV_MAX_BATCH = 8
 
 
 def rmsnorm_gemv(x, norm_w, w, out):
-    """out [B, n] bf16 = w [n, k] . bf16(rmsnorm(x [B, k] f32) * (1 + norm_w)), B <= 8."""
+    """out [B, n] bf16 = w [n, k] fp16 . fp16(rmsnorm(x [B, k] f32) * (1 + norm_w)), B <= 8."""
     _require_cuda(x, norm_w, w, out)
+    if w.dtype != torch.float16 or out.dtype != torch.bfloat16:
+        raise ValueError(f"rmsnorm_gemv: fp16 weights and a bf16 output expected, got {w.dtype} / {out.dtype}")
     with _Hooked("rmsnorm_gemv"):
         rc = lib().ria_rmsnorm_gemv(x.data_ptr(), x.stride(0), norm_w.data_ptr(), w.data_ptr(), w.stride(0),
                                     out.data_ptr(), out.stride(0), x.shape[0], w.shape[0], w.shape[1], _stream(x))
@@ -460,11 +465,18 @@ def argmax_f16_rows(logits, out):
 
 
 def rmsnorm_rows(x, weight, out):
+    """out = rmsnorm(x) * (1 + weight) in out's dtype (bf16 or fp16)."""
     _require_cuda(x, weight, out)
+    if out.dtype == torch.float16:
+        fn, name = lib().ria_rmsnorm_rows_f16, "ria_rmsnorm_rows_f16"
+    elif out.dtype == torch.bfloat16:
+        fn, name = lib().ria_rmsnorm_rows, "ria_rmsnorm_rows"
+    else:
+        raise ValueError(f"rmsnorm_rows: output dtype {out.dtype} (bf16 or fp16)")
     with _Hooked("rmsnorm"):
-        rc = lib().ria_rmsnorm_rows(x.data_ptr(), x.stride(0), weight.data_ptr(), out.data_ptr(), out.stride(0),
-                                    x.shape[0], x.shape[1], _stream(x))
-    _check(rc, "ria_rmsnorm_rows")
+        rc = fn(x.data_ptr(), x.stride(0), weight.data_ptr(), out.data_ptr(), out.stride(0), x.shape[0], x.shape[1],
+                _stream(x))
+    _check(rc, name)
 
 
 def residual_add(x0, proj, out):
@@ -489,3 +501,17 @@ def rope_apply(x, inv_freq, rope_dim: int, position: int):
     with _Hooked("rope_apply"):
         rc = lib().ria_rope_apply(x.data_ptr(), rows, head_dim, rope_dim, inv_freq.data_ptr(), int(position), _stream(x))
     _check(rc, "ria_rope_apply")
+
+
+def kv_append_paged(k_new, v_new, k_pool, v_pool, block_table, seq_lens=None, seq_len0: int = 0):
+    """Write k_new[b], v_new[b] ([B, 512] bf16 or f32) at row seq_lens[b] of
+    sequence b's paged cache (see ria_kv_append_paged)."""
+    _require_cuda(k_new, v_new, k_pool, v_pool, block_table)
+    if k_new.dtype != v_new.dtype or k_new.dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError(f"kv_append_paged: bf16 or f32 K/V rows expected, got {k_new.dtype} / {v_new.dtype}")
+    with _Hooked("kv_append"):
+        rc = lib().ria_kv_append_paged(k_new.data_ptr(), k_new.stride(0), v_new.data_ptr(), v_new.stride(0),
+                                       1 if k_new.dtype == torch.float32 else 0, k_pool.data_ptr(), v_pool.data_ptr(),
+                                       k_pool.shape[1], block_table.data_ptr(), block_table.stride(0), _ptr(seq_lens),
+                                       int(seq_len0), k_new.shape[0], _stream(k_new))
+    _check(rc, "ria_kv_append_paged")

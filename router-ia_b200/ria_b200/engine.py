@@ -35,17 +35,29 @@ def _cdiv(a: int, b: int) -> int:
 
 
 def _in_projection(x: torch.Tensor, w: DeltaNetWeights | GqaWeights) -> torch.Tensor:
-    """bf16(rmsnorm(x) * (1 + w)) through the layer's fused in-projection: one
-    weight-streaming GEMV kernel with the norm fused for small batches, the
-    norm kernel plus a library GEMM otherwise."""
+    """bf16(W_in . fp16(rmsnorm(x) * (1 + w))) through the layer's fused fp16
+    in-projection: one weight-streaming GEMV kernel with the norm fused for
+    small batches, the norm kernel plus a library fp16 GEMM with fp32 output
+    otherwise (rounded once to bf16, the kernels' input type)."""
     batch = x.shape[0]
     if batch <= _ext.GEMV_MAX_BATCH:
         proj = torch.empty(batch, w.w_in.shape[0], dtype=torch.bfloat16, device=x.device)
         _ext.rmsnorm_gemv(x, w.in_norm, w.w_in, proj)
         return proj
-    h = torch.empty(batch, C.HIDDEN, dtype=torch.bfloat16, device=x.device)
+    return _norm_gemm(x, w)
+
+
+def _norm_gemm(x: torch.Tensor, w: DeltaNetWeights | GqaWeights) -> torch.Tensor:
+    """Rows x [N, 2048] fp32 -> bf16(W_in . fp16(rmsnorm(x) * (1 + w))) [N, n].
+
+    The library GEMM writes fp32 and the result is rounded to bf16 once: an
+    fp16 GEMM output rounded again to bf16 lands on bf16 ties in about one
+    element in sixteen (fp16 holds every bf16 midpoint) and moved the
+    DeltaNet conv input, which both paths round to bf16, by a bf16 step
+    there -- about 1e-2 on single tokens' attention output."""
+    h = torch.empty(x.shape[0], C.HIDDEN, dtype=torch.float16, device=x.device)
     _ext.rmsnorm_rows(x, w.in_norm, h)
-    return F.linear(h, w.w_in)
+    return torch.mm(h, w.w_in.t(), out_dtype=torch.float32).to(torch.bfloat16)
 
 
 def _out_projection(a: torch.Tensor, w: DeltaNetWeights | GqaWeights, x: torch.Tensor) -> torch.Tensor:
@@ -121,9 +133,7 @@ def deltanet_prefill(x: torch.Tensor, w: DeltaNetWeights, rec: torch.Tensor, con
     (K2) instead of token by token."""
     B, T, _ = x.shape
     xf = x.reshape(B * T, C.HIDDEN)
-    h = torch.empty(B * T, C.HIDDEN, dtype=torch.bfloat16, device=x.device)
-    _ext.rmsnorm_rows(xf, w.in_norm, h)
-    proj = F.linear(h, w.w_in)
+    proj = _norm_gemm(xf, w)
     mixed = proj.view(B, T, C.DN_PROJ_WIDTH)[:, :, C.DN_PROJ_QKV[0]:C.DN_PROJ_QKV[1]]
     y = torch.empty(B, T, C.LINEAR_CONV_DIM, dtype=torch.bfloat16, device=x.device)
     _ext.conv1d_prefill(mixed, conv, w.conv_w, y)
@@ -152,9 +162,7 @@ def gqa_prefill(x: torch.Tensor, w: GqaWeights, k_pool: torch.Tensor, v_pool: to
     at seq_lens[b] + t, RoPE at positions[b] + t."""
     B, T, _ = x.shape
     xf = x.reshape(B * T, C.HIDDEN)
-    h = torch.empty(B * T, C.HIDDEN, dtype=torch.bfloat16, device=x.device)
-    _ext.rmsnorm_rows(xf, w.in_norm, h)
-    proj = F.linear(h, w.w_in).view(B, T, C.GQA_PROJ_WIDTH)
+    proj = _norm_gemm(xf, w).view(B, T, C.GQA_PROJ_WIDTH)
     attn = torch.empty(B, T, C.FULL_Q_DIM, dtype=torch.bfloat16, device=x.device)
     workspace = _ext.gqa_prefill(proj[:, :, C.GQA_PROJ_Q[0]:C.GQA_PROJ_Q[1]], proj[:, :, C.GQA_PROJ_K[0]:C.GQA_PROJ_K[1]],
                                  proj[:, :, C.GQA_PROJ_V[0]:C.GQA_PROJ_V[1]], w.q_norm, w.k_norm, inv_freq, k_pool,

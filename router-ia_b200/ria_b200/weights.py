@@ -6,6 +6,13 @@ layers' attention weights resident (about 2.6 GB in bf16), so this module
 loads them once, fuses each layer's input projections into one matrix (one
 GEMM per layer instead of four / three) and converts the small vectors to fp32.
 
+The fused in-projection is kept in fp16 (checkpoint bf16 values convert
+exactly inside fp16's range), as router-ia's CUDA path keeps every projection
+(qwen36_cached_loop.py:552-557), so that the normalised layer input can enter
+it in fp16: a bf16 input (2^-9 rounding) moved single tokens' attention
+output by up to ~2e-2 against the fp32 CPU path, an fp16 one by ~6e-3.  The
+out-projections stay bf16 (their input, the attention output, is bf16).
+
 Sources: a dict of checkpoint tensors (``{suffix: tensor}``) or a checkpoint
 directory laid out like the reference expects (``model.safetensors.index.json``
 or ``*.safetensors`` with names ``model.language_model.layers.{L}.<suffix>``);
@@ -26,10 +33,19 @@ from . import constants as C
 FP8_BLOCK = 128
 
 
+def _fp16_projection(parts: list[torch.Tensor]) -> torch.Tensor:
+    """Row-concatenated projection matrices in fp16; raises if a weight lies
+    outside fp16's range."""
+    w = torch.cat([p.to(torch.float16) for p in parts], dim=0).contiguous()
+    if not bool(torch.isfinite(w).all()):
+        raise ValueError("projection weights exceed the fp16 range (|w| > 65504)")
+    return w
+
+
 @dataclass
 class DeltaNetWeights:
     in_norm: torch.Tensor  # [2048] f32, the (1+w) RMSNorm weight
-    w_in: torch.Tensor  # [12352, 2048] bf16 = [qkv | z | b | a]
+    w_in: torch.Tensor  # [12352, 2048] fp16 = [qkv | z | b | a]
     conv_w: torch.Tensor  # [8192, 4] bf16
     a_log: torch.Tensor  # [32] f32
     dt_bias: torch.Tensor  # [32] f32
@@ -40,21 +56,15 @@ class DeltaNetWeights:
     @classmethod
     def from_tensors(cls, t: dict[str, torch.Tensor], device) -> "DeltaNetWeights":
         bf = torch.bfloat16
-        w_in = torch.cat(
-            [
-                t["linear_attn.in_proj_qkv.weight"].to(bf),
-                t["linear_attn.in_proj_z.weight"].to(bf),
-                t["linear_attn.in_proj_b.weight"].to(bf),
-                t["linear_attn.in_proj_a.weight"].to(bf),
-            ],
-            dim=0,
-        )
+        w_in = _fp16_projection(
+            [t["linear_attn.in_proj_qkv.weight"], t["linear_attn.in_proj_z.weight"], t["linear_attn.in_proj_b.weight"],
+             t["linear_attn.in_proj_a.weight"]])
         conv = t["linear_attn.conv1d.weight"]
         if tuple(conv.shape) != (C.LINEAR_CONV_DIM, 1, C.LINEAR_CONV_KERNEL):
             raise ValueError(f"Unexpected conv weight shape: {tuple(conv.shape)}")
         return cls(
             in_norm=t["input_layernorm.weight"].float().contiguous().to(device),
-            w_in=w_in.contiguous().to(device),
+            w_in=w_in.to(device),
             conv_w=conv.reshape(C.LINEAR_CONV_DIM, C.LINEAR_CONV_KERNEL).to(bf).contiguous().to(device),
             a_log=t["linear_attn.A_log"].float().reshape(C.LINEAR_NUM_V_HEADS).contiguous().to(device),
             dt_bias=t["linear_attn.dt_bias"].float().reshape(C.LINEAR_NUM_V_HEADS).contiguous().to(device),
@@ -67,7 +77,7 @@ class DeltaNetWeights:
 @dataclass
 class GqaWeights:
     in_norm: torch.Tensor  # [2048] f32
-    w_in: torch.Tensor  # [9216, 2048] bf16 = [q_gate | k | v]
+    w_in: torch.Tensor  # [9216, 2048] fp16 = [q_gate | k | v]
     q_norm: torch.Tensor  # [256] f32
     k_norm: torch.Tensor  # [256] f32
     w_out: torch.Tensor  # [2048, 4096] bf16
@@ -75,14 +85,11 @@ class GqaWeights:
     @classmethod
     def from_tensors(cls, t: dict[str, torch.Tensor], device) -> "GqaWeights":
         bf = torch.bfloat16
-        w_in = torch.cat(
-            [t["self_attn.q_proj.weight"].to(bf), t["self_attn.k_proj.weight"].to(bf),
-             t["self_attn.v_proj.weight"].to(bf)],
-            dim=0,
-        )
+        w_in = _fp16_projection([t["self_attn.q_proj.weight"], t["self_attn.k_proj.weight"],
+                                 t["self_attn.v_proj.weight"]])
         return cls(
             in_norm=t["input_layernorm.weight"].float().contiguous().to(device),
-            w_in=w_in.contiguous().to(device),
+            w_in=w_in.to(device),
             q_norm=t["self_attn.q_norm.weight"].float().reshape(C.FULL_HEAD_DIM).contiguous().to(device),
             k_norm=t["self_attn.k_norm.weight"].float().reshape(C.FULL_HEAD_DIM).contiguous().to(device),
             w_out=t["self_attn.o_proj.weight"].to(bf).contiguous().to(device),

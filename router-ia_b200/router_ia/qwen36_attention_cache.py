@@ -471,8 +471,11 @@ def _append_full_kv(
     if paged:
         n = kv.length
         kv.ensure(n + 1)
-        kv.k[:, n].copy_(k_token.reshape(_C.FULL_NUM_KV_HEADS, _C.FULL_HEAD_DIM))
-        kv.v[:, n].copy_(v_token.reshape(_C.FULL_NUM_KV_HEADS, _C.FULL_HEAD_DIM))
+        row = _C.FULL_NUM_KV_HEADS * _C.FULL_HEAD_DIM
+        dt = torch.float32 if k_token.dtype == torch.float32 else torch.bfloat16
+        k_row = k_token.detach().to(device=kv.device, dtype=dt).reshape(1, row).contiguous()
+        v_row = v_token.detach().to(device=kv.device, dtype=dt).reshape(1, row).contiguous()
+        _ext.kv_append_paged(k_row, v_row, kv.k, kv.v, kv.table, seq_len0=n)
         kv.length = n + 1
         full_k, full_v = kv.views()
     elif full_k is None or full_v is None or full_k.device != k_token.device:

@@ -6,9 +6,10 @@ with in-kernel L2 norms).
 Tolerances (the bars of the attention path): outputs, stored in bf16, within
 1e-2 relative RMS and 2e-2 in the scale-aware max form (max |d| / max(1,
 |ref|)); the final fp32 state within 1e-3 relative RMS of the float64
-recurrence.  The kernel's tensor-core operands are bf16 q/k for the Gram
-product and fp16 for everything else (fp32 accumulation, fp32 state), which
-puts the state about 4e-4 from the recurrence on these inputs.
+recurrence.  The kernel runs the products that feed the state on fp16
+operands and the rest on bf16 (fp32 accumulation, fp32 state), which puts the
+state about 4e-4 and the outputs about 2.4e-3 from the recurrence on these
+inputs.
 
 Configuration 2 (8 sequences x 8192 tokens, 16 key / 32 value heads) runs at
 full size; four seeded (sequence, value head) pairs, the two value heads of
