@@ -162,10 +162,27 @@ class AttentionState:
 
 _STATES: dict[Path, AttentionState] = {}
 _ACTIVE_STATES: dict[Path, AttentionState] = {}
+_ROOT_KEYS: dict = {}
+
+
+def _rkey(root) -> Path:
+    """``Path(root).resolve()``, the registry key, memoised per root object:
+    resolving touches the filesystem (about 15 us), and step_attention needs
+    the key three times per layer.  A root's resolution is fixed for the life
+    of the process."""
+    try:
+        return _ROOT_KEYS[root]
+    except (KeyError, TypeError):
+        key = Path(root).resolve()
+        try:
+            _ROOT_KEYS[root] = key
+        except TypeError:
+            pass
+        return key
 
 
 def state_for(root: Path, device: str) -> AttentionState:
-    key = Path(root).resolve()
+    key = _rkey(root)
     state = _STATES.get(key)
     if state is None:
         state = AttentionState()
@@ -175,7 +192,7 @@ def state_for(root: Path, device: str) -> AttentionState:
 
 
 def reset(root: Path) -> AttentionState:
-    key = Path(root).resolve()
+    key = _rkey(root)
     state = _STATES.get(key)
     if state is None:
         state = AttentionState()
@@ -185,15 +202,15 @@ def reset(root: Path) -> AttentionState:
 
 
 def activate(root: Path, state: AttentionState) -> None:
-    _ACTIVE_STATES[Path(root).resolve()] = state
+    _ACTIVE_STATES[_rkey(root)] = state
 
 
 def deactivate(root: Path) -> None:
-    _ACTIVE_STATES.pop(Path(root).resolve(), None)
+    _ACTIVE_STATES.pop(_rkey(root), None)
 
 
 def active(root: Path, device: str) -> AttentionState:
-    key = Path(root).resolve()
+    key = _rkey(root)
     state = _ACTIVE_STATES.get(key)
     if state is None:
         state = state_for(key, device)
@@ -213,7 +230,7 @@ _INV_FREQ: dict[str, torch.Tensor] = {}
 def register_layer_weights(root: Path, layer: int, tensors: dict[str, torch.Tensor]) -> None:
     """Provide one layer's tensors (``{suffix: tensor}`` as in the checkpoint)
     without a checkpoint on disk, e.g. seeded synthetic weights."""
-    key = (Path(root).resolve(), int(layer))
+    key = (_rkey(root), int(layer))
     _REGISTERED[key] = dict(tensors)
     _KINDS.pop(key, None)
     for dkey in [k for k in _DEVICE_WEIGHTS if k[:2] == key]:
@@ -221,7 +238,7 @@ def register_layer_weights(root: Path, layer: int, tensors: dict[str, torch.Tens
 
 
 def _reader(root: Path) -> CheckpointReader:
-    key = Path(root).resolve()
+    key = _rkey(root)
     reader = _READERS.get(key)
     if reader is None:
         reader = CheckpointReader(key)
@@ -232,7 +249,7 @@ def _reader(root: Path) -> CheckpointReader:
 def attention_type(root: Path, layer: int) -> str:
     """``linear_attention`` or ``full_attention``, memoised per (root, layer)
     (qwen36_40layer_loop.py:68-78)."""
-    key = (Path(root).resolve(), int(layer))
+    key = (_rkey(root), int(layer))
     kind = _KINDS.get(key)
     if kind is None:
         tensors = _REGISTERED.get(key)
@@ -250,7 +267,7 @@ def attention_type(root: Path, layer: int) -> str:
 
 
 def _device_weights(root: Path, layer: int, device) -> DeltaNetWeights | GqaWeights:
-    rkey = Path(root).resolve()
+    rkey = _rkey(root)
     dev = torch.device(device)
     key = (rkey, int(layer), str(dev))
     w = _DEVICE_WEIGHTS.get(key)
@@ -268,7 +285,7 @@ def _device_weights(root: Path, layer: int, device) -> DeltaNetWeights | GqaWeig
 
 def _projection(root: Path, prefix: str, device: str) -> torch.Tensor:
     """Projection weight ``prefix + '.weight'`` as a bf16 device tensor."""
-    rkey = Path(root).resolve()
+    rkey = _rkey(root)
     name = prefix + ".weight"
     for (r, layer), tensors in _REGISTERED.items():
         lp = _C.layer_prefix(layer)
@@ -496,7 +513,7 @@ def step_attention(root: Path, layer: int, x0: torch.Tensor, device: str) -> tor
 
 
 def stats(root: Path) -> dict[str, int | float]:
-    state = _STATES.get(Path(root).resolve())
+    state = _STATES.get(_rkey(root))
     return (
         state.snapshot()
         if state is not None
