@@ -51,3 +51,25 @@ def test_errors_map_to_python_exceptions():
         _ext._check(2, "x")
     _ext._check(0, "x")
     assert isinstance(_ext.lib(), ctypes.CDLL)
+
+
+def test_new_entry_points_reject_bad_arguments_on_the_host():
+    lib = _ext.lib()
+    # kv append: null pointers, NULL seq_lens with batch > 1, a scalar length past the block table
+    assert lib.ria_kv_append_paged(None, 512, None, 512, 0, None, None, 64, None, 1, None, 0, 2, None) == \
+        _ext.RIA_ERR_INVALID
+    buf = ctypes.create_string_buffer(4096)
+    p = ctypes.addressof(buf) // 256 * 256 + 256 if ctypes.addressof(buf) % 256 else ctypes.addressof(buf)
+    assert lib.ria_kv_append_paged(p, 512, p, 512, 0, p, p, 64, p, 1, None, 0, 2, None) == _ext.RIA_ERR_INVALID
+    assert "batch 1" in _ext.last_error()
+    assert lib.ria_kv_append_paged(p, 512, p, 512, 0, p, p, 64, p, 1, None, 64, 1, None) == _ext.RIA_ERR_INVALID
+    assert "block table" in _ext.last_error()
+    assert lib.ria_kv_append_paged(p, 100, p, 512, 0, p, p, 64, p, 1, None, 0, 1, None) == _ext.RIA_ERR_INVALID
+    assert lib.ria_kv_append_paged(None, 0, None, 0, 0, None, None, 0, None, 0, None, 0, 0, None) == 0  # empty batch
+    # fp16 norm: bad sizes
+    assert lib.ria_rmsnorm_rows_f16(None, 0, None, None, 0, 1, 3, None) == _ext.RIA_ERR_INVALID
+    # GQA decode with scalar lengths: a split plan covering fewer pages than the sequence needs
+    args = [p, 8192, p, 512, p, 512, p, p, p, p, p, 64 * 64, p, 64, None, None, 1000, 1000, p, 4096, p, 1 << 20,
+            1, 2, 3, None]
+    assert lib.ria_gqa_decode_paged(*args) == _ext.RIA_ERR_INVALID
+    assert "pages" in _ext.last_error()

@@ -101,3 +101,25 @@ def test_balanced_assignment_equal_counts_and_loads():
 def test_balanced_assignment_rejects_uneven_split():
     with pytest.raises(ValueError):
         balanced_assignment([1, 2, 3], 2)
+
+
+def test_benchmark_workload_splits():
+    """bench.py's configuration-3 request lists: weak scaling gives every rank
+    the same multiset of 256 KV lengths; strong scaling splits the one-GPU
+    job of 256 sequences into disjoint, equal-count shards whose summed KV
+    lengths are within one request's length of each other."""
+    import argparse
+
+    import bench
+    from ria_b200 import synthetic
+
+    args = argparse.Namespace(batch=256, len_lo=512, len_hi=32768)
+    job = synthetic.stratified_lengths(256, 512, 32768, seed=0)
+    for world in (1, 2, 4, 8):
+        weak = [bench.weak_lengths(args, r, world) for r in range(world)]
+        assert all(sorted(w) == sorted(job) for w in weak)
+        strong = [bench.strong_lengths(args, r, world) for r in range(world)]
+        assert all(len(s) == 256 // world for s in strong)
+        assert sorted(x for s in strong for x in s) == sorted(job)
+        sums = [sum(s) for s in strong]
+        assert max(sums) - min(sums) <= max(job)
