@@ -6,6 +6,7 @@
     python router-ia_b200/ria_b200/profile_cases.py --kernel head --batch 8 --iters 3
     python router-ia_b200/ria_b200/profile_cases.py --kernel model_step --batch 64
     python router-ia_b200/ria_b200/profile_cases.py --kernel model_prefill --batch 64 --seq 2048
+    python router-ia_b200/ria_b200/profile_cases.py --kernel stack --batch 1 --len 4096
 
 Each case allocates only one layer's state (about 1 GB), so a multi-pass
 ``ncu`` capture of one launch stays small, while one launch still moves more
@@ -201,6 +202,43 @@ def model_prefill_case(batch: int, seq: int, device) -> dict:
     return {"kernel": "model_prefill", "batch": batch, "seq": seq, "ms": s.elapsed_time(e)}
 
 
+def stack_case(batch: int, length: int, iters: int, device) -> dict:
+    """The 40-layer decode step without MoE (30 DeltaNet + 10 GQA layers,
+    ``length`` cached tokens per sequence on every GQA layer): mean eager and
+    CUDA-graph-replay times per token, then one eager step in the NVTX range
+    ``stack_step`` (for ``ncu --nvtx --nvtx-include``)."""
+    from ria_b200.engine import BatchedAttentionState, DecodeGraph
+
+    layers = {}
+    for layer in range(C.NUM_LAYERS):
+        t = synthetic.layer_weights_on_device(layer, device, seed=0)
+        cls = GqaWeights if C.is_full_attention_layer(layer) else DeltaNetWeights
+        layers[layer] = cls.from_tensors(t, device)
+        del t
+    nb = (length + 2 * iters + 128) // C.KV_BLOCK + 2
+    eng = BatchedAttentionState(layers, batch=batch, pool_blocks=nb * batch, max_blocks_per_seq=nb, device=device)
+    g = torch.Generator(device=device)
+    g.manual_seed(7)
+    for layer in eng.rec:
+        eng.rec[layer].normal_(0.0, 0.1, generator=g)
+    for layer in eng.k_pool:
+        eng.k_pool[layer].normal_(0.0, 1.0, generator=g)
+        eng.v_pool[layer].normal_(0.0, 1.0, generator=g)
+    for i in range(batch):
+        eng.set_length(i, length)
+    eng.sync_tables()
+    x = torch.randn(batch, C.HIDDEN, device=device, generator=g)
+    eager_ms = _time(lambda: eng.step(x), iters, device)
+    graph = DecodeGraph(eng)
+    graph_ms = _time(lambda: graph.step(x), iters, device)
+    del graph
+    torch.cuda.nvtx.range_push("stack_step")
+    eng.step(x)
+    torch.cuda.synchronize(device)
+    torch.cuda.nvtx.range_pop()
+    return {"kernel": "stack", "batch": batch, "len": length, "eager_ms": eager_ms, "graph_ms": graph_ms}
+
+
 def _time(fn, iters, device):
     for _ in range(3):
         fn()
@@ -217,7 +255,7 @@ def _time(fn, iters, device):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--kernel", choices=("gdn", "gqa", "prefill", "gqa_prefill", "moe", "head", "model_step",
-                                         "model_prefill", "all"),
+                                         "model_prefill", "stack", "all"),
                     default="all")
     ap.add_argument("--seq", type=int, default=8192)
     ap.add_argument("--batch", type=int, default=64)
@@ -243,6 +281,8 @@ def main():
         print(model_step_case(args.batch, dev), flush=True)
     if args.kernel == "model_prefill":
         print(model_prefill_case(args.batch, args.seq, dev), flush=True)
+    if args.kernel == "stack":
+        print(stack_case(args.batch, args.len, args.iters, dev), flush=True)
     if _ext.device_error():
         raise SystemExit("device error word set")
 
