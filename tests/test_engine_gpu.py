@@ -6,7 +6,9 @@ oracle on the same input (the GPU's own output of the layer below), at the
 per-layer bound -- 2e-2 max-abs, 1e-2 relative RMS on the fp32 residual;
 (2) ``BatchedAttentionState.step`` equal, bit for bit, to the same layers run
 one at a time.  Checking each layer on its own input keeps the bound that of
-one layer: compared end to end, the bf16 roundings of 8 layers compound."""
+one layer: compared end to end, the bf16 roundings of 8 layers compound.
+Five sequences run the projections as the fused GEMVs, twenty-four as the
+norm kernel plus library GEMMs."""
 
 from __future__ import annotations
 
@@ -22,17 +24,19 @@ from ria_b200.weights import DeltaNetWeights, GqaWeights
 pytestmark = pytest.mark.gpu
 
 
-def test_ragged_hybrid_stack_matches_per_sequence_oracle(cuda_device):
+RAGGED_24 = [0, 1, 63, 64, 65, 127, 128, 129, 200, 255, 256, 257] + [(37 * i) % 300 for i in range(1, 13)]
+
+
+@pytest.mark.parametrize("lengths,steps", [([0, 5, 64, 130, 257], 3), (RAGGED_24, 2)])
+def test_ragged_hybrid_stack_matches_per_sequence_oracle(cuda_device, lengths, steps):
     from ria_b200.engine import deltanet_decode, gqa_decode
 
     layers = [0, 1, 2, 3, 4, 5, 6, 7]  # DN DN DN GQA DN DN DN GQA
     wt = {layer: synthetic.layer_weights(layer, 3) for layer in layers}
     dev_w = {layer: (GqaWeights if C.is_full_attention_layer(layer) else DeltaNetWeights).from_tensors(w, cuda_device)
              for layer, w in wt.items()}
-    lengths = [0, 5, 64, 130, 257]
     B = len(lengths)
-    steps = 3
-    engines = [BatchedAttentionState(dev_w, batch=B, pool_blocks=40, max_blocks_per_seq=8, device=cuda_device)
+    engines = [BatchedAttentionState(dev_w, batch=B, pool_blocks=8 * B, max_blocks_per_seq=8, device=cuda_device)
                for _ in range(2)]
     eng, twin = engines
     gen = torch.Generator().manual_seed(5)
