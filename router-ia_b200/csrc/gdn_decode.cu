@@ -28,6 +28,14 @@
 //   * The next unit's conv state, conv weights, projections and gates are
 //     loaded into registers one unit ahead, so the per-unit prologue never waits
 //     on global memory.  Two barriers per tile, two per unit.
+//   * Small batches (16 key-head units per sequence leave SMs idle) use one
+//     unit per (sequence, value head) instead: twice the CTAs, each with one
+//     tile's chain; the two value heads of a key head both compute its q / k
+//     conv and norms (the even one writes its conv state) and each writes the
+//     conv state of its own v channels.  The two are one 2-CTA cluster, and a
+//     cluster barrier separates both CTAs' reads of a unit's conv state from
+//     its write.  The per-tile arithmetic is the same in both forms, so their
+//     results are bit-identical.
 #include <algorithm>
 #include <mutex>
 
@@ -69,6 +77,7 @@ struct GdnParams {
   int64_t out_stride;
   int batch;
   int num_slots;
+  int per_vhead;  // units are (sequence, value head) instead of (sequence, key head)
   unsigned int* err;
 };
 
@@ -140,10 +149,15 @@ __global__ void __launch_bounds__(kThreads, 2) gdn_decode_kernel(const GdnParams
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
-  const int units = p.batch * kHk;
+  const int nt = p.per_vhead ? 1 : 2;  // tiles (value heads) per unit
+  const int units = p.batch * kHk * (p.per_vhead ? 2 : 1);
   if (static_cast<int>(blockIdx.x) >= units) return;
   const int my_units = (units - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1;
-  const int my_halves = 4 * my_units;  // 2 tiles x 2 halves per unit
+  const int my_halves = 2 * nt * my_units;  // nt tiles x 2 halves per unit
+  // unit -> sequence, key head, first value head offset (0 or 1) within the key head
+  auto unit_b = [&](int u) { return p.per_vhead ? u / (2 * kHk) : u / kHk; };
+  auto unit_j = [&](int u) { return p.per_vhead ? (u % (2 * kHk)) >> 1 : u % kHk; };
+  auto unit_t0 = [&](int u) { return p.per_vhead ? u & 1 : 0; };
 
   auto unit_of = [&](int ui) { return static_cast<int>(blockIdx.x) + ui * static_cast<int>(gridDim.x); };
   // Out-of-range slots read slot 0 (always mapped) and skip every write; the
@@ -156,9 +170,9 @@ __global__ void __launch_bounds__(kThreads, 2) gdn_decode_kernel(const GdnParams
 
   // Producer (warp 0): half tile jh -> ring slot jh % kSlots.
   auto issue = [&](int jh) {
-    const int u = unit_of(jh >> 2);
-    const int b = u / kHk;
-    const int h = 2 * (u % kHk) + ((jh >> 1) & 1);
+    const int u = unit_of(jh / (2 * nt));
+    const int b = unit_b(u);
+    const int h = 2 * unit_j(u) + unit_t0(u) + ((jh >> 1) % nt);
     const int s = jh % kSlots;
     const float* src = p.rec_state + (static_cast<int64_t>(slot_of(b)) * kHv + h) * kTileFloats + (jh & 1) * kHalfFloats;
     if (lane == 0) mbar_arrive_expect_tx(&full[s], kHalfBytes);
@@ -172,8 +186,8 @@ __global__ void __launch_bounds__(kThreads, 2) gdn_decode_kernel(const GdnParams
   // Channels owned by this thread inside a unit: one of q/k, one of v.
   auto load_prefetch = [&](int ui, Prefetch& pf) {
     const int u = unit_of(ui);
-    const int b = u / kHk;
-    const int j = u % kHk;
+    const int b = unit_b(u);
+    const int j = unit_j(u);
     const int slot = slot_of(b);
     const int ch_qk = (tid < 128) ? (j * kD + tid) : (kKeyDim + j * kD + (tid - 128));
     const int ch_v = 2 * kKeyDim + j * 2 * kD + tid;
@@ -217,20 +231,30 @@ __global__ void __launch_bounds__(kThreads, 2) gdn_decode_kernel(const GdnParams
 
   for (int ui = 0; ui < my_units; ++ui) {
     const int u = unit_of(ui);
-    const int b = u / kHk;
-    const int j = u % kHk;
+    const int b = unit_b(u);
+    const int j = unit_j(u);
+    const int t0 = unit_t0(u);
     const int slot = slot_of(b);
     const int rs = raw_slot(b);
     const bool wr = rs >= 0 && rs < p.num_slots;
+    // conv-state writes: q / k channels by the even value head's unit, v
+    // channels (threads 0-127: head 2j, 128-255: head 2j + 1) by their head's
+    const bool wr_qk = wr && t0 == 0;
+    const bool wr_v = wr && (!p.per_vhead || (tid >> 7) == t0);
 
     // ---- unit prologue from the prefetched registers
+    if (p.per_vhead) {
+      // both value heads' CTAs have read this unit's conv state (the loads
+      // ordered before the release) before the even one overwrites it
+      asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+    }
     __syncthreads();  // previous unit's readers of qs/ks/vs/scal are done
     {
       __nv_bfloat16* cs = p.conv_state + static_cast<int64_t>(slot) * kConvDim * 4;
       const int ch_qk = (tid < 128) ? (j * kD + tid) : (kKeyDim + j * kD + (tid - 128));
       const int ch_v = 2 * kKeyDim + j * 2 * kD + tid;
-      const float yqk = conv_silu(pf.st_qk, pf.w_qk, pf.x_qk, cs + ch_qk * 4, wr);
-      const float yv = conv_silu(pf.st_v, pf.w_v, pf.x_v, cs + ch_v * 4, wr);
+      const float yqk = conv_silu(pf.st_qk, pf.w_qk, pf.x_qk, cs + ch_qk * 4, wr_qk);
+      const float yv = conv_silu(pf.st_v, pf.w_v, pf.x_v, cs + ch_v * 4, wr_v);
       vs[tid] = yv;
       if (tid < 128) qs[tid] = yqk; else ks[tid - 128] = yqk;
       if (tid < 2) {
@@ -255,8 +279,9 @@ __global__ void __launch_bounds__(kThreads, 2) gdn_decode_kernel(const GdnParams
       }
     }
 
-    for (int t = 0; t < 2; ++t) {
-      const int n = 2 * ui + t;
+    for (int tt = 0; tt < nt; ++tt) {
+      const int t = t0 + tt;  // value head 2j + t
+      const int n = nt * ui + tt;
       const int h = 2 * j + t;
       const int jh = 2 * n + half;
       const int s = jh % kSlots;
@@ -405,10 +430,25 @@ extern "C" int ria_gdn_decode_step(const void* mixed, int64_t mixed_stride, cons
       attr_set[dev] = true;
     }
   }
-  const int units = batch * kHk;
-  const int grid = std::min(units, 2 * ria::num_sms());
-  const cudaError_t le = ria::launch_pdl(gdn_decode_kernel, grid, dim3(kThreads), kSmemBytes,
-                                        static_cast<cudaStream_t>(stream), p);
+  // value-head units when the key-head units would leave SMs idle
+  p.per_vhead = batch * kHk < ria::num_sms() ? 1 : 0;
+  const int units = batch * kHk * (p.per_vhead ? 2 : 1);
+  const int grid = std::min(units, 2 * ria::num_sms());  // even in the value-head form (units = 32 x batch)
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = p.per_vhead ? 2 : 1;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  const cudaError_t le = cudaLaunchKernelEx(&cfg, gdn_decode_kernel, p);
   if (le != cudaSuccess) return ria::fail(RIA_ERR_CUDA, "ria_gdn_decode_step: %s", cudaGetErrorString(le));
   return ria::check_launch("ria_gdn_decode_step");
 }
