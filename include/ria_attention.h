@@ -296,6 +296,36 @@ RIA_API int ria_gemv_residual(const void* a, int64_t a_stride, const void* w, in
                               int64_t x0_stride, float* out, int64_t out_stride, int32_t batch, int32_t n, int32_t k,
                               ria_stream_t stream);
 
+/* Whole decode layer steps for batch <= 8 in one call: the launches a
+ * DeltaNet or GQA layer makes through ria_rmsnorm_gemv, ria_gdn_decode_step /
+ * ria_gqa_decode_paged and ria_gemv_residual, issued back to back from C with
+ * the intermediates in `scratch` (identical results).  For callers that step
+ * one layer per call from an interpreter, as router-ia's run_forward_token
+ * does through step_attention (qwen36_chat_batch.py:181-207;
+ * qwen36_attention_cache.py:224-324 for the layer bodies): the host work of
+ * three or four separate foreign calls per layer exceeds a batch-1 layer's
+ * GPU time.  x [batch, 2048] f32 is the layer input and out [batch, 2048] f32
+ * its residual output (out may not alias x); weights, state and cache
+ * arguments are those of the separate entry points (w_in fp16 [n_in, 2048],
+ * w_out bf16 [2048, 4096]).  scratch: at least the *_scratch_bytes bytes,
+ * 256-byte aligned, not shared by calls that overlap on the GPU. */
+RIA_API int64_t ria_deltanet_layer_decode_scratch_bytes(int32_t batch);
+RIA_API int ria_deltanet_layer_decode(const float* x, int64_t x_stride, const float* in_norm, const void* w_in,
+                                      int64_t w_in_stride, const void* conv_weight, const float* a_log,
+                                      const float* dt_bias, const float* norm_weight, const void* w_out,
+                                      int64_t w_out_stride, void* conv_state, float* rec_state, const int32_t* slots,
+                                      int32_t num_slots, float* out, int64_t out_stride, void* scratch,
+                                      int64_t scratch_bytes, int32_t batch, ria_stream_t stream);
+RIA_API int64_t ria_gqa_layer_decode_scratch_bytes(int32_t batch, int32_t max_splits);
+RIA_API int ria_gqa_layer_decode(const float* x, int64_t x_stride, const float* in_norm, const void* w_in,
+                                 int64_t w_in_stride, const float* q_norm_weight, const float* k_norm_weight,
+                                 const float* inv_freq, void* k_pool, void* v_pool, int64_t pool_tokens,
+                                 const int32_t* block_table, int32_t block_table_stride, const int32_t* seq_lens,
+                                 const int32_t* positions, int32_t seq_len0, int32_t position0, const void* w_out,
+                                 int64_t w_out_stride, float* out, int64_t out_stride, void* scratch,
+                                 int64_t scratch_bytes, int32_t batch, int32_t split_pages, int32_t max_splits,
+                                 ria_stream_t stream);
+
 /* out[B, n] f32 = x0[B, n] f32 + proj[B, n] bf16: the residual add that ends
  * _linear_stateful / _full_stateful (qwen36_attention_cache.py:276-277, 320-321). */
 RIA_API int ria_residual_add(const float* x0, int64_t x0_stride, const void* proj, int64_t proj_stride, float* out,

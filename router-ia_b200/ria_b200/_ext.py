@@ -71,6 +71,16 @@ _SIGNATURES: dict[str, tuple[object, list]] = {
     "ria_gemv_residual": (
         c_int, [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_int32, c_int32, c_int32,
                 c_void_p]),
+    "ria_deltanet_layer_decode_scratch_bytes": (c_int64, [c_int32]),
+    "ria_deltanet_layer_decode": (
+        c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                c_int64, c_void_p, c_void_p, c_void_p, c_int32, c_void_p, c_int64, c_void_p, c_int64, c_int32,
+                c_void_p]),
+    "ria_gqa_layer_decode_scratch_bytes": (c_int64, [c_int32, c_int32]),
+    "ria_gqa_layer_decode": (
+        c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                c_int64, c_void_p, c_int32, c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_int64, c_void_p,
+                c_int64, c_void_p, c_int64, c_int32, c_int32, c_int32, c_void_p]),
     "ria_moe_workspace_bytes": (c_int64, [c_int32, c_int32, c_int32]),
     "ria_moe_decode": (
         c_int,
@@ -377,6 +387,68 @@ def gemv_residual(a, w, x0, out):
         rc = lib().ria_gemv_residual(a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), x0.data_ptr(), x0.stride(0),
                                      out.data_ptr(), out.stride(0), a.shape[0], w.shape[0], w.shape[1], _stream(a))
     _check(rc, "ria_gemv_residual")
+
+
+def deltanet_layer_scratch_bytes(batch: int) -> int:
+    return int(lib().ria_deltanet_layer_decode_scratch_bytes(batch))
+
+
+def gqa_layer_scratch_bytes(batch: int, max_splits: int) -> int:
+    return int(lib().ria_gqa_layer_decode_scratch_bytes(batch, max_splits))
+
+
+def deltanet_layer_args(w) -> tuple:
+    """The weight arguments of ria_deltanet_layer_decode for one layer's
+    DeltaNetWeights (device pointers and strides; valid while ``w`` lives)."""
+    _require_cuda(w.in_norm, w.w_in, w.conv_w, w.a_log, w.dt_bias, w.norm_w, w.w_out)
+    return (w.in_norm.data_ptr(), w.w_in.data_ptr(), w.w_in.stride(0), w.conv_w.data_ptr(), w.a_log.data_ptr(),
+            w.dt_bias.data_ptr(), w.norm_w.data_ptr(), w.w_out.data_ptr(), w.w_out.stride(0))
+
+
+def gqa_layer_args(w) -> tuple:
+    """The weight arguments of ria_gqa_layer_decode for one layer's GqaWeights."""
+    _require_cuda(w.in_norm, w.w_in, w.q_norm, w.k_norm, w.w_out)
+    return (w.in_norm.data_ptr(), w.w_in.data_ptr(), w.w_in.stride(0), w.q_norm.data_ptr(), w.k_norm.data_ptr(),
+            w.w_out.data_ptr(), w.w_out.stride(0))
+
+
+def deltanet_layer_decode(x, wargs, conv_state, rec_state, out, scratch, slots=None):
+    """One DeltaNet layer step for x [B <= 8, 2048] f32 in one C call
+    (ria_deltanet_layer_decode): out = the layer's residual output."""
+    if not (x.is_cuda and out.is_cuda and scratch.is_cuda):
+        raise RuntimeError("router-ia B200 kernels need CUDA tensors (no CPU fallback)")
+    in_norm, w_in, w_in_s, conv_w, a_log, dt_bias, norm_w, w_out, w_out_s = wargs
+    args = (x.data_ptr(), x.stride(0), in_norm, w_in, w_in_s, conv_w, a_log, dt_bias, norm_w, w_out, w_out_s,
+            conv_state.data_ptr(), rec_state.data_ptr(), _ptr(slots), rec_state.shape[0], out.data_ptr(),
+            out.stride(0), scratch.data_ptr(), scratch.numel() * scratch.element_size(), x.shape[0], _stream(x))
+    if launch_hook is None:
+        rc = lib().ria_deltanet_layer_decode(*args)
+    else:
+        with _Hooked("deltanet_layer", 3):
+            rc = lib().ria_deltanet_layer_decode(*args)
+    if rc:
+        _check(rc, "ria_deltanet_layer_decode")
+
+
+def gqa_layer_decode(x, wargs, inv_freq, k_pool, v_pool, block_table, out, scratch, split_pages, max_splits,
+                     seq_lens=None, positions=None, seq_len0=0, position0=0):
+    """One GQA layer step for x [B <= 8, 2048] f32 in one C call
+    (ria_gqa_layer_decode): out = the layer's residual output."""
+    if not (x.is_cuda and out.is_cuda and scratch.is_cuda and k_pool.is_cuda):
+        raise RuntimeError("router-ia B200 kernels need CUDA tensors (no CPU fallback)")
+    in_norm, w_in, w_in_s, q_norm, k_norm, w_out, w_out_s = wargs
+    args = (x.data_ptr(), x.stride(0), in_norm, w_in, w_in_s, q_norm, k_norm, inv_freq.data_ptr(), k_pool.data_ptr(),
+            v_pool.data_ptr(), k_pool.shape[1], block_table.data_ptr(), block_table.stride(0), _ptr(seq_lens),
+            _ptr(positions), int(seq_len0), int(position0), w_out, w_out_s, out.data_ptr(), out.stride(0),
+            scratch.data_ptr(), scratch.numel() * scratch.element_size(), x.shape[0], int(split_pages),
+            int(max_splits), _stream(x))
+    if launch_hook is None:
+        rc = lib().ria_gqa_layer_decode(*args)
+    else:
+        with _Hooked("gqa_layer", 4 if int(max_splits) > 1 else 3):
+            rc = lib().ria_gqa_layer_decode(*args)
+    if rc:
+        _check(rc, "ria_gqa_layer_decode")
 
 
 def moe_workspace_bytes(batch: int, num_experts: int, top_k: int) -> int:

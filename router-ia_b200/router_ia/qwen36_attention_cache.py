@@ -33,7 +33,6 @@ if str(_SRC_ROOT) not in sys.path:
 
 from ria_b200 import _ext  # noqa: E402
 from ria_b200 import constants as _C  # noqa: E402
-from ria_b200.engine import GqaLaunch, deltanet_decode, gqa_decode, plan_gqa_split  # noqa: E402
 from ria_b200.weights import CheckpointReader, DeltaNetWeights, GqaWeights, rope_inv_freq  # noqa: E402
 
 ROPE_THETA = 10_000_000.0
@@ -110,7 +109,6 @@ class AttentionState:
     tokens_seen: int = 0
     device: str | None = None
     _paged: dict[int, _PagedKV] = field(default_factory=dict, repr=False, compare=False)
-    _workspace: torch.Tensor | None = field(default=None, repr=False, compare=False)
 
     def reset(self) -> None:
         self.full_keys.clear()
@@ -223,6 +221,11 @@ def active(root: Path, device: str) -> AttentionState:
 _REGISTERED: dict[tuple[Path, int], dict[str, torch.Tensor]] = {}
 _READERS: dict[Path, CheckpointReader] = {}
 _DEVICE_WEIGHTS: dict[tuple[Path, int, str], DeltaNetWeights | GqaWeights] = {}
+# The same layers' weight arguments for the one-call layer steps (device
+# pointers and strides): one foreign call per layer instead of three or four
+# -- router-ia calls step_attention once per layer, and the host work of the
+# separate calls exceeded a batch-1 layer's GPU time.
+_LAYER_ARGS: dict[tuple[Path, int, str], tuple] = {}
 _KINDS: dict[tuple[Path, int], str] = {}
 _INV_FREQ: dict[str, torch.Tensor] = {}
 
@@ -235,6 +238,7 @@ def register_layer_weights(root: Path, layer: int, tensors: dict[str, torch.Tens
     _KINDS.pop(key, None)
     for dkey in [k for k in _DEVICE_WEIGHTS if k[:2] == key]:
         del _DEVICE_WEIGHTS[dkey]
+        _LAYER_ARGS.pop(dkey, None)
 
 
 def _reader(root: Path) -> CheckpointReader:
@@ -267,6 +271,12 @@ def attention_type(root: Path, layer: int) -> str:
 
 
 def _device_weights(root: Path, layer: int, device) -> DeltaNetWeights | GqaWeights:
+    return _device_layer(root, layer, device)[0]
+
+
+def _device_layer(root: Path, layer: int, device) -> tuple:
+    """(weights, weight arguments of the one-call layer step) of one layer on
+    ``device``, converted once and cached until the layer is re-registered."""
     rkey = _rkey(root)
     dev = torch.device(device)
     key = (rkey, int(layer), str(dev))
@@ -280,7 +290,8 @@ def _device_weights(root: Path, layer: int, device) -> DeltaNetWeights | GqaWeig
         cls = DeltaNetWeights if kind == "linear_attention" else GqaWeights
         w = cls.from_tensors(tensors, dev)
         _DEVICE_WEIGHTS[key] = w
-    return w
+        _LAYER_ARGS[key] = _ext.deltanet_layer_args(w) if cls is DeltaNetWeights else _ext.gqa_layer_args(w)
+    return w, _LAYER_ARGS[key]
 
 
 def _projection(root: Path, prefix: str, device: str) -> torch.Tensor:
@@ -389,17 +400,32 @@ def _linear_state(state: AttentionState, layer: int, dev: torch.device) -> torch
 
 
 # --------------------------------------------------------------------------- layer steps
+# Per device and stream, the scratch the one-call layer steps keep their
+# intermediates in (grown on demand, never shared by concurrent streams).
+_SCRATCH: dict = {}
+
+
+def _scratch(dev: torch.device, nbytes: int) -> torch.Tensor:
+    key = (dev.index, torch._C._cuda_getCurrentRawStream(dev.index))
+    buf = _SCRATCH.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=dev)
+        _SCRATCH[key] = buf
+    return buf
+
+
 def _linear_stateful(root: Path, layer: int, x0: torch.Tensor, device: str) -> torch.Tensor:
     """One Gated DeltaNet layer for one token: returns the residual (1, 2048)
     fp32 (reference :224-282), state updated in place."""
     state = active(root, device)
     dev = _cuda_device(device)
-    w = _device_weights(root, layer, dev)
+    _, wargs = _device_layer(root, layer, dev)
     x = x0.reshape(1, _C.HIDDEN).to(device=dev, dtype=torch.float32).contiguous()
     conv = _conv_state(state, layer, dev)
     rec = _linear_state(state, layer, dev)
-    return deltanet_decode(x, w, rec.reshape(1, _C.LINEAR_NUM_V_HEADS, _C.LINEAR_HEAD_DIM, _C.LINEAR_HEAD_DIM),
-                           conv)
+    out = torch.empty(1, _C.HIDDEN, dtype=torch.float32, device=dev)
+    _ext.deltanet_layer_decode(x, wargs, conv, rec, out, _scratch(dev, _ext.deltanet_layer_scratch_bytes(1)))
+    return out
 
 
 def _paged_kv(state: AttentionState, layer: int, dev: torch.device) -> _PagedKV:
@@ -444,15 +470,19 @@ def _full_stateful(root: Path, layer: int, x0: torch.Tensor, device: str) -> tor
     state = active(root, device)
     dev = _cuda_device(device)
     position = int(state.tokens_seen)
-    w = _device_weights(root, layer, dev)
+    _, wargs = _device_layer(root, layer, dev)
     kv = _paged_kv(state, layer, dev)
     n = kv.length
     _check_full_kv_limits(state, n, _KV_TOKEN_BYTES)
     kv.ensure(n + 1)
-    launch: GqaLaunch = plan_gqa_split([n + 1], dev, state._workspace)
-    state._workspace = launch.workspace
+    blocks = (n + 1 + _C.KV_BLOCK - 1) // _C.KV_BLOCK  # the split plan of plan_gqa_split for one sequence
+    split_pages = _ext.gqa_split_pages(blocks, _C.FULL_NUM_KV_HEADS)
+    max_splits = (blocks + split_pages - 1) // split_pages
     x = x0.reshape(1, _C.HIDDEN).to(device=dev, dtype=torch.float32).contiguous()
-    out = gqa_decode(x, w, kv.k, kv.v, kv.table, _inv_freq(dev), launch, seq_len0=n, position0=position)
+    out = torch.empty(1, _C.HIDDEN, dtype=torch.float32, device=dev)
+    _ext.gqa_layer_decode(x, wargs, _inv_freq(dev), kv.k, kv.v, kv.table, out,
+                          _scratch(dev, _ext.gqa_layer_scratch_bytes(1, max_splits)), split_pages, max_splits,
+                          seq_len0=n, position0=position)
     kv.length = n + 1
     state.full_keys[int(layer)], state.full_values[int(layer)] = kv.views()
     return out
