@@ -20,6 +20,8 @@ by a batch dimension.  All state stays in HBM:
 
 from __future__ import annotations
 
+import weakref
+
 from dataclasses import dataclass, field
 
 import torch
@@ -73,10 +75,46 @@ def _out_projection(a: torch.Tensor, w: DeltaNetWeights | GqaWeights, x: torch.T
     return out
 
 
+# Batches up to 8 step a layer with one C call (ria_*_layer_decode: the same
+# GEMV / attention / GEMV launches issued from C), its intermediates in a
+# scratch buffer per device and stream (allocated from the capture pool when
+# first used inside a CUDA-graph capture) and the weights' pointers cached per
+# weights object: three or four Python-level calls per layer cost more host
+# time than a small-batch layer's GPU time.
+_LAYER_SCRATCH: dict = {}
+_LAYER_SCRATCH_OUTGROWN: list = []  # kept alive: a captured graph may still point at one
+_LAYER_ARGS: dict = {}
+
+
+def _layer_scratch(dev: torch.device, nbytes: int) -> torch.Tensor:
+    key = (dev.index, torch._C._cuda_getCurrentRawStream(dev.index))
+    buf = _LAYER_SCRATCH.get(key)
+    if buf is None or buf.numel() < nbytes:
+        if buf is not None:
+            _LAYER_SCRATCH_OUTGROWN.append(buf)
+        buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=dev)
+        _LAYER_SCRATCH[key] = buf
+    return buf
+
+
+def _layer_args(w: DeltaNetWeights | GqaWeights) -> tuple:
+    entry = _LAYER_ARGS.get(id(w))
+    if entry is None or entry[0]() is not w:
+        args = _ext.deltanet_layer_args(w) if isinstance(w, DeltaNetWeights) else _ext.gqa_layer_args(w)
+        entry = (weakref.ref(w), args)
+        _LAYER_ARGS[id(w)] = entry
+    return entry[1]
+
+
 def deltanet_decode(x: torch.Tensor, w: DeltaNetWeights, rec: torch.Tensor, conv: torch.Tensor,
                     slots: torch.Tensor | None = None) -> torch.Tensor:
     """One DeltaNet layer step for ``x`` [B, 2048] fp32; returns the residual."""
     batch = x.shape[0]
+    if batch <= _ext.GEMV_MAX_BATCH:
+        out = torch.empty(batch, C.HIDDEN, dtype=torch.float32, device=x.device)
+        _ext.deltanet_layer_decode(x, _layer_args(w), conv, rec, out,
+                                   _layer_scratch(x.device, _ext.deltanet_layer_scratch_bytes(batch)), slots)
+        return out
     proj = _in_projection(x, w)
     gated = torch.empty(batch, C.LINEAR_VALUE_DIM, dtype=torch.bfloat16, device=x.device)
     _ext.gdn_decode_step(
@@ -115,6 +153,12 @@ def gqa_decode(x: torch.Tensor, w: GqaWeights, k_pool: torch.Tensor, v_pool: tor
     """One GQA layer step for ``x`` [B, 2048] fp32; returns the residual.  The
     new token of sequence i is appended to the pool at index seq_lens[i]."""
     batch = x.shape[0]
+    if batch <= _ext.GEMV_MAX_BATCH:
+        out = torch.empty(batch, C.HIDDEN, dtype=torch.float32, device=x.device)
+        _ext.gqa_layer_decode(x, _layer_args(w), inv_freq, k_pool, v_pool, block_table, out,
+                              _layer_scratch(x.device, _ext.gqa_layer_scratch_bytes(batch, launch.max_splits)),
+                              launch.split_pages, launch.max_splits, seq_lens, positions, seq_len0, position0)
+        return out
     proj = _in_projection(x, w)
     attn = torch.empty(batch, C.FULL_Q_DIM, dtype=torch.bfloat16, device=x.device)
     _ext.gqa_decode_paged(

@@ -403,12 +403,15 @@ def _linear_state(state: AttentionState, layer: int, dev: torch.device) -> torch
 # Per device and stream, the scratch the one-call layer steps keep their
 # intermediates in (grown on demand, never shared by concurrent streams).
 _SCRATCH: dict = {}
+_SCRATCH_OUTGROWN: list = []  # kept alive: work already queued may still use one
 
 
 def _scratch(dev: torch.device, nbytes: int) -> torch.Tensor:
     key = (dev.index, torch._C._cuda_getCurrentRawStream(dev.index))
     buf = _SCRATCH.get(key)
     if buf is None or buf.numel() < nbytes:
+        if buf is not None:
+            _SCRATCH_OUTGROWN.append(buf)
         buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=dev)
         _SCRATCH[key] = buf
     return buf

@@ -13,7 +13,7 @@ import torch
 
 from ria_b200 import _ext, synthetic
 from ria_b200 import constants as C
-from ria_b200.engine import deltanet_decode, gqa_decode, plan_gqa_split
+from ria_b200.engine import plan_gqa_split
 from ria_b200.weights import DeltaNetWeights, GqaWeights, rope_inv_freq
 
 pytestmark = pytest.mark.gpu
@@ -21,6 +21,35 @@ pytestmark = pytest.mark.gpu
 
 def _scratch(dev, nbytes):
     return torch.empty(nbytes, dtype=torch.uint8, device=dev)
+
+
+def _dn_separate(x, w, rec, conv):
+    """The DeltaNet layer step as three separate entry-point calls."""
+    B = x.shape[0]
+    proj = torch.empty(B, C.DN_PROJ_WIDTH, dtype=torch.bfloat16, device=x.device)
+    _ext.rmsnorm_gemv(x, w.in_norm, w.w_in, proj)
+    gated = torch.empty(B, C.LINEAR_VALUE_DIM, dtype=torch.bfloat16, device=x.device)
+    _ext.gdn_decode_step(proj[:, C.DN_PROJ_QKV[0]:C.DN_PROJ_QKV[1]], proj[:, C.DN_PROJ_Z[0]:C.DN_PROJ_Z[1]],
+                         proj[:, C.DN_PROJ_B[0]:C.DN_PROJ_B[1]], proj[:, C.DN_PROJ_A[0]:C.DN_PROJ_A[1]], w.conv_w,
+                         w.a_log, w.dt_bias, w.norm_w, conv, rec, None, gated)
+    out = torch.empty(B, C.HIDDEN, device=x.device)
+    _ext.gemv_residual(gated, w.w_out, x, out)
+    return out
+
+
+def _gqa_separate(x, w, k_pool, v_pool, table, inv, launch, **lens):
+    """The GQA layer step as three separate entry-point calls."""
+    B = x.shape[0]
+    proj = torch.empty(B, C.GQA_PROJ_WIDTH, dtype=torch.bfloat16, device=x.device)
+    _ext.rmsnorm_gemv(x, w.in_norm, w.w_in, proj)
+    attn = torch.empty(B, C.FULL_Q_DIM, dtype=torch.bfloat16, device=x.device)
+    _ext.gqa_decode_paged(proj[:, C.GQA_PROJ_Q[0]:C.GQA_PROJ_Q[1]], proj[:, C.GQA_PROJ_K[0]:C.GQA_PROJ_K[1]],
+                          proj[:, C.GQA_PROJ_V[0]:C.GQA_PROJ_V[1]], w.q_norm, w.k_norm, inv, k_pool, v_pool, table,
+                          lens.get("seq_lens"), lens.get("positions"), attn, launch.workspace, launch.split_pages,
+                          launch.max_splits, seq_len0=lens.get("seq_len0", 0), position0=lens.get("position0", 0))
+    out = torch.empty(B, C.HIDDEN, device=x.device)
+    _ext.gemv_residual(attn, w.w_out, x, out)
+    return out
 
 
 @pytest.mark.parametrize("batch", [1, 3])
@@ -35,7 +64,7 @@ def test_deltanet_layer_step_equals_separate_calls(cuda_device, batch):
     scratch = _scratch(dev, _ext.deltanet_layer_scratch_bytes(batch))
     for step in range(3):
         x = torch.randn(batch, C.HIDDEN, device=dev, generator=g)
-        ref = deltanet_decode(x, w, rec_a, conv_a)
+        ref = _dn_separate(x, w, rec_a, conv_a)
         out = torch.empty(batch, C.HIDDEN, device=dev)
         _ext.deltanet_layer_decode(x, args, conv_b, rec_b, out, scratch)
         torch.cuda.synchronize(dev)
@@ -65,13 +94,13 @@ def test_gqa_layer_step_equals_separate_calls(cuda_device, lengths):
         out = torch.empty(B, C.HIDDEN, device=dev)
         scratch = _scratch(dev, _ext.gqa_layer_scratch_bytes(B, launch.max_splits))
         if B == 1:  # scalar length and position, as the drop-in module calls it
-            ref = gqa_decode(x, w, k_a, v_a, table, inv, launch, seq_len0=cur[0], position0=cur[0] + 11)
+            ref = _gqa_separate(x, w, k_a, v_a, table, inv, launch, seq_len0=cur[0], position0=cur[0] + 11)
             _ext.gqa_layer_decode(x, args, inv, k_b, v_b, table, out, scratch, launch.split_pages, launch.max_splits,
                                   seq_len0=cur[0], position0=cur[0] + 11)
         else:
             seq_lens = torch.tensor(cur, dtype=torch.int32, device=dev)
             positions = seq_lens + 11
-            ref = gqa_decode(x, w, k_a, v_a, table, inv, launch, seq_lens, positions)
+            ref = _gqa_separate(x, w, k_a, v_a, table, inv, launch, seq_lens=seq_lens, positions=positions)
             _ext.gqa_layer_decode(x, args, inv, k_b, v_b, table, out, scratch, launch.split_pages, launch.max_splits,
                                   seq_lens=seq_lens, positions=positions)
         torch.cuda.synchronize(dev)
