@@ -242,7 +242,10 @@ extern "C" int ria_conv1d_prefill(const void* x, int64_t x_stride_b, int64_t x_s
   const int64_t threads = static_cast<int64_t>(channels / 2) * groups;
   const int vgroups = (seq_len + kVecTok - 1) / kVecTok;
   const int64_t vthreads = static_cast<int64_t>(channels / kVecCh) * vgroups;
-  if (vec_ok && (vthreads + 255) / 256 <= INT32_MAX) {
+  // the vector form once it fills the GPU (two 256-thread CTAs per SM or more);
+  // short prompts keep the pairs form's eight-token threads and four times the CTAs
+  if (vec_ok && static_cast<int64_t>(vthreads) * batch >= 2LL * 256 * ria::num_sms() &&
+      (vthreads + 255) / 256 <= INT32_MAX) {
     conv1d_prefill_vec_kernel<<<dim3(static_cast<unsigned>((vthreads + 255) / 256), batch), 256, 0, st>>>(
         xb, x_stride_b, x_stride_t, sb, static_cast<const __nv_bfloat16*>(weight), static_cast<__nv_bfloat16*>(out),
         out_stride_b, out_stride_t, seq_len, channels / kVecCh, vgroups);
