@@ -42,6 +42,44 @@ def test_conv1d_prefill_equals_steps(cuda_device, T, offset):
         assert torch.equal(st[b], state[0]), b
 
 
+def test_conv1d_prefill_vector_form_equals_pair_form(cuda_device):
+    """At sizes that fill the GPU, 16-byte aligned rows take the vector form
+    (eight channels x sixteen tokens per thread); the same values in rows
+    that are only 4-byte aligned take the pair form.  Same per-channel
+    arithmetic and order: bit-identical outputs and states; sequence 0 is
+    also checked against the oracle's steps."""
+    dev = cuda_device
+    B, T, Cc = 4, 1024, 8192
+    g = torch.Generator(device=dev).manual_seed(99)
+    vals = torch.randn(B, T, Cc, device=dev, generator=g).to(torch.bfloat16)
+    wide_v = torch.zeros(B, T, Cc + 64, dtype=torch.bfloat16, device=dev)
+    wide_p = torch.zeros_like(wide_v)
+    wide_v[:, :, 16:16 + Cc] = vals  # 32-byte offset: the vector form
+    wide_p[:, :, 18:18 + Cc] = vals  # 36-byte offset: the pair form
+    state0 = (torch.randn(B, Cc, 4, device=dev, generator=g) * 0.5).to(torch.bfloat16)
+    weight = (torch.rand(Cc, 4, device=dev, generator=g) - 0.5).to(torch.bfloat16)
+    outs, states = [], []
+    for wide, off in ((wide_v, 16), (wide_p, 18)):
+        st = state0.clone()
+        out = torch.empty(B, T, Cc, dtype=torch.bfloat16, device=dev)
+        _ext.conv1d_prefill(wide[:, :, off:off + Cc], st, weight, out)
+        outs.append(out)
+        states.append(st)
+    torch.cuda.synchronize(dev)
+    assert torch.equal(outs[0], outs[1]) and torch.equal(states[0], states[1])
+    assert _ext.device_error() == 0
+    x0 = vals[0].cpu()
+    w3 = weight.cpu().reshape(Cc, 1, 4)
+    got = outs[0][0].float().cpu()
+    state = state0[0:1].cpu()  # every 37th token against the oracle's steps
+    for t in range(T):
+        ref, state = O.conv1d_step(state, x0[t:t + 1], w3)
+        if t % 37 == 0 or t == T - 1:
+            err = ((got[t] - ref[0].float()).abs() / ref[0].float().abs().clamp_min(1e-2)).max().item()
+            assert err <= 2 ** -7, (t, err)
+    assert torch.equal(states[0][0].cpu(), state[0])
+
+
 def test_gdn_gates(cuda_device):
     rows, heads = 300, 32
     g = torch.Generator().manual_seed(3)
