@@ -385,8 +385,6 @@ def config1_latency(device, iters=50):
     x = torch.randn(1, 2048, device=device)
     for _ in range(10):
         gqa_decode(x, w, k, v, table, inv, launch, seq_len0=L, position0=L)
-    hook = EventHook(timed=("gqa_decode",))
-    _ext.launch_hook = hook
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize(device)
     s.record()
@@ -394,9 +392,28 @@ def config1_latency(device, iters=50):
         gqa_decode(x, w, k, v, table, inv, launch, seq_len0=L, position0=L)
     e.record()
     torch.cuda.synchronize(device)
+    step_ms = s.elapsed_time(e) / iters
+    # the attention kernel (K3 and its split combine) on its own, from a fixed
+    # projection row (at batch 1 the layer step issues it inside one C call)
+    from ria_b200 import constants as C
+
+    proj = torch.randn(1, C.GQA_PROJ_WIDTH, device=device).to(torch.bfloat16)
+    attn = torch.empty(1, C.FULL_Q_DIM, dtype=torch.bfloat16, device=device)
+    qkv = [proj[:, a:b] for a, b in (C.GQA_PROJ_Q, C.GQA_PROJ_K, C.GQA_PROJ_V)]
+
+    def attention():
+        _ext.gqa_decode_paged(*qkv, w.q_norm, w.k_norm, inv, k, v, table, None, None, attn, launch.workspace,
+                              launch.split_pages, launch.max_splits, seq_len0=L, position0=L)
+
+    for _ in range(10):
+        attention()
+    hook = EventHook(timed=("gqa_decode",))
+    _ext.launch_hook = hook
+    for _ in range(iters):
+        attention()
+    torch.cuda.synchronize(device)
     _ext.launch_hook = None
     kms, _ = hook.mean_ms("gqa_decode")
-    step_ms = s.elapsed_time(e) / iters
     # the same layer step replayed from a CUDA graph (no per-launch host work)
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, capture_error_mode="thread_local"):
