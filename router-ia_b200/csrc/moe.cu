@@ -16,7 +16,7 @@
 // streams: every weight byte is loaded once, straight from HBM into MMA
 // fragments, and applied to all of that expert's tokens at once.  Three
 // launches:
-//   * moe_route_kernel, a CTA per (16 router rows, 8 tokens): the norm of its
+//   * moe_route_kernel, a CTA per (8 or 16 router rows, 8 tokens): the norm of its
 //     tokens, then router and shared-gate logits (fp32 sums over the bf16
 //     rows).  The last CTA to finish a token group takes the group's top-k
 //     (a warp per token: rounds of a warp-wide max, ties to the lower expert
@@ -64,7 +64,6 @@ constexpr int kMaxPairs = 2048;   // batch * top_k per launch
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 constexpr int kTokens = 8;        // tokens per unit and per route CTA
-constexpr int kLogitRows = 16;    // router rows per route CTA (2 per warp)
 constexpr int kLogitSmem = kTokens * kH * 4;
 constexpr int kGuTiles = kI / 16;  // 16-row gate/up tiles per unit
 constexpr int kDnRows = 16 * kWarps;  // down rows per tile: 16 per warp
@@ -226,8 +225,12 @@ __device__ void build_plan(const MoeParams& p) {
   if (tid == 0) *p.n_units = routed_units + shared_units;
 }
 
-template <int kPer>
+// kRowsPerWarp router rows per warp, 8 kRowsPerWarp per CTA: one row for a
+// single token group (a shorter logits chain per warp, twice the CTAs), two
+// for more groups (each CTA also recomputes its group's norms).
+template <int kPer, int kRowsPerWarp>
 __global__ void __launch_bounds__(kThreads) moe_route_kernel(const MoeParams p) {
+  constexpr int kLogitRows = kRowsPerWarp * kWarps;
   extern __shared__ __align__(16) unsigned char smem[];
   float* xs = reinterpret_cast<float*>(smem);  // [kTokens][kH]
   __shared__ int flag;
@@ -235,7 +238,7 @@ __global__ void __launch_bounds__(kThreads) moe_route_kernel(const MoeParams p) 
   const int t0 = blockIdx.y * kTokens;
   const int nt = min(kTokens, p.B - t0);
   // warp w < nt: the norm of token t0 + w.  Its row and the norm weight are
-  // loaded first, then this warp's 2 router rows (row E is the shared gate),
+  // loaded first, then this warp's router row (row E is the shared gate),
   // which stay in flight while the norm runs.
   float4 v[kH / 128];
   float2 wa[kH / 128], wb[kH / 128];
@@ -249,10 +252,10 @@ __global__ void __launch_bounds__(kThreads) moe_route_kernel(const MoeParams p) 
       wb[i] = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p.post_w + d + 2));
     }
   }
-  const int rbase = blockIdx.x * kLogitRows + warp * 2;
-  uint4 w[2][kH / 256];
+  const int rbase = blockIdx.x * kLogitRows + warp * kRowsPerWarp;
+  uint4 w[kRowsPerWarp][kH / 256];
 #pragma unroll
-  for (int q = 0; q < 2; ++q) {
+  for (int q = 0; q < kRowsPerWarp; ++q) {
     const int r = min(rbase + q, p.E);
     const __nv_bfloat16* wr = r < p.E ? p.router_w + static_cast<int64_t>(r) * kH : p.shared_gate_w;
 #pragma unroll
@@ -276,16 +279,16 @@ __global__ void __launch_bounds__(kThreads) moe_route_kernel(const MoeParams p) 
     }
   }
   __syncthreads();
-  float acc[2][kTokens];
+  float acc[kRowsPerWarp][kTokens];
 #pragma unroll
-  for (int q = 0; q < 2; ++q)
+  for (int q = 0; q < kRowsPerWarp; ++q)
 #pragma unroll
     for (int t = 0; t < kTokens; ++t) acc[q][t] = 0.f;
 #pragma unroll
   for (int c = 0; c < kH / 256; ++c) {
-    float wf[2][8];
+    float wf[kRowsPerWarp][8];
 #pragma unroll
-    for (int q = 0; q < 2; ++q) bf16x8(w[q][c], wf[q]);
+    for (int q = 0; q < kRowsPerWarp; ++q) bf16x8(w[q][c], wf[q]);
 #pragma unroll
     for (int t = 0; t < kTokens; ++t) {
       if (t < nt) {
@@ -293,14 +296,14 @@ __global__ void __launch_bounds__(kThreads) moe_route_kernel(const MoeParams p) 
         const float4 xb = *reinterpret_cast<const float4*>(xs + t * kH + c * 256 + lane * 8 + 4);
         const float xf[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
 #pragma unroll
-        for (int q = 0; q < 2; ++q)
+        for (int q = 0; q < kRowsPerWarp; ++q)
 #pragma unroll
           for (int j = 0; j < 8; ++j) acc[q][t] = fmaf(wf[q][j], xf[j], acc[q][t]);
       }
     }
   }
 #pragma unroll
-  for (int q = 0; q < 2; ++q)
+  for (int q = 0; q < kRowsPerWarp; ++q)
 #pragma unroll
     for (int t = 0; t < kTokens; ++t) {
       if (t < nt) {
@@ -718,9 +721,14 @@ extern "C" int ria_moe_decode(const float* residual, int64_t residual_stride, co
   std::lock_guard<std::mutex> attr_lock(attr_mu);
   if (dev < 0 || dev >= 64 || !attr_set[dev]) {
     const int max_ids = kMaxPairs * 4;
-    cudaError_t e = cudaFuncSetAttribute(moe_route_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, kLogitSmem);
+    cudaError_t e = cudaFuncSetAttribute(moe_route_kernel<8, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kLogitSmem);
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(moe_route_kernel<kMaxExperts / 32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      e = cudaFuncSetAttribute(moe_route_kernel<8, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kLogitSmem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(moe_route_kernel<kMaxExperts / 32, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               kLogitSmem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(moe_route_kernel<kMaxExperts / 32, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                kLogitSmem);
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(moe_gate_up_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -763,11 +771,20 @@ extern "C" int ria_moe_decode(const float* residual, int64_t residual_stride, co
   p.E = num_experts;
   p.k = top_k;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const dim3 route_grid((num_experts + 1 + kLogitRows - 1) / kLogitRows, (batch + kTokens - 1) / kTokens);
-  if (num_experts <= 256)
-    moe_route_kernel<8><<<route_grid, kThreads, kLogitSmem, st>>>(p);
-  else
-    moe_route_kernel<kMaxExperts / 32><<<route_grid, kThreads, kLogitSmem, st>>>(p);
+  const int rows_per_warp = batch <= kTokens ? 1 : 2;
+  const dim3 route_grid((num_experts + kWarps * rows_per_warp) / (kWarps * rows_per_warp),
+                        (batch + kTokens - 1) / kTokens);
+  if (num_experts <= 256) {
+    if (rows_per_warp == 1)
+      moe_route_kernel<8, 1><<<route_grid, kThreads, kLogitSmem, st>>>(p);
+    else
+      moe_route_kernel<8, 2><<<route_grid, kThreads, kLogitSmem, st>>>(p);
+  } else {
+    if (rows_per_warp == 1)
+      moe_route_kernel<kMaxExperts / 32, 1><<<route_grid, kThreads, kLogitSmem, st>>>(p);
+    else
+      moe_route_kernel<kMaxExperts / 32, 2><<<route_grid, kThreads, kLogitSmem, st>>>(p);
+  }
   int rc = ria::check_launch("ria_moe_decode (route and plan)");
   if (rc) return rc;
   const int64_t units = max_units(batch, num_experts, top_k);
