@@ -51,7 +51,8 @@ RIA_API int ria_abi_version(void);
  * otherwise the first code set: 1, 2 or 5 a bounded wait gave up (DeltaNet
  * decode, GQA decode, prefill kernels), 3 a block id outside the pool, 6 a
  * state slot outside the pool, 7 a too-small GQA split plan (that sequence was
- * left untouched: no pool, workspace or output write). */
+ * left untouched: no pool, workspace or output write), 8 the MoE block's down
+ * phase gave up waiting for a unit's gate/up tiles. */
 RIA_API int ria_device_error(int clear, unsigned int* code_out);
 
 /* ------------------------------------------------------------------------

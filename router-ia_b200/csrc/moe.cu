@@ -14,7 +14,7 @@
 // experts that some token chose (6 MB of bf16 weights per expert: 54 MB for
 // one token, about 1.3 GB for 64 tokens), so the expert kernels are weight
 // streams: every weight byte is loaded once, straight from HBM into MMA
-// fragments, and applied to all of that expert's tokens at once.  Three
+// fragments, and applied to all of that expert's tokens at once.  Two
 // launches:
 //   * moe_route_kernel, a CTA per (8 or 16 router rows, 8 tokens): the norm of its
 //     tokens, then router and shared-gate logits (fp32 sums over the bf16
@@ -25,17 +25,21 @@
 //     expert some token chose, units of up to 8 of its (token, slot) pairs in
 //     token order, then the shared expert's units of 8 tokens.  Experts
 //     nobody chose get no unit; their weights are never read.
-//   * moe_gate_up_kernel, persistent, over 16-row tiles: finds a unit's pairs
-//     in the routing table, stages their activations in SMEM as bf16 hi + lo
-//     parts; warps stream gate / up rows through mma.sync m16n8k16 (weight
-//     rows = M, activations = N, fp32 accumulation) with the next stage's
-//     loads in flight, and write h = silu(gate) * up per (token, slot).
-//   * moe_down_kernel, the same over 128-row tiles of the down rows (a warp
-//     per 16 rows, all 512 columns): y[token][slot] = scale * down . h,
-//     scale = the slot's router weight (the shared gate for the shared
-//     slot).  The CTA that finishes the last of a (token, tile)'s k + 1
-//     slots writes that piece of the output: x + (routed slots summed in slot
-//     order + shared slot).
+//   * moe_experts_kernel, persistent and cooperative (every CTA resident),
+//     two phases per CTA:
+//     - gate/up over 16-row tiles: finds a unit's pairs in the routing
+//       table, stages their activations in SMEM as bf16 hi + lo parts; warps
+//       stream gate / up rows through mma.sync m16n8k16 (weight rows = M,
+//       activations = N, fp32 accumulation) with the next stage's loads in
+//       flight, write h = silu(gate) * up per (token, slot) and publish the
+//       unit's finished tiles on a per-unit counter;
+//     - down over 128-row tiles of the down rows (a warp per 16 rows, all
+//       512 columns), each segment starting once its unit's gate/up tiles
+//       are all published (a bounded wait): y[token][slot] = scale * down .
+//       h, scale = the slot's router weight (the shared gate for the shared
+//       slot).  The CTA that finishes the last of a (token, tile)'s k + 1
+//       slots writes that piece of the output: x + (routed slots summed in
+//       slot order + shared slot).
 // "Last CTA" hand-offs use a fence and an atomic counter (no waiting); the
 // last arrival resets the counter, so the workspace counters stay zero
 // between calls.  Every sum runs in a fixed order: results are deterministic
@@ -98,6 +102,8 @@ struct MoeParams {
   unsigned* cnt_group;  // [kMaxGroups] route CTAs done per token group
   unsigned* cnt_plan;   // token groups done
   unsigned* cnt_out;    // [B][kDnTiles] slots done per (token, down row tile)
+  unsigned* unit_done;  // [units] gate/up tiles finished per unit (zeroed by the plan)
+  unsigned int* err;    // device error word
   int B, E, k;
 };
 
@@ -222,6 +228,7 @@ __device__ void build_plan(const MoeParams& p) {
   const int shared_units = (p.B + kTokens - 1) / kTokens;
   for (int q = tid; q < shared_units; q += kThreads)
     p.units[routed_units + q] = make_int4(p.E, q * kTokens, min(kTokens, p.B - q * kTokens), 0);
+  for (int q = tid; q < routed_units + shared_units; q += kThreads) p.unit_done[q] = 0u;
   if (tid == 0) *p.n_units = routed_units + shared_units;
 }
 
@@ -334,7 +341,7 @@ __device__ __forceinline__ int64_t pair_row(const MoeParams& p, int pr) {
 __device__ __forceinline__ void stage_split(const float* __restrict__ src, int len, __nv_bfloat16* xh,
                                             __nv_bfloat16* xl) {
   for (int c4 = threadIdx.x * 4; c4 < len; c4 += kThreads * 4) {
-    const float4 v = *reinterpret_cast<const float4*>(src + c4);
+    const float4 v = __ldcg(reinterpret_cast<const float4*>(src + c4));
     const __nv_bfloat162 h01 = __floats2bfloat162_rn(v.x, v.y), h23 = __floats2bfloat162_rn(v.z, v.w);
     const float2 f01 = __bfloat1622float2(h01), f23 = __bfloat1622float2(h23);
     const __nv_bfloat162 l01 = __floats2bfloat162_rn(v.x - f01.x, v.y - f01.y);
@@ -468,8 +475,7 @@ __device__ __forceinline__ Segment segment_at(int64_t tt, int64_t t_end, int til
 // up rows, each over a quarter of the 2048 columns; at each tile's end the
 // quarters are summed in a fixed order and h = silu(gate) * up is written per
 // (token, slot) for the down kernel.
-__global__ void __launch_bounds__(kThreads, 2) moe_gate_up_kernel(const MoeParams p) {
-  extern __shared__ __align__(16) unsigned char smem[];
+__device__ __forceinline__ void gate_up_phase(const MoeParams& p, unsigned char* smem) {
   __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem);  // rows 0-7 hi, 8-15 lo
   float* red = reinterpret_cast<float*>(xs + 2 * kTokens * kXStride);  // [2][8 warps][16][8]
   int* ids_s = reinterpret_cast<int*>(red + 2 * kWarps * 16 * kTokens);  // [B * k]
@@ -530,7 +536,29 @@ __global__ void __launch_bounds__(kThreads, 2) moe_gate_up_kernel(const MoeParam
     else
       stream_stages<false>(nst, kH, xs + g * kXStride + 8 * t, xs + (kTokens + g) * kXStride + 8 * t, addr, xcol,
                            done, ra, rb);
+    // publish the segment's h rows: the down phase of any CTA waits for all
+    // kGuTiles tiles of a unit before reading its h
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) atomicAdd(p.unit_done + sg.unit, static_cast<unsigned>(sg.tb - sg.ta));
   }
+}
+
+// Bounded wait (one thread) until all kGuTiles gate/up tiles of unit u are
+// published.  Every CTA of the cooperative launch is resident and the
+// gate/up phase never waits, so the count always completes; one that does
+// not sets device error 8 after about a second, and the kernel finishes on
+// whatever h holds instead of hanging.
+__device__ __forceinline__ void wait_unit(const MoeParams& p, int u) {
+  const volatile unsigned* c = p.unit_done + u;
+  for (uint32_t i = 0; *c < static_cast<unsigned>(kGuTiles); ++i) {
+    if (i >= (1u << 22)) {
+      ria_set_error(p.err, RIA_DEVERR_MOE_WAIT);
+      break;
+    }
+    __nanosleep(256);
+  }
+  __threadfence();
 }
 
 // down: tiles of 128 rows; warp w streams rows 16 w .. 16 w + 15 of each tile
@@ -539,8 +567,7 @@ __global__ void __launch_bounds__(kThreads, 2) moe_gate_up_kernel(const MoeParam
 // tile) counts its k + 1 slots; the CTA that brings the count to k + 1
 // writes that token's tile of the output: x + (routed slots in slot order +
 // shared slot).
-__global__ void __launch_bounds__(kThreads, 2) moe_down_kernel(const MoeParams p) {
-  extern __shared__ __align__(16) unsigned char smem[];
+__device__ __forceinline__ void down_phase(const MoeParams& p, unsigned char* smem) {
   __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem);  // rows 0-7 hi, 8-15 lo
   int* ids_s = reinterpret_cast<int*>(xs + 2 * kTokens * kHStride);  // [B * k]
   __shared__ int pr_s[kTokens];
@@ -567,6 +594,7 @@ __global__ void __launch_bounds__(kThreads, 2) moe_down_kernel(const MoeParams p
     __syncthreads();  // the previous segment is done with pr_s, sc_s, xs and fin_s; ids_s is complete
     if (tid == 0) n_fin = 0;
     unit_pairs(p, e, start, ntok, ids_s, pr_s);
+    if (tid == 0) wait_unit(p, sg.unit);  // the unit's h rows, from the gate/up phase of any CTA
     __syncthreads();
     if (tid < ntok) {
       const int tok = pr_s[tid] / kMaxTopK, slot = pr_s[tid] % kMaxTopK;
@@ -641,6 +669,19 @@ __global__ void __launch_bounds__(kThreads, 2) moe_down_kernel(const MoeParams p
   }
 }
 
+// The expert FFNs as one persistent launch (cooperative: every CTA is
+// resident): each CTA streams its gate/up range, then its down range.  A
+// down segment starts as soon as its unit's gate/up tiles are published, so
+// the CTAs that finish gate/up early move on instead of waiting for the
+// slowest one and a second launch.  The per-tile arithmetic and every sum
+// order are those of two separate launches: results are unchanged.
+__global__ void __launch_bounds__(kThreads, 2) moe_experts_kernel(const MoeParams p) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  gate_up_phase(p, smem);
+  __syncthreads();  // the gate/up phase is done with the shared memory
+  down_phase(p, smem);
+}
+
 int64_t round_up(int64_t v) { return (v + 255) / 256 * 256; }
 
 int64_t max_units(int64_t b, int64_t e, int64_t k) {
@@ -648,7 +689,7 @@ int64_t max_units(int64_t b, int64_t e, int64_t k) {
 }
 
 struct Layout {
-  int64_t counters, xin, logits, hbuf, ybuf, units, total;
+  int64_t counters, xin, logits, hbuf, ybuf, units, unit_done, total;
 };
 
 // The counters come first (a workspace zeroed once stays valid: every call
@@ -669,6 +710,8 @@ Layout layout(int64_t b, int64_t e, int64_t k) {
   off += round_up(b * (k + 1) * kH * 4);
   l.units = off;
   off += round_up(max_units(b, e, k) * 16);
+  l.unit_done = off;
+  off += round_up(max_units(b, e, k) * 4);
   l.total = off;
   return l;
 }
@@ -714,8 +757,10 @@ extern "C" int ria_moe_decode(const float* residual, int64_t residual_stride, co
   const int ids_bytes = batch * top_k * 4;
   const int gu_smem = 2 * kTokens * kXStride * 2 + 2 * kWarps * 16 * kTokens * 4 + ids_bytes;
   const int dn_smem = 2 * kTokens * kHStride * 2 + ids_bytes;
+  const int ex_smem = std::max(gu_smem, dn_smem);
   static std::mutex attr_mu;  // the SMEM opt-ins are per-device function attributes
   static bool attr_set[64] = {false};
+  static int resident_per_sm[64] = {0};  // experts-kernel CTAs resident per SM at the largest SMEM size
   int dev = -1;
   cudaGetDevice(&dev);
   std::lock_guard<std::mutex> attr_lock(attr_mu);
@@ -730,16 +775,21 @@ extern "C" int ria_moe_decode(const float* residual, int64_t residual_stride, co
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(moe_route_kernel<kMaxExperts / 32, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                kLogitSmem);
+    const int ex_max = std::max(2 * kTokens * kXStride * 2 + 2 * kWarps * 16 * kTokens * 4, 2 * kTokens * kHStride * 2) +
+                       max_ids;
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(moe_gate_up_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               2 * kTokens * kXStride * 2 + 2 * kWarps * 16 * kTokens * 4 + max_ids);
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(moe_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               2 * kTokens * kHStride * 2 + max_ids);
+      e = cudaFuncSetAttribute(moe_experts_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ex_max);
+    int per_sm = 0;
+    if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, moe_experts_kernel, kThreads, ex_max);
     if (e != cudaSuccess)
-      return ria::fail(RIA_ERR_CUDA, "ria_moe_decode: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+      return ria::fail(RIA_ERR_CUDA, "ria_moe_decode: kernel attributes: %s", cudaGetErrorString(e));
+    if (per_sm < 1) return ria::fail(RIA_ERR_CUDA, "ria_moe_decode: the experts kernel does not fit an SM");
+    if (dev >= 0 && dev < 64) {
+      resident_per_sm[dev] = std::min(per_sm, 2);
+      attr_set[dev] = true;
+    }
   }
+  const int per_sm = (dev >= 0 && dev < 64) ? resident_per_sm[dev] : 1;
   MoeParams p;
   p.residual = residual;
   p.rs = residual_stride;
@@ -767,6 +817,8 @@ extern "C" int ria_moe_decode(const float* residual, int64_t residual_stride, co
   p.hbuf = reinterpret_cast<float*>(ws + l.hbuf);
   p.ybuf = reinterpret_cast<float*>(ws + l.ybuf);
   p.units = reinterpret_cast<int4*>(ws + l.units);
+  p.unit_done = reinterpret_cast<unsigned*>(ws + l.unit_done);
+  p.err = ria::device_error_word();
   p.B = batch;
   p.E = num_experts;
   p.k = top_k;
@@ -788,11 +840,20 @@ extern "C" int ria_moe_decode(const float* residual, int64_t residual_stride, co
   int rc = ria::check_launch("ria_moe_decode (route and plan)");
   if (rc) return rc;
   const int64_t units = max_units(batch, num_experts, top_k);
-  // persistent grids: two CTAs per SM, or fewer when there are fewer tiles
-  const int resident = 2 * ria::num_sms();
-  moe_gate_up_kernel<<<static_cast<unsigned>(std::min<int64_t>(resident, units * kGuTiles)), kThreads, gu_smem, st>>>(p);
-  rc = ria::check_launch("ria_moe_decode (gate/up)");
-  if (rc) return rc;
-  moe_down_kernel<<<static_cast<unsigned>(std::min<int64_t>(resident, units * kDnTiles)), kThreads, dn_smem, st>>>(p);
-  return ria::check_launch("ria_moe_decode (down and combine)");
+  // one persistent cooperative grid: two CTAs per SM (all resident), or
+  // fewer when there are fewer gate/up tiles
+  const int resident = per_sm * ria::num_sms();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(std::min<int64_t>(resident, units * kGuTiles)));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = static_cast<size_t>(ex_smem);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, moe_experts_kernel, p);
+  if (e != cudaSuccess) return ria::fail(RIA_ERR_CUDA, "ria_moe_decode (experts): %s", cudaGetErrorString(e));
+  return ria::check_launch("ria_moe_decode (experts)");
 }

@@ -29,6 +29,7 @@ enum RiaDeviceError : unsigned int {
   RIA_DEVERR_MBAR_TIMEOUT_PREFILL = 5,
   RIA_DEVERR_BAD_SLOT = 6,
   RIA_DEVERR_SPLIT_PLAN = 7,  // a sequence needs more KV splits than were launched
+  RIA_DEVERR_MOE_WAIT = 8,    // the MoE down phase gave up waiting for a unit's gate/up tiles
 };
 
 __device__ __forceinline__ void ria_set_error(unsigned int* err, unsigned int code) {

@@ -462,7 +462,7 @@ def moe_decode(residual, w, out, expert_ids, expert_weights, shared_gate, worksp
     receive the routing; workspace a uint8 device buffer."""
     _require_cuda(residual, out, expert_ids, expert_weights, shared_gate, workspace)
     num_experts = w["router"].shape[0]
-    with _Hooked("moe", kernels=3):
+    with _Hooked("moe", kernels=2):
         rc = lib().ria_moe_decode(
             residual.data_ptr(), residual.stride(0), w["post_norm"].data_ptr(), w["router"].data_ptr(),
             w["shared_gate"].data_ptr(), w["experts_gate"].data_ptr(), w["experts_up"].data_ptr(),
